@@ -1,0 +1,351 @@
+"""Benchmark of the fused sampling step (sampled rows/s; % of the HBM roofline; CPU baseline beside it).
+
+Workload (default ``thinker``): Thinker text sampling on a Qwen3-8B-sized head, the configuration the
+north-star target is quoted on (B >= 64, V = 151,936 on one B200): per GPU B = 64 rows of bf16 logits
+(Zipf(1.1) rank profile + N(0,1), permuted per row), temperature 0.7, top-k 20, top-p 0.8, count-based
+repetition penalty 1.05 over a 512-token history, omni order, Philox4x32-10 uniforms keyed by
+(seed = row, step).  One step = one launch of the fused kernel over the batch: penalties, temperature,
+top-k, top-p, draw, and the in-place history / step update.  Synthetic data, generated on the host.
+
+``--gpus N`` (under torchrun): every rank runs its own B rows (row sharding, no collective on the data
+path; ``scaling`` = weak); timing is the max over ranks.  ``--impl reference`` times the CPU oracle (the
+reference algorithm restated in C, all host threads) on the same workload instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    # name: rows per GPU, vocab, dtype, window, temperature, top_k, top_p, penalty
+    "thinker": dict(rows=64, vocab=151_936, dtype="bf16", window=512, temperature=0.7, top_k=20, top_p=0.8,
+                    penalty=1.05),
+    "large": dict(rows=1024, vocab=151_936, dtype="f32", window=2048, temperature=1.0, top_k=50, top_p=0.95,
+                  penalty=1.1),
+    "talker": dict(rows=8, vocab=6562, dtype="bf16", window=64, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05),
+}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def bytes_per_row(w) -> int:
+    """Algorithmic bytes of one sampled row: logits read once, history ids as int32, 40 B params/state/token."""
+    e = 2 if w["dtype"] == "bf16" else 4
+    return w["vocab"] * e + 4 * w["window"] + 40
+
+
+def make_inputs(w, rows: int, seed: int):
+    """Host arrays of one batch: logits (fp32 values, bf16-rounded for bf16), history, seeds."""
+    from tests.golden import inputs as I
+
+    g = I.rng(seed)
+    if w["vocab"] == 151_936 and w["dtype"] == "bf16":
+        logits, hist = I.zipf_rows(g, rows, w["vocab"], w["window"])
+    else:
+        logits = (g.standard_normal((rows, w["vocab"])) * 3.0).astype(np.float32)
+        hist = g.integers(0, w["vocab"], size=(rows, w["window"]))
+    if w["dtype"] == "bf16":
+        logits = I.bf16_bits_to_f32(I.to_bf16_bits(logits))
+    return logits, hist.astype(np.int64)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "50"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peak_gbs():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(workload: str):
+    """DRAM bytes per launch of the sampling kernel from the committed ncu summary, or None."""
+    f = ROOT / "profiles" / f"sample_kernel_{workload}.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
+    """The CPU oracle (reference algorithm in C, OpenMP over rows) on rows of the same workload."""
+    from oracle import oracle as orc
+    from tests.golden import inputs as I
+
+    threads = threads or len(os.sched_getaffinity(0))
+    rows = min(w["rows"], 64)
+    logits, hist = make_inputs(w, rows, 1234)
+    x = I.to_bf16_bits(logits) if w["dtype"] == "bf16" else logits
+    cfg = orc.Cfg(temperature=w["temperature"], top_p=w["top_p"], top_k=w["top_k"], repetition_penalty=w["penalty"],
+                  window=w["window"], min_new_tokens=0, max_new_tokens=1 << 40, min_keep=1, semantics="omni")
+    seeds = np.arange(rows, dtype=np.int64)
+    done = 0
+    t0 = time.perf_counter()
+    step = 0
+    while True:
+        orc.sample(x, hist, np.full(rows, step, np.int64), seeds, -1, cfg, rng=orc.RNG_PHILOX,
+                   requests=np.zeros(rows, np.int64), want_processed=False, threads=threads)
+        done += rows
+        step += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": done / el, "unit": "rows/s", "cores": threads, "kind": "port",
+            "sample": f"{step} steps x {rows} rows of the {w['vocab']}-vocab workload in {el:.1f} s "
+                      f"(oracle/sampler_oracle.c, OpenMP)"}
+
+
+def run_reference(args, w, rank: int):
+    if rank != 0:
+        return
+    cb = cpu_baseline(w, seconds=args.cpu_seconds)
+    line = {"impl": "reference", "metric": f"sampled rows/s at B={w['rows']} x V={w['vocab']}", "value": cb["value"],
+            "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "f32" if w["dtype"] == "f32" else "bf16->f32",
+            "data": "synthetic", "config": {"workload": args.workload, **{k: w[k] for k in w}},
+            "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "rows/s", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="thinker", choices=sorted(WORKLOADS))
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--eager", action="store_true", help="time plain launches instead of CUDA graphs (profiling)")
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, w, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    pkg = __graft_entry__.load_package()
+    ts = pkg.talker_sampler
+    B, V, W = w["rows"], w["vocab"], w["window"]
+    tdt = torch.bfloat16 if w["dtype"] == "bf16" else torch.float32
+    row_bytes = bytes_per_row(w)
+    step_bytes = B * row_bytes
+    # enough distinct logits buffers that one sweep over them exceeds twice the L2
+    nbuf = max(2, math.ceil(2 * L2_BYTES / (B * V * (2 if tdt == torch.bfloat16 else 4))))
+    logits_h, hist_h = make_inputs(w, B, 1000 + rank)
+    base = torch.from_numpy(logits_h).to(dev).to(tdt)
+    bufs = []
+    g = torch.Generator(device=dev).manual_seed(rank)
+    for i in range(nbuf):  # distinct contents: a per-buffer permutation of the columns of each row
+        perm = torch.randperm(V, device=dev, generator=g)
+        bufs.append(base[:, perm].contiguous())
+    del base
+    cfg = ts.TalkerSampling(temperature=w["temperature"], top_p=w["top_p"], top_k=w["top_k"],
+                            repetition_penalty=w["penalty"], window=W, min_new_tokens=0, max_new_tokens=1 << 62,
+                            semantics="omni", rng="counter")
+    state = ts.DecodeState.new(list(range(rank * B, rank * B + B)), cfg, device=dev)
+    state.history.copy_(torch.from_numpy(hist_h).to(dev))
+    kw = ts._cfg_kwargs(cfg, state.history, dev)
+    ops = pkg._native.ops()
+
+    def one_step(i):
+        return ops.sample_state_(bufs[i % nbuf], state.history, state.steps, state.finished, state.seeds, None,
+                                 state.active, kw["alpha"], None, kw["temperature"], cfg.top_p, cfg.top_k, 1,
+                                 cfg.min_new_tokens, cfg.max_new_tokens, -1, ts.SEM_OMNI, ts.RNG_PHILOX,
+                                 kw["max_top_k"], 0)
+
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            one_step(i)
+    torch.cuda.synchronize()
+    # the K timed steps as CUDA graphs (G steps per graph): no host launch cost between steps
+    G = min(args.steps, 1000)
+    reps, rem = divmod(args.steps, G)
+    graphs = []
+    for n in ([] if args.eager else ([G] if reps else []) + ([rem] if rem else [])):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for i in range(n):
+                one_step(i)
+        graphs.append((gr, n))
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(vis.split(",")[local].strip() if vis else local)
+    clocks.start()
+    time.sleep(0.1)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):  # a graph replays on the current stream: time that stream
+        ev0.record(stream)
+        if args.eager:
+            for i in range(args.steps):
+                one_step(i)
+        else:
+            for r in range(reps):
+                graphs[0][0].replay()
+            if rem:
+                graphs[-1][0].replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ck = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = B * world * args.steps / (ms / 1e3)
+    peak, peak_kind = measured_peak_gbs()
+    achieved = step_bytes / (ms_per_step / 1e3) / 1e9
+
+    # end to end through the public API: pinned host logits -> device, sample, tokens -> host, every step
+    e2e_steps = max(1, args.e2e_steps)
+    host = torch.from_numpy(logits_h).to(tdt).pin_memory()
+    dbuf = torch.empty_like(host, device=dev)
+    tok_h = torch.empty(B, dtype=torch.int64).pin_memory()
+    hist_e = state.history.clone()
+    steps_e = torch.zeros(B, dtype=torch.int64, device=dev)
+    seeds_e = state.seeds.clone()
+    for i in range(3 if args.e2e_steps else 0):
+        dbuf.copy_(host, non_blocking=True)
+        tok = ts.sample(dbuf, hist_e, steps_e, seeds_e, -1, cfg, rng="philox")
+        tok_h.copy_(tok, non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        dbuf.copy_(host, non_blocking=True)
+        tok = ts.sample(dbuf, hist_e, steps_e, seeds_e, -1, cfg, rng="philox")
+        tok_h.copy_(tok, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    et = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_value = B * world * e2e_steps / (float(et.item()) / 1e3)
+
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(w, seconds=args.cpu_seconds)
+    for gr, _ in graphs:
+        del gr
+    graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    traffic = profiled_traffic(args.workload)
+    line = {
+        "metric": f"sampled rows/s at B={B} x V={V} per GPU (fused penalty+temperature+top-k+top-p+draw)",
+        "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16->f32" if tdt == torch.bfloat16 else "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "rows_per_gpu": B, "global_batch": B * world, "vocab": V,
+                   "logits_dtype": w["dtype"], "window": W, "temperature": w["temperature"], "top_k": w["top_k"],
+                   "top_p": w["top_p"], "repetition_penalty": w["penalty"], "order": "omni", "rng": "philox",
+                   "parallelism": f"rows x{world}", "l2": f"{nbuf} rotating logits buffers "
+                   f"({nbuf * B * V * (2 if tdt == torch.bfloat16 else 4) / 2**20:.0f} MiB > L2)",
+                   "cuda_graph_steps": 0 if args.eager else G},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "bytes_per_row": row_bytes, "peak_source": peak_kind},
+        "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": host.numel() * host.element_size(),
+                "d2h_bytes_per_step": B * 8, "steps": e2e_steps},
+        "gpu_launches": args.steps,
+        "clocks": ck,
+        "cpu_baseline": cb,
+    }
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,176 @@
+/*
+ * b2s_sampler.h -- C-ABI of the B200 token-sampling engine for MiniCPM-o 4.5 (sm_100a).
+ *
+ * Every entry point takes plain device pointers and sizes plus a CUDA stream handle
+ * (cudaStream_t passed as void*), enqueues its kernels on that stream, never synchronises,
+ * never allocates, and returns B2S_OK or a B2S_ERR_* code for invalid arguments or launch
+ * failures.  Errors that can only be seen on the device (history ids >= vocab, a per-row
+ * top_k above the declared bound, a timed-out wait) are OR-ed into an optional device status
+ * word and the affected row yields token PAD (-1); there are no device traps.
+ *
+ * The interface replaces the reference module engine/talker_sampler.py (pure torch in the
+ * reference; the reference has no native library) and the greedy argmax of the Thinker call
+ * sites.  Each function below cites the reference interface it replaces.
+ */
+#ifndef B2S_SAMPLER_H
+#define B2S_SAMPLER_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2S_ABI_VERSION 1
+
+/* return codes */
+#define B2S_OK 0
+#define B2S_ERR_INVALID 1     /* bad argument (null pointer, size, dtype, parameter range) */
+#define B2S_ERR_UNSUPPORTED 2 /* shape outside what the kernels are built for (e.g. row too large) */
+#define B2S_ERR_CUDA 3        /* a CUDA runtime call failed (see b2s_last_cuda_error) */
+
+/* logits element types */
+#define B2S_DTYPE_F32 0
+#define B2S_DTYPE_BF16 1
+
+/* processing order (engine/talker_sampler.py:142-156) */
+#define B2S_SEM_HF 0       /* x/T -> penalty -> top-p(min_keep) -> top-k; frame 0 unfiltered */
+#define B2S_SEM_OMNI 1     /* EOS censor -> penalty -> /T -> top-k -> top-p (min_keep 1) */
+#define B2S_SEM_IDENTITY 2 /* rows are already processed: draw() only */
+
+/* where the per-row uniform comes from */
+#define B2S_RNG_UNIFORM 0 /* caller-provided uniform_values (draw(uniform_values=...)) */
+#define B2S_RNG_COUNTER 1 /* the reference counter hash of (seed, step), talker_sampler.py:60-76 */
+#define B2S_RNG_PHILOX 2  /* Philox4x32-10: key = seed, counter = (step, request) */
+
+/* bits of the device status word */
+#define B2S_STATUS_HISTORY_RANGE 1u /* a history id >= vocab was ignored */
+#define B2S_STATUS_TOPK_LIMIT 2u    /* a row's top_k exceeded max_top_k; the row returned PAD */
+#define B2S_STATUS_WAIT_TIMEOUT 4u  /* a bounded wait for an in-flight copy gave up; the row returned PAD */
+#define B2S_STATUS_COUNT_LIMIT 8u   /* a token repeated more times than alpha_len-1 in the history */
+#define B2S_STATUS_SHARD_INCOMPLETE 16u /* a shard's candidate list overflowed `cap` or failed; the row returned PAD */
+
+/* flags */
+#define B2S_FLAG_FORCE_GENERAL 1 /* take the exact radix-select path even when the candidate path applies */
+#define B2S_FLAG_TOPK_ONLY 2     /* no top-p cut: keep every value >= the k-th largest (top_k_filter) */
+
+typedef struct b2s_sample_args {
+    /* logits [rows, vocab], row-major with logits_row_stride elements between rows */
+    const void* logits;
+    int32_t logits_dtype;
+    int32_t rows;
+    int32_t vocab;
+    int32_t cluster; /* CTAs per row: 0 = choose automatically, else 1, 2, 4 or 8 */
+    int64_t logits_row_stride;
+    /* penalty history [rows, window] int64 (most recent last); ids < 0 are empty (PAD) */
+    const int64_t* history;
+    int64_t history_row_stride;
+    int32_t window;
+    int32_t eos; /* EOS column; outside [0, vocab) = no EOS column */
+    const int64_t* steps;        /* [rows] frame index of the token being sampled */
+    const int64_t* seeds;        /* [rows] request seeds (B2S_RNG_COUNTER / B2S_RNG_PHILOX) */
+    const int64_t* requests;     /* [rows] Philox counter words 2-3, or NULL (= 0) */
+    const float* uniform_values; /* [rows] (B2S_RNG_UNIFORM) */
+    const uint8_t* active;       /* [rows] bool or NULL (= all active) */
+    const uint8_t* finished;     /* [rows] bool or NULL (= none finished) */
+    /* parameters; the per-row arrays override the scalars when non-NULL */
+    float temperature;
+    float top_p;
+    float presence_penalty;  /* omni order only: subtracted once from seen tokens */
+    float frequency_penalty; /* omni order only: subtracted count times from seen tokens */
+    int32_t top_k;
+    int32_t min_keep; /* k = max(top_k, min_keep) and the top-p cut keeps >= min_keep (omni callers pass 1) */
+    int64_t min_new_tokens;
+    int64_t max_new_tokens;
+    const float* row_temperature;
+    const float* row_top_p;
+    const int32_t* row_top_k;
+    /* alpha[n] = penalty**n for n in [0, alpha_len); alpha_row_stride 0 = one table for all rows */
+    const float* alpha;
+    int32_t alpha_len;
+    int32_t alpha_row_stride;
+    int32_t max_top_k; /* bound on every row's top_k (sizes on-chip buffers); 0 = use top_k */
+    int32_t semantics;
+    int32_t rng;
+    int32_t flags;
+    /* outputs, each optional */
+    int64_t* tokens;                 /* [rows]; PAD (-1) for inactive / finished rows */
+    float* processed;                /* [rows, vocab] processed logits */
+    int64_t processed_row_stride;
+    int64_t* history_out;            /* [rows, window] state after the step (may alias history) */
+    int64_t history_out_row_stride;
+    int64_t* steps_out;              /* [rows] (may alias steps) */
+    uint8_t* finished_out;           /* [rows] (may alias finished) */
+    uint32_t* status;                /* device status word (bits OR-ed), or NULL */
+} b2s_sample_args;
+
+/*
+ * Fused sampling step: per row, processed_logits (temperature, count-based repetition penalty,
+ * optional presence/frequency penalties, EOS min/max rules, top-k/top-p value threshold) and the
+ * inverse-CDF draw in vocabulary order, optionally writing the processed row and advancing the
+ * step() state.
+ * Replaces: engine/talker_sampler.py:136-158 processed_logits, :161-172 draw, :234-249 step
+ * (and :252-254 decode_k as K calls), and the graph bodies engine/runtime/talker_decode.py:120-128,
+ * engine/runtime/talker_post_graph.py:56-76.  With semantics B2S_SEM_IDENTITY it is draw() alone.
+ */
+int b2s_sample(const b2s_sample_args* args, void* stream);
+
+/*
+ * Greedy next token: argmax over each row (first index among equal maxima, NaN wins).
+ * Replaces the Thinker sampling step F.linear(h, lm_head).float().argmax(-1) at
+ * engine/runtime/thinker_decode.py:83,107, engine/runtime/backend_s.py:893,
+ * engine/runtime/backend.py:238, engine/runtime/backend_npu.py:890, engine/runtime/track_s.py:60.
+ */
+int b2s_argmax(const void* logits, int32_t logits_dtype, int32_t rows, int32_t vocab, int64_t row_stride,
+               int64_t* tokens, void* stream);
+
+/*
+ * Per-row U[0,1) from (seed, step[, request]): rng B2S_RNG_COUNTER is the reference counter hash
+ * (engine/talker_sampler.py:60-76 _mix32/uniform), B2S_RNG_PHILOX is Philox4x32-10.
+ */
+int b2s_uniform(const int64_t* seeds, const int64_t* steps, const int64_t* requests, int64_t n, int32_t rng,
+                float* out, void* stream);
+
+/*
+ * Vocabulary-sharded head, stage 1 (no counterpart in the reference, which has no multi-device code).
+ * `args` describes this rank's shard: logits [rows, shard_vocab] are the columns
+ * [vocab_offset, vocab_offset + shard_vocab) of the full head; history ids and eos are global ids.
+ * Omni order only.  Per row it writes every processed element >= the shard's k-th largest value
+ * (k = max(top_k, min_keep)) as (value fp32, global id int32) pairs, unordered, into
+ * cand_values / cand_ids [rows][cap], and the true number of such elements into cand_count[rows]
+ * (> cap means the list was cut; -1 means the row failed on the device).
+ */
+int b2s_shard_candidates(const b2s_sample_args* args, int64_t vocab_offset, int32_t cap, float* cand_values,
+                         int32_t* cand_ids, int32_t* cand_count, void* stream);
+
+/*
+ * Vocabulary-sharded head, stage 2: from the all-gathered stage-1 outputs of `shards` shards
+ * (layout [shards][rows][cap], counts [shards][rows]) draw each row's token over the full vocabulary
+ * `vocab`: top-k values, top-p cut, value threshold, inverse-CDF draw in global id order.  The token
+ * equals b2s_sample's on the unsharded row.  Rows whose lists are incomplete get PAD and set
+ * B2S_STATUS_SHARD_INCOMPLETE.  Uses args->top_k / top_p / min_keep / row_* / rng / seeds / steps /
+ * requests / uniform_values / tokens / status / flags; k must be <= 128.
+ */
+int b2s_shard_merge(const float* cand_values, const int32_t* cand_ids, const int32_t* cand_count, int32_t shards,
+                    int32_t rows, int32_t cap, int32_t vocab, const b2s_sample_args* args, void* stream);
+
+/*
+ * Count-based repetition penalty on its own: out = x * penalty**n where x < 0, x / penalty**n otherwise,
+ * n = occurrences of the column in the row's history (ids < 0 ignored), alpha[n] = penalty**n.
+ * Replaces engine/talker_sampler.py:79-84 repetition_penalty (out is fp32 [rows, vocab]).
+ */
+int b2s_repetition_penalty(const void* x, int32_t x_dtype, int32_t rows, int32_t vocab, int64_t x_row_stride,
+                           const int64_t* history, int32_t window, int64_t history_row_stride, const float* alpha,
+                           int32_t alpha_len, int32_t alpha_row_stride, float* out, int64_t out_row_stride,
+                           uint32_t* status, void* stream);
+
+/* Human-readable text of a B2S_ERR_* code, and of the last CUDA error seen by this library. */
+const char* b2s_error_string(int code);
+const char* b2s_last_cuda_error(void);
+int b2s_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2S_SAMPLER_H */

@@ -1,0 +1,268 @@
+// Device helpers of the B200 sampler: the sampler numerics spec (exp, order keys), the two RNGs,
+// bulk-copy / mbarrier PTX wrappers and CTA-wide primitives (reductions, scans, radix select).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b2s {
+
+constexpr int NT = 512;        // threads per CTA of the row kernels
+constexpr int NWARP = NT / 32;
+constexpr uint32_t WAIT_LIMIT = 1u << 22;  // bounded spin on an mbarrier (each try_wait also sleeps)
+
+// ---------------------------------------------------------------- numerics spec
+
+// exp(x) in fp32: n = rint(x*log2 e), r = x - n*ln2 by a two-constant Cody-Waite reduction, exp(r) by its
+// Taylor series to degree 7 in FMA Horner form, then scaled by exact powers of two.  Every operation is
+// an explicitly rounded fp32 op, so the CPU oracle (same sequence, -ffp-contract=off) gives the same bits.
+__device__ __forceinline__ float b2s_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+    if (x < -103.97208404541015625f) return 0.0f;
+    float t = __fmul_rn(x, 1.44269502162933349609375f);
+    float n = rintf(t);
+    float r = __fmaf_rn(n, -0.693145751953125f, x);
+    r = __fmaf_rn(n, -1.428606765330187045037746429443359375e-6f, r);
+    float p = 1.98412701138295233249664306640625e-4f;
+    p = __fmaf_rn(p, r, 1.3888889225199818611145019531250e-3f);
+    p = __fmaf_rn(p, r, 8.3333337679505348205566406250000e-3f);
+    p = __fmaf_rn(p, r, 4.1666667908430099487304687500000e-2f);
+    p = __fmaf_rn(p, r, 1.6666667163372039794921875000000e-1f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    int ni = (int)n;
+    if (ni > 127) { p = __fmul_rn(p, 2.0f); ni -= 1; }
+    if (ni < -126) { p = __fmul_rn(p, 5.42101086242752217003726400434970855712890625e-20f); ni += 64; }
+    return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+
+__device__ __forceinline__ float f_inf() { return __int_as_float(0x7f800000); }
+__device__ __forceinline__ float f_ninf() { return __int_as_float(0xff800000); }
+
+// Order-preserving 32-bit key of an fp32 value (larger value -> larger key); -0 is keyed as +0 so that
+// the two zeros tie exactly as they do under IEEE comparison.
+__device__ __forceinline__ uint32_t okey(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) == 0) u = 0;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float okey_to_f(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+    return __uint_as_float(u);
+}
+
+__device__ __forceinline__ float bf16_bits_to_f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
+
+// ---------------------------------------------------------------- RNG
+
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x7FEB352Du;
+    x ^= x >> 15;
+    x *= 0x846CA68Bu;
+    x ^= x >> 16;
+    return x;
+}
+
+// Reference counter uniform of (seed, step): three chained lowbias32 finalisers, 24-bit mantissa.
+__device__ __forceinline__ float uniform_counter(int64_t seed, int64_t step) {
+    uint64_t s = (uint64_t)seed;
+    uint32_t h = mix32((uint32_t)s);
+    h = mix32(h ^ (uint32_t)(s >> 32) ^ 0x9E3779B9u);
+    h = mix32(h ^ (uint32_t)((uint64_t)step) ^ 0x632BE5ABu);
+    return (float)(h >> 8) * (1.0f / 16777216.0f);
+}
+
+// Philox4x32-10 (Salmon et al., SC'11); returns the first output word.
+__device__ __forceinline__ uint32_t philox4x32_10_w0(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
+                                                     uint32_t k1) {
+#pragma unroll
+    for (int i = 0; i < 10; ++i) {
+        if (i) { k0 += 0x9E3779B9u; k1 += 0xBB67AE85u; }
+        uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
+        uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
+        uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+        c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+    }
+    return c0;
+}
+
+__device__ __forceinline__ float uniform_philox(int64_t seed, int64_t step, int64_t request) {
+    uint64_t s = (uint64_t)seed, t = (uint64_t)step, q = (uint64_t)request;
+    uint32_t w = philox4x32_10_w0((uint32_t)t, (uint32_t)(t >> 32), (uint32_t)q, (uint32_t)(q >> 32), (uint32_t)s,
+                                  (uint32_t)(s >> 32));
+    return (float)(w >> 8) * (1.0f / 16777216.0f);
+}
+
+// ---------------------------------------------------------------- PTX: mbarrier + bulk copy (no multicast)
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar` (bytes: multiple of 16,
+// both addresses 16-byte aligned).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; returns false when the limit ran out (the caller flags the row and carries on).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    for (uint32_t it = 0; it < WAIT_LIMIT; ++it)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// ---------------------------------------------------------------- warp / CTA primitives
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_incl_scan(double v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        double u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+    }
+    return v;
+}
+
+// CTA-wide helpers use a caller-provided shared scratch of >= NWARP+1 doubles.
+__device__ __forceinline__ float block_max(float v, float* red) {
+    v = warp_max(v);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float r = red[0];
+#pragma unroll
+    for (int i = 1; i < NWARP; ++i) r = fmaxf(r, red[i]);
+    return r;
+}
+// Sum of doubles reduced in a fixed order (warp butterfly, then warps in index order).
+__device__ __forceinline__ double block_sum(double v, double* red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    double r = 0.0;
+#pragma unroll
+    for (int i = 0; i < NWARP; ++i) r += red[i];
+    return r;
+}
+__device__ __forceinline__ int block_sum_i(int v, int* red) {
+    v = warp_sum_i(v);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    int r = 0;
+#pragma unroll
+    for (int i = 0; i < NWARP; ++i) r += red[i];
+    return r;
+}
+// Exclusive scan of one double per thread in thread order; returns the exclusive prefix, *total = sum.
+__device__ __forceinline__ double block_excl_scan(double v, double* red, double* total) {
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    double incl = warp_incl_scan(v);
+    __syncthreads();
+    if (lane == 31) red[w] = incl;
+    __syncthreads();
+    double off = 0.0, tot = 0.0;
+#pragma unroll
+    for (int i = 0; i < NWARP; ++i) {
+        if (i < w) off += red[i];
+        tot += red[i];
+    }
+    *total = tot;
+    return off + incl - v;
+}
+
+// Radix select: the key of the k-th largest (1-based, 1 <= k <= n) of n keys produced by key(i), over 4
+// rounds of 8-bit digits, most significant first.  hist: 256 shared words; ctl: 2 shared words.
+template <typename KeyFn>
+__device__ uint32_t block_kth_largest(int n, int k, KeyFn key, uint32_t* hist, uint32_t* ctl) {
+    uint32_t prefix = 0, mask = 0;
+    int krem = k;
+    const int tid = threadIdx.x;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += NT) hist[i] = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += NT) {
+            uint32_t kk = key(i);
+            if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (tid < 32) {
+            // lane l owns digits 255-8l .. 248-8l (descending)
+            uint32_t c[8];
+            uint32_t s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) { c[j] = hist[255 - 8 * tid - j]; s += c[j]; }
+            uint32_t incl = s;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                uint32_t u = __shfl_up_sync(0xffffffffu, incl, o);
+                if (tid >= o) incl += u;
+            }
+            uint32_t excl = incl - s;
+            if (excl < (uint32_t)krem && (uint32_t)krem <= incl) {
+                uint32_t cum = excl;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (cum + c[j] >= (uint32_t)krem) {
+                        ctl[0] = (uint32_t)(255 - 8 * tid - j);
+                        ctl[1] = (uint32_t)krem - cum;
+                        break;
+                    }
+                    cum += c[j];
+                }
+            }
+        }
+        __syncthreads();
+        prefix |= ctl[0] << shift;
+        mask |= 0xFFu << shift;
+        krem = (int)ctl[1];
+        __syncthreads();
+    }
+    return prefix;
+}
+
+}  // namespace b2s

@@ -1,0 +1,144 @@
+// The final stage of a row, shared by the candidate path of the sampling kernel and the vocabulary-shard
+// merge: from a list of (processed value, vocabulary id) items that contains every element >= the row's
+// k-th largest value (ties included), take the top-k values, the top-p cut, the value threshold, and the
+// inverse-CDF draw over the kept items in vocabulary order.  One CTA (NT threads) runs it.
+#pragma once
+
+#include "b2s_device.cuh"
+
+namespace b2s {
+
+constexpr int KLIST = 128;  // largest k the list stage serves (top-p runs in one warp, 4 values per lane)
+
+// Pointers into the CTA's shared scratch.
+struct Scr {
+    uint32_t* hist;  // 256 words
+    uint32_t* rctl;  // 2 words
+    int* gather_n;
+    int* kn;
+    float* thr;
+    double* red_d;   // NWARP + 1
+    float* red_f;
+    int* red_i;
+};
+
+// Top-k values (descending, with multiplicity) of cv[0..n) into vals[0..k) and the value threshold of the
+// top-p cut (hf: probabilities exp(v - lse) of the full row; omni: softmax over the k values), kept count
+// clamped to [min(min_keep, k), k] (talker_sampler.py:110-115, :127-132).  vals needs 2*KLIST floats;
+// requires k <= KLIST and n >= k.  Returns the threshold (same value in every thread).
+__device__ __forceinline__ float list_threshold(const float* cv, int n, int k, bool hf, float lse, float top_p,
+                                                int min_keep, bool topk_only, float* vals, const Scr& sc) {
+    const int tid = threadIdx.x;
+    const uint32_t kthg = block_kth_largest(n, k, [&](int i) { return okey(cv[i]); }, sc.hist, sc.rctl);
+    if (tid == 0) *sc.gather_n = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += NT)
+        if (okey(cv[i]) > kthg) vals[KLIST + atomicAdd(sc.gather_n, 1)] = cv[i];
+    __syncthreads();
+    const int ng = *sc.gather_n;  // < k
+    for (int i = tid; i < ng; i += NT) {
+        const float vi = vals[KLIST + i];
+        int rank = 0;
+        for (int j = 0; j < ng; ++j) {
+            const float vj = vals[KLIST + j];
+            rank += (vj > vi) || (vj == vi && j < i);
+        }
+        vals[rank] = vi;
+    }
+    for (int i = ng + tid; i < k; i += NT) vals[i] = okey_to_f(kthg);
+    __syncthreads();
+    if (tid < 32) {
+        float pk[4];
+        const float m = vals[0];
+        double ls = 0.0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int idx = tid * 4 + j;
+            float e = 0.0f;
+            if (idx < k) e = hf ? b2s_expf(__fsub_rn(vals[idx], lse)) : b2s_expf(__fsub_rn(vals[idx], m));
+            pk[j] = e;
+            ls += (double)e;
+        }
+        if (!hf) {
+            const float sf = (float)warp_sum(ls);
+            ls = 0.0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                pk[j] = (tid * 4 + j < k) ? __fdiv_rn(pk[j], sf) : 0.0f;
+                ls += (double)pk[j];
+            }
+        }
+        const double incl = warp_incl_scan(ls);
+        double acc = incl - ls;
+        int cnt = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int idx = tid * 4 + j;
+            if (idx < k) {
+                acc += (double)pk[j];
+                cnt += __fsub_rn((float)acc, pk[j]) < top_p;
+            }
+        }
+        cnt = warp_sum_i(cnt);
+        const int kept = topk_only ? k : max(min(min_keep, k), min(cnt, k));
+        if (tid == 0) *sc.thr = vals[kept - 1];
+    }
+    __syncthreads();
+    return *sc.thr;
+}
+
+// Draw over the items >= thr (minus `drop_id` when >= 0): softmax over them, cumulative mass in vocabulary
+// order (fp64, rounded per prefix), first id whose mass exceeds u * total, else V - 1
+// (talker_sampler.py:168-172).  kv/ki and sv/si: scratch of >= n items each.
+__device__ __forceinline__ int64_t list_draw(const float* cv, const int* ci, int n, float thr, int drop_id, float u,
+                                             int V, float* kv, int* ki, float* sv, int* si, const Scr& sc) {
+    const int tid = threadIdx.x;
+    if (tid == 0) *sc.kn = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += NT) {
+        if (cv[i] >= thr && ci[i] != drop_id) {
+            const int pos = atomicAdd(sc.kn, 1);
+            kv[pos] = cv[i];
+            ki[pos] = ci[i];
+        }
+    }
+    __syncthreads();
+    const int kn = *sc.kn;
+    for (int i = tid; i < kn; i += NT) {
+        int rank = 0;
+        const int ii = ki[i];
+        for (int j = 0; j < kn; ++j) rank += ki[j] < ii;
+        sv[rank] = kv[i];
+        si[rank] = ii;
+    }
+    __syncthreads();
+    float lm = __int_as_float(0xff800000);
+    for (int i = tid; i < kn; i += NT) lm = fmaxf(lm, sv[i]);
+    const float m = block_max(lm, sc.red_f);
+    const int per_t = (kn + NT - 1) / NT;
+    const int i0 = min(kn, tid * per_t), i1 = min(kn, i0 + per_t);
+    double es = 0.0;
+    for (int i = i0; i < i1; ++i) es += (double)b2s_expf(__fsub_rn(sv[i], m));
+    const float sf = (float)block_sum(es, sc.red_d);
+    double ps = 0.0;
+    for (int i = i0; i < i1; ++i) ps += (double)__fdiv_rn(b2s_expf(__fsub_rn(sv[i], m)), sf);
+    double total;
+    double off = block_excl_scan(ps, sc.red_d, &total);
+    const float target = __fmul_rn(u, (float)total);
+    int first = 0x7fffffff;
+    for (int i = i0; i < i1; ++i) {
+        const float pi = __fdiv_rn(b2s_expf(__fsub_rn(sv[i], m)), sf);
+        off += (double)pi;
+        if ((float)off > target) { first = i; break; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+    __syncthreads();
+    if ((tid & 31) == 0) sc.red_i[tid >> 5] = first;
+    __syncthreads();
+    int best = 0x7fffffff;
+    for (int w = 0; w < NWARP; ++w) best = min(best, sc.red_i[w]);
+    return best == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)si[best];
+}
+
+}  // namespace b2s

@@ -1,0 +1,107 @@
+"""Vocabulary-sharded Thinker sampling across the GPUs of one node (no counterpart in the reference, which
+runs on a single device).
+
+Rank s holds logits for the contiguous columns [offset_s, offset_s + V_s) of the LM head.  One step:
+
+1. ``shard_candidates`` (kernel): the shard's processed values (omni order: penalty -> /T) and every
+   element >= the shard's k-th largest value, as (value, global id) pairs, plus their count;
+2. one ``all_gather_into_tensor`` over NCCL of the packed [rows, 2*cap+1] int32 buffer (values as bits,
+   ids, count) -- the only exchange;
+3. ``merge_candidates`` (kernel, on every rank): global top-k values, top-p cut, threshold, and the draw in
+   global id order.  Every rank computes the same token, so nothing else is exchanged.
+
+A shard list that overflows ``cap`` (more ties at its k-th value than fit) makes that row's token PAD and
+sets a status bit; it is never silently wrong.  The result equals the unsharded kernel's token on the
+concatenated row.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+
+from . import _native
+from . import talker_sampler as ts
+
+
+def _k(cfg) -> int:
+    return max(int(cfg.top_k), 1)
+
+
+def default_cap(cfg) -> int:
+    k = _k(cfg)
+    c = 1
+    while c < 2 * k:
+        c <<= 1
+    return max(c, 32)
+
+
+def shard_candidates(logits: torch.Tensor, offset: int, history: Optional[torch.Tensor], steps: torch.Tensor, cfg, *,
+                     cap: Optional[int] = None, eos: int = -1, status: Optional[torch.Tensor] = None,
+                     cluster: int = 0):
+    """Stage 1 on this rank's shard ``logits`` [B, V_s] (columns start at global id ``offset``; history ids
+    are global).  Returns (values [B, cap] fp32, ids [B, cap] int32 global, count [B] int32)."""
+    ts._need_cuda(logits, history, steps)
+    cap = cap or default_cap(cfg)
+    W = 0 if history is None else history.shape[-1]
+    alpha = ts.alpha_table(cfg.repetition_penalty, W + 1, logits.device) if W > 0 else None
+    return _native.ops().shard_candidates(
+        logits, history, steps.to(torch.int64), alpha, None, None, None, status, ts._temperature(cfg.temperature),
+        float(cfg.top_p), int(cfg.top_k), 1, float(getattr(cfg, "presence_penalty", 0.0)),
+        float(getattr(cfg, "frequency_penalty", 0.0)), int(eos), _k(cfg), int(offset), int(cap), int(cluster))
+
+
+def merge_candidates(values, ids, counts, vocab: int, steps: torch.Tensor, seeds: Optional[torch.Tensor], cfg, *,
+                     uniform_values: Optional[torch.Tensor] = None, requests: Optional[torch.Tensor] = None,
+                     rng: str = "philox", status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Stage 2 over all shards' candidates (lists of per-shard tensors, or stacked [S, B, cap] / [S, B])."""
+    if isinstance(values, (list, tuple)):
+        values, ids, counts = torch.stack(list(values)), torch.stack(list(ids)), torch.stack(list(counts))
+    ts._need_cuda(values, ids, counts, steps, seeds, uniform_values, requests)
+    if _k(cfg) > 128:
+        raise ValueError("vocabulary-sharded sampling supports top_k <= 128")
+    if uniform_values is not None:
+        r = ts.RNG_UNIFORM
+        uniform_values = uniform_values.to(torch.float32).contiguous()
+    else:
+        r = {"philox": ts.RNG_PHILOX, "counter": ts.RNG_COUNTER}[rng]
+    return _native.ops().shard_merge(values.contiguous(), ids.contiguous(), counts.contiguous(), int(vocab),
+                                     steps.to(torch.int64), seeds, requests, uniform_values, None, None, status,
+                                     float(cfg.top_p), int(cfg.top_k), 1, r, 0)
+
+
+def pack(values: torch.Tensor, ids: torch.Tensor, counts: torch.Tensor) -> torch.Tensor:
+    """[B, 2*cap+1] int32: value bits | ids | count (one buffer -> one collective)."""
+    return torch.cat([values.view(torch.int32), ids, counts[:, None]], dim=1).contiguous()
+
+
+def unpack(buf: torch.Tensor, shards: int, rows: int, cap: int):
+    b = buf.view(shards, rows, 2 * cap + 1)
+    return (b[:, :, :cap].contiguous().view(torch.float32), b[:, :, cap:2 * cap].contiguous(),
+            b[:, :, 2 * cap].contiguous())
+
+
+def sample_sharded(logits: torch.Tensor, offset: int, vocab: int, history: Optional[torch.Tensor],
+                   steps: torch.Tensor, seeds: Optional[torch.Tensor], cfg, *, group=None, cap: Optional[int] = None,
+                   uniform_values: Optional[torch.Tensor] = None, requests: Optional[torch.Tensor] = None,
+                   rng: str = "philox", status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One sampled token per row of the full vocabulary, from this rank's shard; every rank returns the same
+    tokens.  ``group``: the torch.distributed process group of the shards (rank order = shard order)."""
+    import torch.distributed as dist
+
+    cap = cap or default_cap(cfg)
+    v, i, n = shard_candidates(logits, offset, history, steps, cfg, cap=cap, status=status)
+    mine = pack(v, i, n)
+    world = dist.get_world_size(group)
+    allb = torch.empty((world * mine.shape[0], mine.shape[1]), dtype=torch.int32, device=mine.device)
+    dist.all_gather_into_tensor(allb, mine, group=group)
+    vv, ii, nn = unpack(allb, world, mine.shape[0], cap)
+    return merge_candidates(vv, ii, nn, vocab, steps, seeds, cfg, uniform_values=uniform_values, requests=requests,
+                            rng=rng, status=status)
+
+
+def shard_bounds(vocab: int, shards: int) -> Sequence[int]:
+    """Contiguous shard offsets (the last shard takes the remainder)."""
+    per = -(-vocab // shards)
+    return [min(vocab, s * per) for s in range(shards + 1)]

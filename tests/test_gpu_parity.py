@@ -1,0 +1,335 @@
+"""CUDA path against the CPU oracle and the reference's golden outputs (B200 only).
+
+Parity bar: processed logits bit-identical (finite values and -inf pattern); kept set and token ids
+identical -- no boundary exceptions against the oracle, which evaluates the same numerics spec.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as orc
+from tests import _harness as H
+from tests.golden import cases as C
+from tests.golden import inputs as I
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+GROUPS = {"talker": C.talker_cases, "thinker": C.thinker_cases, "edge": C.edge_cases}
+
+
+def _cases():
+    for group, make in GROUPS.items():
+        for case in make():
+            yield pytest.param(group, case, id=case.name)
+
+
+def gpu_logits(case):
+    if case.dtype == "bf16":
+        return torch.from_numpy(case.bf16_bits().view(np.int16)).view(torch.bfloat16).to(DEV)
+    return torch.from_numpy(case.logits).to(DEV)
+
+
+def cfg_of(ts, case):
+    c = case.cfgs[0]
+    return ts.TalkerSampling(**{k: v for k, v in c.items() if k in ts.TalkerSampling.__dataclass_fields__})
+
+
+def row_params(ts, case):
+    if case.uniform_cfg():
+        return None
+    cs = case.cfgs
+    return ts.RowParams(temperature=torch.tensor([c["temperature"] for c in cs], dtype=torch.float32, device=DEV),
+                        top_p=torch.tensor([c["top_p"] for c in cs], dtype=torch.float32, device=DEV),
+                        top_k=torch.tensor([c["top_k"] for c in cs], dtype=torch.int32, device=DEV),
+                        repetition_penalty=[c["repetition_penalty"] for c in cs],
+                        max_top_k=max(c["top_k"] for c in cs))
+
+
+def run_gpu(ts, case, *, counter=False, exact=False, cluster=0, processed=True):
+    x = gpu_logits(case)
+    hist = torch.from_numpy(case.history).to(DEV)
+    steps = torch.from_numpy(case.steps).to(DEV)
+    seeds = torch.from_numpy(case.seeds).to(DEV)
+    u = None if counter else torch.from_numpy(case.uniforms).to(DEV)
+    kw = ts._cfg_kwargs(cfg_of(ts, case), hist, DEV, row_params(ts, case))
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    tok, proc, _, _, _ = ts._run(x, history=hist, steps=steps, seeds=seeds, uniform_values=u, eos=case.eos,
+                                 rng=ts.RNG_COUNTER if counter else ts.RNG_UNIFORM, status=status,
+                                 flags=ts.FLAG_FORCE_EXACT if exact else 0, cluster=cluster, tokens=True,
+                                 processed=processed, **kw)
+    return (proc.cpu().numpy() if processed else None), tok.cpu().numpy(), int(status.item())
+
+
+@pytest.mark.parametrize("group,case", list(_cases()))
+def test_sample_matches_oracle_and_reference(pkg, group, case):
+    ts = pkg.talker_sampler
+    fx = H.fixture(group)
+    assert str(fx[f"{case.name}.digest"]) == case.digest()
+    want_p, want_t, meta, _ = H.run_oracle(case)
+    got_p, got_t, status = run_gpu(ts, case)
+    assert status == 0
+    assert len(H.compare_processed(want_p, got_p)) == 0
+    assert np.array_equal(got_t, want_t), (got_t, want_t, meta)
+    # and the reference's own outputs (identical on every fixture so far)
+    assert len(H.compare_processed(fx[f"{case.name}.processed"], got_p)) == 0
+    mism = np.nonzero(fx[f"{case.name}.tok_u"] != got_t)[0]
+    assert all(H.boundary_rows(meta)[r] for r in mism)
+    # counter RNG (the reference's uniform(seed, step))
+    _, got_c, _ = run_gpu(ts, case, counter=True, processed=False)
+    assert np.array_equal(got_c, fx[f"{case.name}.tok_c"])
+
+
+@pytest.mark.parametrize("group,case", [p for p in _cases() if p.values[1].name in (
+    "hf_t5", "hf_t60", "omni_t7", "cfg2_talker_batched", "cfg3_thinker", "cfg4_large", "cfg5_ties",
+    "edge_quantised_hf", "edge_quantised_omni", "edge_temperature_3.0_omni", "edge_penalty_big_hf",
+    "edge_min_new_boundary_hf", "edge_bf16_hf", "edge_small_vocab_omni")])
+@pytest.mark.parametrize("cluster", [1, 2, 4, 8])
+def test_exact_path_and_cluster_sizes_agree(pkg, group, case, cluster):
+    """The radix-select path and every cluster split give the same bits as the candidate path."""
+    ts = pkg.talker_sampler
+    if case.vocab * (2 if case.dtype == "bf16" else 4) / cluster > 200 * 1024:
+        pytest.skip("a row slice this large does not fit one CTA's shared memory (the launcher refuses it)")
+    want_p, want_t, _, _ = H.run_oracle(case)
+    for exact in (False, True):
+        got_p, got_t, _ = run_gpu(ts, case, exact=exact, cluster=cluster)
+        assert len(H.compare_processed(want_p, got_p)) == 0, (exact, cluster)
+        assert np.array_equal(got_t, want_t), (exact, cluster, got_t, want_t)
+
+
+def test_draw_matches_reference(pkg):
+    ts = pkg.talker_sampler
+    fx = H.fixture("talker")
+    for case in C.talker_cases():
+        proc = torch.from_numpy(fx[f"{case.name}.processed"]).to(DEV)
+        tok = ts.draw(proc, torch.from_numpy(case.seeds).to(DEV), torch.from_numpy(case.steps).to(DEV),
+                      uniform_values=torch.from_numpy(case.uniforms).to(DEV))
+        want, _ = orc.draw(fx[f"{case.name}.processed"], case.uniforms)
+        assert np.array_equal(tok.cpu().numpy(), want), case.name
+        assert np.array_equal(tok.cpu().numpy(), fx[f"{case.name}.tok_u"]), case.name
+
+
+def test_uniform_counter_and_philox(pkg):
+    ts = pkg.talker_sampler
+    fx = H.fixture("rng")
+    seeds = torch.from_numpy(fx["seeds"]).to(DEV)
+    steps = torch.arange(1024, dtype=torch.int64, device=DEV)[:, None]
+    got = ts.uniform(seeds[None, :], steps).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), fx["uniform"].view(np.uint32))
+    s = np.repeat(fx["seeds"], 64)
+    t = np.tile(np.arange(64, dtype=np.int64), len(fx["seeds"]))
+    q = np.arange(s.size, dtype=np.int64) * 3
+    want = orc.uniform(s, t, rng=orc.RNG_PHILOX, requests=q)
+    got = ts.philox_uniform(torch.from_numpy(s).to(DEV), torch.from_numpy(t).to(DEV), torch.from_numpy(q).to(DEV))
+    assert np.array_equal(got.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_argmax_matches_reference(pkg):
+    fx = H.fixture("rng")
+    g = I.rng(9)
+    am_f32 = I.quantised_rows(g, 6, I.THINKER_V, q=4)
+    am_f32[3, 1000:1010] = am_f32[3].max() + 1.0
+    bits = I.to_bf16_bits(I.quantised_rows(g, 6, I.THINKER_V, q=16))
+    am = pkg.thinker_sampler.argmax
+    assert np.array_equal(am(torch.from_numpy(am_f32).to(DEV)).cpu().numpy(), fx["argmax_f32"])
+    x = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(DEV)
+    assert np.array_equal(am(x).cpu().numpy(), fx["argmax_bf16"])
+    # odd vocabularies / misaligned rows / NaN
+    for V in (1, 7, 6562, 151_748):
+        y = torch.randn(5, V + 3, device=DEV)[:, 3:]
+        assert torch.equal(am(y), y.float().argmax(-1))
+        yb = y.to(torch.bfloat16)
+        assert torch.equal(am(yb), yb.float().cpu().argmax(-1).to(DEV))
+    z = torch.randn(2, 1000, device=DEV)
+    z[1, 17] = float("nan")
+    assert am(z)[1].item() == 17
+
+
+def test_sequences_match_reference(pkg):
+    ts = pkg.talker_sampler
+    fx = H.fixture("seq")
+    for name in C.SEQUENCES:
+        x, cfgd, seeds, inactive = C.sequence_inputs(name)
+        assert str(fx[f"{name}.digest"]) == I.digest(x)
+        cfg = ts.TalkerSampling(**cfgd)
+        st = ts.DecodeState.new(seeds, cfg, device=DEV)
+        for r in inactive:
+            st.active[r] = False
+        toks = ts.decode_k(st, torch.from_numpy(x).to(DEV), I.TALKER_EOS, cfg)
+        assert np.array_equal(toks.cpu().numpy(), fx[f"{name}.tokens"]), name
+        assert np.array_equal(st.steps.cpu().numpy(), fx[f"{name}.steps"])
+        assert np.array_equal(st.history.cpu().numpy(), fx[f"{name}.history"])
+        assert np.array_equal(st.finished.cpu().numpy(), fx[f"{name}.finished"])
+
+
+def _full_size(ts, kind, B, seed):
+    g = I.rng(seed)
+    if kind == "cfg3":
+        logits, hist = I.zipf_rows(g, B, I.THINKER_V, 512)
+        logits = I.bf16_bits_to_f32(I.to_bf16_bits(logits))
+        cfg = dict(temperature=0.7, top_k=20, top_p=0.8, repetition_penalty=1.05)
+        dtype = "bf16"
+    elif kind == "cfg4":
+        logits = (g.standard_normal((B, I.THINKER_V)) * 3).astype(np.float32)
+        hist = g.integers(0, I.THINKER_V, size=(B, 2048))
+        cfg = dict(temperature=1.0, top_k=50, top_p=0.95, repetition_penalty=1.1)
+        dtype = "f32"
+    else:
+        logits = I.quantised_rows(g, B, I.THINKER_V)
+        hist = np.full((B, 4), -1, np.int64)
+        cfg = dict(temperature=0.8, top_k=64, top_p=0.9, repetition_penalty=1.0)
+        dtype = "bf16"
+    case = C.Case(kind, logits, dtype, hist, np.full(B, 11, np.int64), g.integers(0, 1 << 62, size=B, dtype=np.int64),
+                  g.random(B, dtype=np.float32), -1,
+                  [C._cfg(window=hist.shape[1], min_new_tokens=0, max_new_tokens=C.BIG, min_keep=1, semantics="omni",
+                          **cfg)] * B)
+    return case
+
+
+@pytest.mark.parametrize("kind,B", [("cfg3", 64), ("cfg4", 24), ("cfg5", 64)])
+def test_benchmark_shapes_match_oracle(pkg, kind, B):
+    """The benchmark workloads at (or near) full size: bit-identical processed rows and tokens."""
+    ts = pkg.talker_sampler
+    case = _full_size(ts, kind, B, 100 + B)
+    want_p, want_t, _, _ = H.run_oracle(case)
+    got_p, got_t, status = run_gpu(ts, case)
+    assert status == 0
+    assert len(H.compare_processed(want_p, got_p)) == 0
+    assert np.array_equal(got_t, want_t)
+    _, got_c, _ = run_gpu(ts, case, counter=True, processed=False)
+    _, want_c, _, _ = H.run_oracle(case, counter=True)
+    assert np.array_equal(got_c, want_c)
+
+
+def test_step_state_matches_oracle_sequence(pkg):
+    """step() over 40 frames (hf, EOS rules, penalties) equals the oracle driven frame by frame."""
+    ts = pkg.talker_sampler
+    cfg = ts.TalkerSampling(min_new_tokens=10, max_new_tokens=30)
+    B, V = 6, I.TALKER_V
+    g = I.rng(77)
+    st = ts.DecodeState.new([int(s) for s in g.integers(0, 1 << 62, size=B)], cfg, device=DEV)
+    st.active[4] = False
+    hist = np.full((B, 16), -1, np.int64)
+    steps = np.zeros(B, np.int64)
+    fin = np.zeros(B, bool)
+    act = np.ones(B, bool)
+    act[4] = False
+    seeds = st.seeds.cpu().numpy()
+    ocfg = orc.Cfg(min_new_tokens=10, max_new_tokens=30)
+    for f in range(40):
+        x = (g.standard_normal((B, V)) * 2).astype(np.float32)
+        if f == 12:
+            x[1, I.TALKER_EOS] = 50.0
+        tok = ts.step(st, torch.from_numpy(x).to(DEV), I.TALKER_EOS, cfg).cpu().numpy()
+        _, want, _, _ = orc.sample(x, hist, steps, seeds, I.TALKER_EOS, ocfg, rng=orc.RNG_COUNTER)
+        live = act & ~fin
+        want = np.where(live, want, -1)
+        assert np.array_equal(tok, want), f
+        hist = np.where(live[:, None], np.concatenate([hist[:, 1:], want[:, None]], 1), hist)
+        steps = steps + live
+        fin = fin | (live & (want == I.TALKER_EOS))
+        assert np.array_equal(st.history.cpu().numpy(), hist)
+        assert np.array_equal(st.steps.cpu().numpy(), steps)
+        assert np.array_equal(st.finished.cpu().numpy(), fin)
+    assert fin[1] and steps[4] == 0
+
+
+def test_step_inplace_matches_step(pkg):
+    ts = pkg.talker_sampler
+    cfg = ts.TalkerSampling(semantics="omni", rng="counter", min_new_tokens=3)
+    a = ts.DecodeState.new([5, 6, 7], cfg, device=DEV)
+    b = ts.DecodeState.new([5, 6, 7], cfg, device=DEV)
+    hist_view = b.history
+    for f in range(12):
+        x = torch.randn(3, I.TALKER_V, device=DEV) * 2
+        t1 = ts.step(a, x, I.TALKER_EOS, cfg)
+        t2 = ts.step_(b, x, I.TALKER_EOS, cfg)
+        assert torch.equal(t1, t2)
+        assert torch.equal(a.history, b.history) and torch.equal(a.steps, b.steps)
+        assert torch.equal(a.finished, b.finished)
+    assert b.history is hist_view  # advanced in place
+
+
+def test_repetition_penalty_matches_reference_formula(pkg):
+    ts = pkg.talker_sampler
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(5, 1000, generator=g) * 3
+    hist = torch.randint(0, 40, (5, 64), generator=g)
+    hist[:, ::5] = -1
+    for pen in (1.05, 0.7, 3.0):
+        got = ts.repetition_penalty(x.to(DEV), hist.to(DEV), pen).cpu()
+        valid = hist >= 0
+        freq = torch.zeros_like(x).scatter_add_(1, hist.clamp(min=0), valid.to(x.dtype))
+        alpha = torch.pow(torch.full_like(x, pen), freq)
+        want = torch.where(x < 0, x * alpha, x / alpha)
+        assert torch.equal(got, want)
+    xb = x.to(torch.bfloat16)
+    got = ts.repetition_penalty(xb.to(DEV), hist.to(DEV), 1.2).cpu()
+    freq = torch.zeros(5, 1000).scatter_add_(1, hist.clamp(min=0), (hist >= 0).float())
+    alpha = torch.pow(torch.full((5, 1000), 1.2), freq)
+    xf = xb.float()
+    assert torch.equal(got, torch.where(xf < 0, xf * alpha, xf / alpha))
+
+
+def test_filters_match_oracle_forms(pkg):
+    ts = pkg.talker_sampler
+    g = torch.Generator().manual_seed(0)
+    for scale in (0.3, 1.0, 3.0, 8.0):
+        x = torch.randn(64, I.TALKER_V, generator=g) * scale
+        xd = x.to(DEV)
+        # top_k_filter: pure selection
+        kth = torch.topk(x, 25, dim=-1).values[:, -1:]
+        assert torch.equal(ts.top_k_filter(xd, 25, 3).cpu(), x.masked_fill(x < kth, float("-inf")))
+        # fused hf / omni filters == the oracle on T=1, no history, step 1, no EOS column
+        for sem, fn in (("hf", lambda: ts.top_p_top_k_filter(xd, 0.85, 25, 3)),
+                        ("omni", lambda: ts.top_k_top_p_filter(xd, 25, 0.85, 1))):
+            want, _, _, _ = orc.sample(x.numpy(), np.full((64, 1), -1), np.ones(64, np.int64), None, -1,
+                                       orc.Cfg(temperature=1.0, top_p=0.85, top_k=25, min_new_tokens=0,
+                                               max_new_tokens=1 << 40, min_keep=3, semantics=sem),
+                                       uniforms=np.zeros(64, np.float32))
+            got = fn().cpu().numpy()
+            assert len(H.compare_processed(want, got)) == 0, sem
+
+
+def test_status_flags_and_pad_rows(pkg):
+    ts = pkg.talker_sampler
+    cfg = ts.TalkerSampling(semantics="omni", rng="counter", min_new_tokens=0)
+    x = torch.randn(4, 100, device=DEV)
+    hist = torch.tensor([[1, 2, 3, 500]] * 4, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    tok = ts.sample(x, hist, torch.ones(4, dtype=torch.int64, device=DEV), torch.arange(4, device=DEV), 99, cfg,
+                    active=torch.tensor([True, False, True, True], device=DEV), status=status)
+    assert int(status.item()) & 1  # B2S_STATUS_HISTORY_RANGE
+    assert tok[1].item() == -1 and (tok[[0, 2, 3]] >= 0).all()
+    with pytest.raises(ValueError):
+        ts.sample(x.cpu(), hist.cpu(), torch.ones(4, dtype=torch.int64), torch.arange(4), 99, cfg)
+    with pytest.raises(ValueError):
+        ts.processed_logits(x, hist, torch.ones(4, dtype=torch.int64, device=DEV), 99,
+                            ts.TalkerSampling(semantics="bogus"))
+    with pytest.raises(ValueError):
+        ts.processed_logits(x, hist, torch.ones(4, dtype=torch.int64, device=DEV), 99,
+                            ts.TalkerSampling(temperature=0.0))
+
+
+def test_shard_candidates_merge_equal_unsharded(pkg):
+    """Vocabulary-sharded sampling on one GPU (8 shards run one after the other) == the unsharded kernel."""
+    vs = pkg.vocab_shard
+    ts = pkg.talker_sampler
+    for kind, B in (("cfg5", 32), ("cfg3", 16)):
+        case = _full_size(ts, kind, B, 7 + B)
+        x = gpu_logits(case)
+        hist = torch.from_numpy(case.history).to(DEV)
+        steps = torch.from_numpy(case.steps).to(DEV)
+        seeds = torch.from_numpy(case.seeds).to(DEV)
+        u = torch.from_numpy(case.uniforms).to(DEV)
+        cfg = cfg_of(ts, case)
+        want = ts.sample(x, hist, steps, seeds, -1, cfg, uniform_values=u).cpu().numpy()
+        _, want_o, _, _ = H.run_oracle(case)
+        assert np.array_equal(want, want_o)
+        shards = 8
+        Vs = I.THINKER_V // shards
+        cand = [vs.shard_candidates(x[:, s * Vs:(s + 1) * Vs].contiguous(), s * Vs, hist, steps, cfg, cap=256)
+                for s in range(shards)]
+        got = vs.merge_candidates([c[0] for c in cand], [c[1] for c in cand], [c[2] for c in cand], I.THINKER_V,
+                                  steps, seeds, cfg, uniform_values=u).cpu().numpy()
+        assert np.array_equal(got, want), kind
