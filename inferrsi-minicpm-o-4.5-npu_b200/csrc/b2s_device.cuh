@@ -120,6 +120,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// Asynchronous 4 / 8-byte copies global -> shared (the issuing thread does not wait for them).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -129,12 +138,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait; returns false when the limit ran out (the caller flags the row and carries on).
+// try_wait that suspends the thread until the phase completes or `ns` nanoseconds pass, so waiting warps do
+// not take issue slots and shared-memory bandwidth from the warps still working
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; returns false when the limit ran out (the caller flags the row and carries on).  At most
+// WAIT_SLEEP_LIMIT suspensions of WAIT_SLEEP_NS each (about 1.3 s).
+constexpr uint32_t WAIT_SLEEP_NS = 5000, WAIT_SLEEP_LIMIT = 1u << 18;
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    for (uint32_t it = 0; it < WAIT_LIMIT; ++it)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    for (uint32_t it = 0; it < WAIT_SLEEP_LIMIT; ++it)
+        if (mbar_try_wait_sleep(bar, parity, WAIT_SLEEP_NS)) return true;
     return false;
 }
+
+// Split cluster barrier (release on arrive, acquire on wait); every thread of every CTA takes part.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- warp / CTA primitives
 
@@ -225,9 +252,16 @@ __device__ uint32_t block_kth_largest(int n, int k, KeyFn key, uint32_t* hist, u
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int i = tid; i < 256; i += NT) hist[i] = 0;
         __syncthreads();
-        for (int i = tid; i < n; i += NT) {
-            uint32_t kk = key(i);
-            if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255u], 1u);
+        // whole warps iterate together so equal digits can be aggregated (one atomic per distinct digit)
+        for (int base = 0; base < n; base += NT) {
+            const int i = base + tid;
+            uint32_t d = 256u;
+            if (i < n) {
+                const uint32_t kk = key(i);
+                if ((kk & mask) == prefix) d = (kk >> shift) & 255u;
+            }
+            const uint32_t same = __match_any_sync(0xffffffffu, d);
+            if (d != 256u && (threadIdx.x & 31) == (uint32_t)(__ffs(same) - 1)) atomicAdd(&hist[d], (uint32_t)__popc(same));
         }
         __syncthreads();
         if (tid < 32) {

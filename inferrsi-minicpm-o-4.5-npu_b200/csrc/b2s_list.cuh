@@ -1,18 +1,19 @@
 // The final stage of a row, shared by the candidate path of the sampling kernel and the vocabulary-shard
 // merge: from a list of (processed value, vocabulary id) items that contains every element >= the row's
 // k-th largest value (ties included), take the top-k values, the top-p cut, the value threshold, and the
-// inverse-CDF draw over the kept items in vocabulary order.  One CTA (NT threads) runs it.
+// inverse-CDF draw over the kept items in vocabulary order.  One CTA (NT threads) runs it; the short
+// sequential parts (top-p, the ordered cumulative mass) run in warp 0 without block barriers.
 #pragma once
 
 #include "b2s_device.cuh"
 
 namespace b2s {
 
-constexpr int KLIST = 128;  // largest k the list stage serves (top-p runs in one warp, 4 values per lane)
+constexpr int KLIST = 128;  // largest k the list stage serves (top-p in one warp, 4 values per lane)
 
 // Pointers into the CTA's shared scratch.
 struct Scr {
-    uint32_t* hist;  // 256 words
+    uint32_t* hist;  // 256 words (radix select)
     uint32_t* rctl;  // 2 words
     int* gather_n;
     int* kn;
@@ -22,18 +23,29 @@ struct Scr {
     int* red_i;
 };
 
-// Top-k values (descending, with multiplicity) of cv[0..n) into vals[0..k) and the value threshold of the
-// top-p cut (hf: probabilities exp(v - lse) of the full row; omni: softmax over the k values), kept count
-// clamped to [min(min_keep, k), k] (talker_sampler.py:110-115, :127-132).  vals needs 2*KLIST floats;
-// requires k <= KLIST and n >= k.  Returns the threshold (same value in every thread).
-__device__ __forceinline__ float list_threshold(const float* cv, int n, int k, bool hf, float lse, float top_p,
-                                                int min_keep, bool topk_only, float* vals, const Scr& sc) {
+// The k largest values of cv[0..n) (n >= k), descending with multiplicity, into vals[0..k).  Small lists
+// rank every item by counting (value desc, position asc: ranks are a permutation); longer ones find the
+// k-th key by radix select first and rank only the items above it.  vals needs 2*KLIST floats.
+__device__ __forceinline__ void list_topk_values(const float* cv, int n, int k, float* vals, const Scr& sc) {
     const int tid = threadIdx.x;
-    const uint32_t kthg = block_kth_largest(n, k, [&](int i) { return okey(cv[i]); }, sc.hist, sc.rctl);
+    if (n <= 2 * NT) {
+        for (int i = tid; i < n; i += NT) {
+            const float vi = cv[i];
+            int rank = 0;
+            for (int j = 0; j < n; ++j) {
+                const float vj = cv[j];
+                rank += (vj > vi) | ((vj == vi) & (j < i));
+            }
+            if (rank < k) vals[rank] = vi;
+        }
+        __syncthreads();
+        return;
+    }
+    const uint32_t kth = block_kth_largest(n, k, [&](int i) { return okey(cv[i]); }, sc.hist, sc.rctl);
     if (tid == 0) *sc.gather_n = 0;
     __syncthreads();
     for (int i = tid; i < n; i += NT)
-        if (okey(cv[i]) > kthg) vals[KLIST + atomicAdd(sc.gather_n, 1)] = cv[i];
+        if (okey(cv[i]) > kth) vals[KLIST + atomicAdd(sc.gather_n, 1)] = cv[i];
     __syncthreads();
     const int ng = *sc.gather_n;  // < k
     for (int i = tid; i < ng; i += NT) {
@@ -41,47 +53,63 @@ __device__ __forceinline__ float list_threshold(const float* cv, int n, int k, b
         int rank = 0;
         for (int j = 0; j < ng; ++j) {
             const float vj = vals[KLIST + j];
-            rank += (vj > vi) || (vj == vi && j < i);
+            rank += (vj > vi) | ((vj == vi) & (j < i));
         }
         vals[rank] = vi;
     }
-    for (int i = ng + tid; i < k; i += NT) vals[i] = okey_to_f(kthg);
+    for (int i = ng + tid; i < k; i += NT) vals[i] = okey_to_f(kth);
     __syncthreads();
-    if (tid < 32) {
-        float pk[4];
-        const float m = vals[0];
-        double ls = 0.0;
+}
+
+// Warp 0: the value threshold of the top-p cut over vals[0..k) (hf: probabilities exp(v - lse) of the full
+// row; omni: softmax over the k values), kept count clamped to [min(min_keep, k), k]
+// (talker_sampler.py:110-115, :127-132).  Returns the threshold in lane 0..31 of warp 0.
+__device__ __forceinline__ float warp_topp_threshold(const float* vals, int k, bool hf, float lse, float top_p,
+                                                     int min_keep, bool topk_only) {
+    const int lane = threadIdx.x & 31;
+    float pk[4];
+    const float m = vals[0];
+    double ls = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int idx = lane * 4 + j;
+        float e = 0.0f;
+        if (idx < k) e = hf ? b2s_expf(__fsub_rn(vals[idx], lse)) : b2s_expf(__fsub_rn(vals[idx], m));
+        pk[j] = e;
+        ls += (double)e;
+    }
+    if (!hf) {
+        const float sf = (float)warp_sum(ls);
+        ls = 0.0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const int idx = tid * 4 + j;
-            float e = 0.0f;
-            if (idx < k) e = hf ? b2s_expf(__fsub_rn(vals[idx], lse)) : b2s_expf(__fsub_rn(vals[idx], m));
-            pk[j] = e;
-            ls += (double)e;
+            pk[j] = (lane * 4 + j < k) ? __fdiv_rn(pk[j], sf) : 0.0f;
+            ls += (double)pk[j];
         }
-        if (!hf) {
-            const float sf = (float)warp_sum(ls);
-            ls = 0.0;
+    }
+    const double incl = warp_incl_scan(ls);
+    double acc = incl - ls;
+    int cnt = 0;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                pk[j] = (tid * 4 + j < k) ? __fdiv_rn(pk[j], sf) : 0.0f;
-                ls += (double)pk[j];
-            }
+    for (int j = 0; j < 4; ++j) {
+        const int idx = lane * 4 + j;
+        if (idx < k) {
+            acc += (double)pk[j];
+            cnt += __fsub_rn((float)acc, pk[j]) < top_p;
         }
-        const double incl = warp_incl_scan(ls);
-        double acc = incl - ls;
-        int cnt = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int idx = tid * 4 + j;
-            if (idx < k) {
-                acc += (double)pk[j];
-                cnt += __fsub_rn((float)acc, pk[j]) < top_p;
-            }
-        }
-        cnt = warp_sum_i(cnt);
-        const int kept = topk_only ? k : max(min(min_keep, k), min(cnt, k));
-        if (tid == 0) *sc.thr = vals[kept - 1];
+    }
+    cnt = warp_sum_i(cnt);
+    const int kept = topk_only ? k : max(min(min_keep, k), min(cnt, k));
+    return vals[kept - 1];
+}
+
+// Top-k values + top-p threshold for the whole CTA (k <= KLIST, n >= k); same value in every thread.
+__device__ __forceinline__ float list_threshold(const float* cv, int n, int k, bool hf, float lse, float top_p,
+                                                int min_keep, bool topk_only, float* vals, const Scr& sc) {
+    list_topk_values(cv, n, k, vals, sc);
+    if (threadIdx.x < 32) {
+        const float t = warp_topp_threshold(vals, k, hf, lse, top_p, min_keep, topk_only);
+        if (threadIdx.x == 0) *sc.thr = t;
     }
     __syncthreads();
     return *sc.thr;
@@ -89,7 +117,7 @@ __device__ __forceinline__ float list_threshold(const float* cv, int n, int k, b
 
 // Draw over the items >= thr (minus `drop_id` when >= 0): softmax over them, cumulative mass in vocabulary
 // order (fp64, rounded per prefix), first id whose mass exceeds u * total, else V - 1
-// (talker_sampler.py:168-172).  kv/ki and sv/si: scratch of >= n items each.
+// (talker_sampler.py:168-172).  kv/ki and sv/si: scratch of >= n items each.  Result in every thread.
 __device__ __forceinline__ int64_t list_draw(const float* cv, const int* ci, int n, float thr, int drop_id, float u,
                                              int V, float* kv, int* ki, float* sv, int* si, const Scr& sc) {
     const int tid = threadIdx.x;
@@ -112,6 +140,50 @@ __device__ __forceinline__ int64_t list_draw(const float* cv, const int* ci, int
         si[rank] = ii;
     }
     __syncthreads();
+    if (kn <= 128) {
+        // warp 0, 4 consecutive items per lane (index order)
+        if (tid < 32) {
+            float pv[4];
+            float lm = __int_as_float(0xff800000);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = tid * 4 + j;
+                pv[j] = i < kn ? sv[i] : __int_as_float(0xff800000);
+                lm = fmaxf(lm, pv[j]);
+            }
+            const float m = warp_max(lm);
+            float e[4];
+            double es = 0.0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                e[j] = (tid * 4 + j < kn) ? b2s_expf(__fsub_rn(pv[j], m)) : 0.0f;
+                es += (double)e[j];
+            }
+            const float sf = (float)warp_sum(es);
+            double ps = 0.0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                e[j] = (tid * 4 + j < kn) ? __fdiv_rn(e[j], sf) : 0.0f;
+                ps += (double)e[j];
+            }
+            const double incl = warp_incl_scan(ps);
+            const double total = __shfl_sync(0xffffffffu, incl, 31);
+            const float target = __fmul_rn(u, (float)total);
+            double acc = incl - ps;
+            int first = 0x7fffffff;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc += (double)e[j];
+                if (first == 0x7fffffff && tid * 4 + j < kn && (float)acc > target) first = tid * 4 + j;
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+            if (tid == 0) *sc.kn = first;
+        }
+        __syncthreads();
+        const int best = *sc.kn;
+        return best == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)si[best];
+    }
     float lm = __int_as_float(0xff800000);
     for (int i = tid; i < kn; i += NT) lm = fmaxf(lm, sv[i]);
     const float m = block_max(lm, sc.red_f);

@@ -1,22 +1,27 @@
 // B200 (sm_100a) token-sampling kernels for MiniCPM-o 4.5 and their C-ABI launchers.
 //
-// One thread-block cluster of C CTAs owns one logits row; CTA c stages the contiguous slice
-// [c*per, min(V, (c+1)*per)) of the row into shared memory with 1-D bulk copies (cp.async.bulk, no
-// multicast) and everything after that reads shared memory only:
+// One CTA owns one logits row (a persistent loop when the batch is larger than the grid).  The row's
+// 16-byte-aligned interior streams through a ring of shared-memory stages filled by 1-D bulk copies
+// (cp.async.bulk, no multicast, one mbarrier per stage); the ragged head / tail elements are plain loads.
+// When the interior fits the ring the row stays resident and later passes read shared memory; otherwise
+// later passes re-read global memory (the row is hot in L2).  Everything else the row needs -- parameters,
+// the RNG inputs, the history ids, the penalty table and the raw values of the history ids -- is fetched
+// while the stream is in flight.
 //
-//   history ids -> per-slice hash (id -> count) -> penalised values of those ids, slots set to -inf
-//   [hf rows with a filter] full-row logsumexp (cluster max, cluster sum)
-//   candidate path: k-th largest of the 512 per-thread slice maxima is a lower bound of the row's k-th
-//       largest non-history value; raw values above it (plus history ids above its image) are the
-//       candidates; each CTA keeps those >= its local k-th; the leader CTA merges the lists over
-//       DSMEM, takes the top-k values, the top-p cut, the value threshold, and draws from the kept set
-//       in vocabulary order
-//   exact path (top_k > 128, candidate overflow, frame-0 hf rows, draw()): cluster-wide radix select
-//       of the k-th key, sorted top-k values, top-p, then a distributed draw (cluster max, cluster sum,
-//       per-CTA mass and an ordered scan for the first cumulative mass above u * total)
+//   prologue: history ids -> bitmap + hash (id -> count) -> exact processed value of every history id
+//   stream:   each thread keeps its 4 largest non-history raw values (and their ids)
+//   candidate path (top_k <= 128): two rounds of a 1024-bucket histogram over the keys of the offered
+//       values give T <= the k-th largest offered value; every non-history element >= T (the offered
+//       ones, plus a rescan by threads whose 4th value clears T) and every history id whose processed
+//       value clears f(T) are the candidates; their top-k values, the top-p cut (one warp), the value
+//       threshold and the draw in vocabulary order (one warp) finish the row
+//   exact path (top_k > 128 or too many candidates): radix select of the k-th processed key over the row,
+//       sorted top-k values, top-p, and an ordered scan of the kept mass; frame-0 hf rows and draw() go
+//       straight to the ordered scan over the whole row
 //
-// Selection is done on raw values: for ids outside the history the processed value is fl(x / T),
-// monotone in x, so the order and the k-th element carry over; history ids are processed exactly.
+// Selection runs on raw values: for ids outside the history the processed value is fl(x / T), monotone in
+// x, so the order and the k-th element carry over; history ids are processed exactly.  No block in this
+// file waits on another block.
 #include "b2s_device.cuh"
 #include "b2s_list.cuh"
 
@@ -32,8 +37,13 @@ namespace cg = cooperative_groups;
 
 namespace b2s {
 
-constexpr int KFAST = KLIST;  // largest top_k served by the candidate path
-constexpr int CAP = 1024;   // candidate slots per CTA
+constexpr int KFAST = KLIST;     // largest top_k served by the candidate path
+constexpr int CHUNK = 32768;     // bytes per ring stage
+constexpr int VPC = CHUNK / 16;  // 16-byte vectors per stage
+constexpr int MAXSTAGE = 8;
+constexpr int NBUCKET = 1024;    // buckets per threshold round
+constexpr int NBH_BITS = 8, NBH = 1 << NBH_BITS;  // candidate histogram buckets during the stream
+constexpr int HPT = 4;           // history positions per thread gathered during the stream
 constexpr int MODE_FILTER = 0, MODE_FULL = 1, MODE_FORCED = 2, MODE_SKIP = 3, MODE_FAIL = 4;
 constexpr int64_t PAD = -1;
 constexpr uint32_t HT_EMPTY = 0xFFFFFFFFu;
@@ -73,74 +83,87 @@ struct Params {
     int32_t* cout_i;
     int32_t* cout_n;
     int ccap;
-    int64_t id_off;  // global id of this row slice's column 0 (history ids are global)
-    // launch geometry and shared-memory layout (bytes)
-    int C, per, lcap, mcap, kbuf, candcap;
-    uint32_t ht_slots;
-    uint32_t off_slice, off_ht, off_htv, off_cand, off_candi, off_list, off_listi, off_vals, off_hist, off_ctl;
+    int64_t id_off;  // global id of column 0 of these rows (history ids are global)
+    // geometry and shared-memory layout (bytes)
+    int nstage, lcap, kbuf, nvals;
+    uint32_t ht_slots, bitwords;
+    uint32_t off_ctl, off_ring, off_bits, off_ht, off_htv, off_hstage, off_atab, off_cand, off_candi, off_lst,
+        off_vals, off_hist, off_hraw;
     uint32_t smem_total;
 };
 
 struct Ctl {
-    uint64_t bar;
-    int cand_n, list_n, overflow, err, gather_n, kn;
+    uint64_t bar[MAXSTAGE];
+    int cand_n, err, gather_n, kn;
     uint32_t rctl[2];
-    uint32_t prefix;
-    int krem;
-    float thr, lse;
-    float xmax1, xmax2;
-    double xsum1, xsum2, xq;
-    int xfirst;
-    int pad_;
+    uint32_t klo, kcnt;
+    float thr;
+    float u;
+    uint32_t consumed[MAXSTAGE];  // warps done with a stage (mod NWARP: the last one refills it)
+    uint32_t tau_key;             // okey of the stream threshold (raised with atomicMax)
+    int ref_n;                    // candidates counted at the last threshold raise
     double red_d[NWARP + 1];
     float red_f[NWARP + 1];
     int red_i[NWARP + 1];
+    uint32_t red_u[2 * NWARP + 2];
 };
 
 template <typename E>
 struct Elem;
 template <>
 struct Elem<float> {
-    static constexpr int SZ = 4;
-    static __device__ __forceinline__ float ld(const unsigned char* s, uint32_t off) {
-        return *reinterpret_cast<const float*>(s + off);
-    }
-    static __device__ __forceinline__ void st_ninf(unsigned char* s, uint32_t off) {
-        *reinterpret_cast<uint32_t*>(s + off) = 0xff800000u;
-    }
+    static constexpr int SZ = 4, EPV = 4;
     static __device__ __forceinline__ float gld(const void* base, int64_t i) {
         return __ldg(reinterpret_cast<const float*>(base) + i);
     }
-    // max of the 4 values of a 16-byte vector
+    static __device__ __forceinline__ float sld(const unsigned char* s) { return *reinterpret_cast<const float*>(s); }
     static __device__ __forceinline__ float vmax(uint4 q) {
         return fmaxf(fmaxf(__uint_as_float(q.x), __uint_as_float(q.y)), fmaxf(__uint_as_float(q.z), __uint_as_float(q.w)));
     }
     static __device__ __forceinline__ float at(uint4 q, int j) {
-        uint32_t w = j == 0 ? q.x : j == 1 ? q.y : j == 2 ? q.z : q.w;
+        const uint32_t w = j == 0 ? q.x : j == 1 ? q.y : j == 2 ? q.z : q.w;
         return __uint_as_float(w);
+    }
+    static constexpr uint32_t NEG = 0xff800000u;  // -inf in every element of a word
+    static __device__ __forceinline__ void st_ninf(unsigned char* s) { *reinterpret_cast<uint32_t*>(s) = NEG; }
+    static __device__ __forceinline__ float vmax4(const uint4* q) {
+        return fmaxf(fmaxf(vmax(q[0]), vmax(q[1])), fmaxf(vmax(q[2]), vmax(q[3])));
     }
 };
 template <>
 struct Elem<__nv_bfloat16> {
-    static constexpr int SZ = 2;
-    static __device__ __forceinline__ float ld(const unsigned char* s, uint32_t off) {
-        return bf16_bits_to_f(*reinterpret_cast<const uint16_t*>(s + off));
-    }
-    static __device__ __forceinline__ void st_ninf(unsigned char* s, uint32_t off) {
-        *reinterpret_cast<uint16_t*>(s + off) = (uint16_t)0xff80u;
-    }
+    static constexpr int SZ = 2, EPV = 8;
     static __device__ __forceinline__ float gld(const void* base, int64_t i) {
         return bf16_bits_to_f(__ldg(reinterpret_cast<const unsigned short*>(base) + i));
     }
+    static __device__ __forceinline__ float sld(const unsigned char* s) {
+        return bf16_bits_to_f(*reinterpret_cast<const uint16_t*>(s));
+    }
     static __device__ __forceinline__ float vmax(uint4 q) {
-        __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&q.x), b = *reinterpret_cast<__nv_bfloat162*>(&q.y);
-        __nv_bfloat162 c = *reinterpret_cast<__nv_bfloat162*>(&q.z), d = *reinterpret_cast<__nv_bfloat162*>(&q.w);
-        __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
+        const __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&q.x), b = *reinterpret_cast<__nv_bfloat162*>(&q.y);
+        const __nv_bfloat162 c = *reinterpret_cast<__nv_bfloat162*>(&q.z), d = *reinterpret_cast<__nv_bfloat162*>(&q.w);
+        const __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
         return fmaxf(__low2float(m), __high2float(m));
     }
     static __device__ __forceinline__ float at(uint4 q, int j) {
-        uint32_t w = (j >> 1) == 0 ? q.x : (j >> 1) == 1 ? q.y : (j >> 1) == 2 ? q.z : q.w;
+        const uint32_t w = (j >> 1) == 0 ? q.x : (j >> 1) == 1 ? q.y : (j >> 1) == 2 ? q.z : q.w;
         return __uint_as_float((j & 1) ? (w & 0xffff0000u) : (w << 16));
+    }
+    static constexpr uint32_t NEG = 0xff80ff80u;
+    static __device__ __forceinline__ void st_ninf(unsigned char* s) { *reinterpret_cast<uint16_t*>(s) = (uint16_t)0xff80u; }
+    // max of 4 x 8 bf16 values in packed bf16x2 arithmetic
+    static __device__ __forceinline__ float vmax4(const uint4* q) {
+        __nv_bfloat162 m[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&q[t].x);
+            const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&q[t].y);
+            const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&q[t].z);
+            const __nv_bfloat162 d = *reinterpret_cast<const __nv_bfloat162*>(&q[t].w);
+            m[t] = __hmax2(__hmax2(a, b), __hmax2(c, d));
+        }
+        const __nv_bfloat162 r = __hmax2(__hmax2(m[0], m[1]), __hmax2(m[2], m[3]));
+        return fmaxf(__low2float(r), __high2float(r));
     }
 };
 
@@ -148,731 +171,944 @@ __device__ __forceinline__ void set_status(const Params& p, uint32_t bits) {
     if (p.status) atomicOr(p.status, bits);
 }
 
-// Per-row view of the shared-memory slice and the history hash.
-template <typename E>
-struct Row {
-    unsigned char* slice;  // 16-byte aligned start = floor16(address of element lo)
-    uint32_t head;         // byte offset of element lo inside the slice buffer
-    int lo, hi;            // element range of this CTA
-    uint32_t* ht;          // packed (id - lo) << 14 | count
-    float* htv;            // processed value of each hashed id
-    uint32_t slots;
-    int nvec;              // 16-byte vectors covering [lo, hi)
-    float T;
-    bool identity;
-
-    __device__ __forceinline__ uint32_t off(int i) const { return head + (uint32_t)(i - lo) * Elem<E>::SZ; }
-    __device__ __forceinline__ float raw(int i) const { return Elem<E>::ld(slice, off(i)); }
-    __device__ __forceinline__ float f(float x) const { return identity ? x : __fdiv_rn(x, T); }
-    // first element index covered by vector v (may be < lo for v = 0)
-    __device__ __forceinline__ int vbase(int v) const { return lo + (int)(((int)(v * 16) - (int)head) / Elem<E>::SZ); }
-    __device__ __forceinline__ uint32_t hslot(int rel) const { return ((uint32_t)rel * 2654435761u) & (slots - 1); }  // == ht_slot
-    // index of the hash slot holding id i, or -1
-    __device__ __forceinline__ int find(int i) const {
-        if (slots == 0) return -1;
-        uint32_t rel = (uint32_t)(i - lo);
-        uint32_t h = hslot((int)rel);
-        for (uint32_t probe = 0; probe < slots; ++probe) {
-            uint32_t w = ht[h];
-            if (w == HT_EMPTY) return -1;
-            if ((w >> HT_CNT_BITS) == rel) return (int)h;
-            h = (h + 1) & (slots - 1);
-        }
-        return -1;
-    }
-    // processed value of element i given its raw slice value (history ids carry their own value)
-    __device__ __forceinline__ float P(int i, float x) const {
-        if (x == f_ninf()) {
-            int s = find(i);
-            if (s >= 0) return htv[s];
-        }
-        return f(x);
-    }
-};
-
-// Open-addressing hash of (id - lo) -> occurrence count, packed as rel << 14 | count in one word.
-__device__ __forceinline__ uint32_t ht_slot(uint32_t rel, uint32_t slots) { return (rel * 2654435761u) & (slots - 1); }
-__device__ __forceinline__ void ht_insert(uint32_t* ht, uint32_t slots, uint32_t rel) {
-    uint32_t hs = ht_slot(rel, slots);
+// Open-addressing hash of id -> occurrence count, packed as id << 14 | count in one word (ids < 2^18).
+__device__ __forceinline__ uint32_t ht_slot(uint32_t id, uint32_t slots) { return (id * 2654435761u) & (slots - 1); }
+__device__ __forceinline__ void ht_insert(uint32_t* ht, uint32_t slots, uint32_t id, uint32_t add) {
+    uint32_t hs = ht_slot(id, slots);
     for (uint32_t probe = 0; probe < slots; ++probe) {
         uint32_t cur = ht[hs];
         if (cur == HT_EMPTY) {
-            cur = atomicCAS(&ht[hs], HT_EMPTY, (rel << HT_CNT_BITS) | 1u);
+            cur = atomicCAS(&ht[hs], HT_EMPTY, (id << HT_CNT_BITS) | add);
             if (cur == HT_EMPTY) return;
         }
-        if ((cur >> HT_CNT_BITS) == rel) {
-            atomicAdd(&ht[hs], 1u);
+        if ((cur >> HT_CNT_BITS) == id) {
+            if (add) atomicAdd(&ht[hs], add);
             return;
         }
         hs = (hs + 1) & (slots - 1);
     }
 }
-
-__device__ __forceinline__ float pen(float v, int n, const float* alpha) {
-    if (n <= 0) return v;
-    float a = alpha[n];
-    return v < 0.0f ? __fmul_rn(v, a) : __fdiv_rn(v, a);
+__device__ __forceinline__ int ht_find(const uint32_t* ht, uint32_t slots, uint32_t id) {
+    uint32_t h = ht_slot(id, slots);
+    for (uint32_t probe = 0; probe < slots; ++probe) {
+        const uint32_t w = ht[h];
+        if (w == HT_EMPTY) return -1;
+        if ((w >> HT_CNT_BITS) == id) return (int)h;
+        h = (h + 1) & (slots - 1);
+    }
+    return -1;
 }
 
-// The whole row program.  Every CTA of a cluster takes the same branches (they depend on row data and
-// on values exchanged through distributed shared memory), so the cluster barriers always match.
+__device__ __forceinline__ float pen_a(float v, int n, float a) {
+    if (n <= 0) return v;  // penalty**0 == 1: v * 1 == v / 1 == v
+    return v < 0.0f ? __fmul_rn(v, a) : __fdiv_rn(v, a);
+}
+__device__ __forceinline__ float pen(float v, int n, const float* alpha) { return n <= 0 ? v : pen_a(v, n, alpha[n]); }
+
+// Per-row context: where the row's elements live and how an element's processed value is obtained.
 template <typename E>
-__global__ void __launch_bounds__(NT, 2) sample_kernel(const Params p) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    cg::cluster_group cluster = cg::this_cluster();
-    const int C = p.C;
-    const int crank = (int)cluster.block_rank();
-    const int r = (int)(blockIdx.x / C);
+struct Row {
+    const unsigned char* rowp;  // element 0 in global memory
+    const uint4* gvec;          // interior vector 0 in global memory
+    const unsigned char* ring;  // stage buffers (vector v of a resident row at ring + 16 v)
+    int V, nh, nvec, e0;        // head elements [0, nh); interior vectors; first interior element e0 == nh
+    bool resident;
+    const uint32_t* bits;       // history bitmap (nullptr: no history ids)
+    const uint32_t* ht;
+    const float* htv;
+    uint32_t slots;
+    float T;
+    bool identity;
+    int censor;                 // element whose processed value is -inf regardless (omni censored EOS) or -1
+
+    __device__ __forceinline__ float f(float x) const { return identity ? x : __fdiv_rn(x, T); }
+    __device__ __forceinline__ bool hbit(int i) const { return bits && ((bits[i >> 5] >> (i & 31)) & 1u); }
+    // bits [i, i + n) of the history bitmap (n <= 8), packed from bit 0
+    __device__ __forceinline__ uint32_t hbits(int i, int n) const {
+        if (!bits) return 0;
+        const int w = i >> 5, o = i & 31;
+        uint32_t b = bits[w] >> o;
+        if (o + n > 32) b |= bits[w + 1] << (32 - o);
+        return b & ((1u << n) - 1u);
+    }
+    __device__ __forceinline__ float raw(int i) const {
+        if (resident && i >= e0 && i < e0 + nvec * Elem<E>::EPV) return Elem<E>::sld(ring + (size_t)(i - e0) * Elem<E>::SZ);
+        return Elem<E>::gld(rowp, i);
+    }
+    // processed value of element i (history ids and the censored EOS carry their own value)
+    __device__ __forceinline__ float P(int i, float x) const {
+        if (hbit(i)) return htv[ht_find(ht, slots, (uint32_t)i)];
+        return f(x);
+    }
+    __device__ __forceinline__ uint4 vec(int v) const {
+        return resident ? reinterpret_cast<const uint4*>(ring)[v] : __ldg(gvec + v);
+    }
+};
+
+// Visit every element of the row as (index, raw value): interior vectors round-robin over the threads,
+// head elements by thread 0, tail elements by thread 1.
+template <typename E, typename Fn>
+__device__ __forceinline__ void row_visit(const Row<E>& R, Fn fn) {
     const int tid = threadIdx.x;
+    constexpr int EPV = Elem<E>::EPV;
+    for (int v = tid; v < R.nvec; v += NT) {
+        const uint4 q = R.vec(v);
+        const int b = R.e0 + v * EPV;
+#pragma unroll
+        for (int j = 0; j < EPV; ++j) fn(b + j, Elem<E>::at(q, j));
+    }
+    if (tid == 0)
+        for (int i = 0; i < R.nh; ++i) fn(i, Elem<E>::gld(R.rowp, i));
+    if (tid == 1)
+        for (int i = R.e0 + R.nvec * EPV; i < R.V; ++i) fn(i, Elem<E>::gld(R.rowp, i));
+}
+
+// Ordered scan of the kept mass: every element i with keep(i, P_i) contributes p_i = fl(expf(P_i - m) / s);
+// returns the first index whose fp64 prefix of p, rounded to fp32, exceeds u * total (talker_sampler.py:
+// 168-172), or V - 1.  m = max kept P, s = fl(sum expf(P - m)).  Contiguous element ranges per thread keep
+// the prefix in index order.
+template <typename E, typename Keep>
+__device__ int64_t ordered_draw(const Row<E>& R, Keep keep, float u, Ctl* ctl) {
+    const int tid = threadIdx.x;
+    const int V = R.V;
+    const int L = (V + NT - 1) / NT;
+    const int i0 = min(V, tid * L), i1 = min(V, i0 + L);
+    float lm = f_ninf();
+    for (int i = i0; i < i1; ++i) {
+        const float P = R.P(i, R.raw(i));
+        if (keep(i, P)) lm = fmaxf(lm, P);
+    }
+    const float m = block_max(lm, ctl->red_f);
+    auto e_of = [&](int i) {
+        const float P = R.P(i, R.raw(i));
+        return keep(i, P) ? b2s_expf(__fsub_rn(P, m)) : 0.0f;
+    };
+    double es = 0.0;
+    for (int i = i0; i < i1; ++i) es += (double)e_of(i);
+    const float sf = (float)block_sum(es, ctl->red_d);
+    double ps = 0.0;
+    for (int i = i0; i < i1; ++i) ps += (double)__fdiv_rn(e_of(i), sf);
+    double total;
+    double acc = block_excl_scan(ps, ctl->red_d, &total);
+    const float target = __fmul_rn(u, (float)total);
+    int first = 0x7fffffff;
+    for (int i = i0; i < i1; ++i) {
+        const float pi = __fdiv_rn(e_of(i), sf);
+        if (pi == 0.0f) continue;
+        acc += (double)pi;
+        if ((float)acc > target) { first = i; break; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+    __syncthreads();
+    if ((tid & 31) == 0) ctl->red_i[tid >> 5] = first;
+    __syncthreads();
+    int best = 0x7fffffff;
+    for (int w = 0; w < NWARP; ++w) best = min(best, ctl->red_i[w]);
+    __syncthreads();
+    return best == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)best;
+}
+
+// Radix select over the row: the key of the k-th largest processed value (1 <= k <= V).
+template <typename E>
+__device__ uint32_t row_kth_key(const Row<E>& R, int k, uint32_t* hist, Ctl* ctl) {
+    const int tid = threadIdx.x;
+    uint32_t prefix = 0, mask = 0;
+    int krem = k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += NT) hist[i] = 0;
+        __syncthreads();
+        row_visit<E>(R, [&](int i, float x) {
+            const uint32_t kk = okey(R.P(i, x));
+            if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255u], 1u);
+        });
+        __syncthreads();
+        if (tid < 32) {
+            uint32_t c[8], s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) { c[j] = hist[255 - 8 * tid - j]; s += c[j]; }  // 8-word stride
+            uint32_t incl = s;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (tid >= o) incl += t;
+            }
+            const uint32_t excl = incl - s;
+            if (excl < (uint32_t)krem && (uint32_t)krem <= incl) {
+                uint32_t cum = excl;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (cum + c[j] >= (uint32_t)krem) {
+                        ctl->rctl[0] = (uint32_t)(255 - 8 * tid - j);
+                        ctl->rctl[1] = (uint32_t)krem - cum;
+                        break;
+                    }
+                    cum += c[j];
+                }
+            }
+        }
+        __syncthreads();
+        prefix |= ctl->rctl[0] << shift;
+        mask |= 0xFFu << shift;
+        krem = (int)ctl->rctl[1];
+        __syncthreads();
+    }
+    return prefix;
+}
+
+// T such that at least k of the n keys produced by key(i) are >= T, found with two rounds of a 1024-bucket
+// histogram over [min key, max key]: T is the lower edge of the bucket holding the k-th largest key (the
+// key itself when the second round resolves it).  Returns 0 when n < k.  Every thread calls it.
+template <typename KeyFn>
+__device__ uint32_t kth_key_bucket(int n, int k, KeyFn key, uint32_t* hist, Ctl* ctl) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    uint32_t kmn = 0xFFFFFFFFu, kmx = 0;
+    for (int i = tid; i < n; i += NT) {
+        const uint32_t kk = key(i);
+        kmn = min(kmn, kk);
+        kmx = max(kmx, kk);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        kmn = min(kmn, __shfl_xor_sync(0xffffffffu, kmn, o));
+        kmx = max(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
+    }
+    __syncthreads();
+    if (lane == 0) {
+        ctl->red_u[2 * (tid >> 5)] = kmn;
+        ctl->red_u[2 * (tid >> 5) + 1] = kmx;
+    }
+    __syncthreads();
+    uint32_t klo = 0xFFFFFFFFu, khi = 0;
+    for (int w = 0; w < NWARP; ++w) {
+        klo = min(klo, ctl->red_u[2 * w]);
+        khi = max(khi, ctl->red_u[2 * w + 1]);
+    }
+    if (n < k) return 0u;
+    int krem = k;
+    for (int round = 0; round < 2 && khi > klo; ++round) {
+        const uint32_t range = khi - klo;
+        const int nbits = 32 - __clz(range);
+        const int sh = nbits > 10 ? nbits - 10 : 0;
+        for (int b = tid; b < NBUCKET; b += NT) hist[b] = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += NT) {
+            const uint32_t kk = key(i);
+            if (kk >= klo && kk <= khi) atomicAdd(&hist[(kk - klo) >> sh], 1u);
+        }
+        __syncthreads();
+        if (tid < 32) {
+            // lane l owns buckets 1023-32l .. 992-32l (descending); find the lane, then the bucket inside it
+            uint32_t sum = 0;
+#pragma unroll 8
+            for (int j = 0; j < 32; ++j) sum += hist[NBUCKET - 1 - 32 * tid - ((j + tid) & 31)];  // rotated: no bank conflicts
+            uint32_t incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (tid >= o) incl += t;
+            }
+            const uint32_t excl = incl - sum;
+            const unsigned who = __ballot_sync(0xffffffffu, excl < (uint32_t)krem && (uint32_t)krem <= incl);
+            const int L = __ffs(who) - 1;  // who != 0: krem <= the total count
+            const uint32_t base = __shfl_sync(0xffffffffu, excl, L);
+            const int b = NBUCKET - 1 - 32 * L - tid;
+            const uint32_t cb = hist[b];
+            uint32_t inc2 = cb;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xffffffffu, inc2, o);
+                if (tid >= o) inc2 += t;
+            }
+            const unsigned who2 = __ballot_sync(0xffffffffu, base + inc2 >= (uint32_t)krem);
+            if (tid == __ffs(who2) - 1) {
+                ctl->klo = klo + ((uint32_t)b << sh);
+                ctl->kcnt = (uint32_t)krem - (base + inc2 - cb);
+            }
+        }
+        __syncthreads();
+        const uint32_t nlo = ctl->klo;
+        const uint32_t span = (1u << sh) - 1u;
+        khi = min(khi, nlo + span);
+        klo = nlo;
+        krem = (int)ctl->kcnt;
+        __syncthreads();
+    }
+    return klo;
+}
+
+// The whole row program; with a grid smaller than the batch each CTA loops over rows.
+template <typename E>
+__global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tid = threadIdx.x, lane = tid & 31;
     Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
-    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + p.off_hist);
+    unsigned char* ring = smem + p.off_ring;
+    uint32_t* bits = reinterpret_cast<uint32_t*>(smem + p.off_bits);
+    uint32_t* ht = reinterpret_cast<uint32_t*>(smem + p.off_ht);
+    float* htv = reinterpret_cast<float*>(smem + p.off_htv);
+    int64_t* hstage = reinterpret_cast<int64_t*>(smem + p.off_hstage);
+    float* hraw = reinterpret_cast<float*>(smem + p.off_hraw);  // raw words of the history positions
+    float* atab = reinterpret_cast<float*>(smem + p.off_atab);
     float* cand_v = reinterpret_cast<float*>(smem + p.off_cand);
     int* cand_i = reinterpret_cast<int*>(smem + p.off_candi);
-    float* list_v = reinterpret_cast<float*>(smem + p.off_list);
-    int* list_i = reinterpret_cast<int*>(smem + p.off_listi);
+    float* kv = reinterpret_cast<float*>(smem + p.off_lst);
+    int* ki = reinterpret_cast<int*>(kv + p.lcap);
+    float* sv = kv + 2 * p.lcap;
+    int* si = reinterpret_cast<int*>(kv + 3 * p.lcap);
     float* vals = reinterpret_cast<float*>(smem + p.off_vals);
-    const bool leader = crank == 0;
+    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + p.off_hist);
+    constexpr int ES = Elem<E>::SZ, EPV = Elem<E>::EPV;
     const int V = p.V;
+    const Scr sc{hist, ctl->rctl, &ctl->gather_n, &ctl->kn, &ctl->thr, ctl->red_d, ctl->red_f, ctl->red_i};
+    uint32_t phase_bits = 0;  // parity of every stage barrier, flipped per completed fill
 
-    // ---------------- row parameters and mode
-    const int64_t step = p.steps ? p.steps[r] : 0;
-    const bool is_live = (p.active ? p.active[r] != 0 : true) && !(p.finished ? p.finished[r] != 0 : false);
-    const bool identity = p.sem == B2S_SEM_IDENTITY;
-    const bool hf = p.sem == B2S_SEM_HF;
-    const float T = p.rT ? p.rT[r] : p.T;
-    const float top_p = p.rP ? p.rP[r] : p.top_p;
-    const int top_k = p.rK ? p.rK[r] : p.top_k;
-    const bool eos_ok = !identity && p.eos >= 0 && p.eos < V;
-    const bool masked_eos = eos_ok && step < p.min_new;
-    int mode;
-    if (!p.proc && !is_live) mode = MODE_SKIP;
-    else if (identity) mode = MODE_FULL;
-    else if (step >= p.max_new - 1) mode = MODE_FORCED;
-    else if (hf && step <= 0) mode = MODE_FULL;
-    else mode = MODE_FILTER;
-    int k = 0;
-    if (mode == MODE_FILTER) {
-        k = min(max(top_k, max(p.min_keep, 1)), V);
-        if (k > p.kbuf) {
-            mode = MODE_FAIL;
-            if (leader && tid == 0) set_status(p, B2S_STATUS_TOPK_LIMIT);
-        }
-    }
-    const int min_keep = p.min_keep;
-    const bool topk_only = (p.flags & B2S_FLAG_TOPK_ONLY) != 0;
-    const int lo = crank * p.per;
-    const int hi = min(V, lo + p.per);
-
-    // state epilogue shared by every mode (leader CTA only)
-    // tok_drawn == PAD marks a row that failed on the device: PAD out, state unchanged
-    auto finish_row = [&](int64_t tok_drawn) {
-        const bool adv = is_live && tok_drawn != PAD;
-        const int64_t tok = adv ? tok_drawn : PAD;
-        if (tid == 0) {
-            if (p.tokens) p.tokens[r] = tok;
-            if (p.steps_out) p.steps_out[r] = step + (adv ? 1 : 0);
-            if (p.fin_out) {
-                bool f0 = p.finished ? p.finished[r] != 0 : false;
-                p.fin_out[r] = (uint8_t)(f0 || (adv && tok == (int64_t)p.eos));
-            }
-        }
-        if (p.hist_out && p.W > 0) {
-            const int64_t* h = p.hist + (int64_t)r * p.hstride;
-            int64_t* ho = p.hist_out + (int64_t)r * p.hostride;
-            // read the whole old row before any write: history_out may alias history (W <= 16 * NT)
-            int64_t v[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                const int j = tid + q * NT;
-                if (j < p.W) v[q] = adv ? (j + 1 < p.W ? h[j + 1] : tok) : h[j];
-            }
-            __syncthreads();
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                const int j = tid + q * NT;
-                if (j < p.W) ho[j] = v[q];
-            }
-        }
-    };
-    auto write_forced = [&]() {
-        if (p.proc) {
-            float* out = p.proc + (int64_t)r * p.pstride;
-            for (int i = lo + tid; i < hi; i += NT) out[i] = (eos_ok && i == p.eos) ? 0.0f : f_ninf();
-        }
-    };
-
-    if (p.cout_n && mode != MODE_FILTER) {  // a shard row that is not sampled contributes no candidates
-        if (leader && tid == 0) p.cout_n[r] = -1;
-        return;
-    }
-    if (mode == MODE_SKIP || mode == MODE_FAIL) {
-        if (leader) finish_row(PAD);
-        return;
-    }
-    if (mode == MODE_FORCED) {
-        write_forced();
-        if (leader) finish_row(eos_ok ? (int64_t)p.eos : (int64_t)(V - 1));
-        return;
-    }
-
-    // ---------------- stage the slice (bulk copy) and hash the history ids of this slice
-    Row<E> R;
-    const int ES = Elem<E>::SZ;
-    const unsigned char* rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
-    const uintptr_t A = reinterpret_cast<uintptr_t>(rowp) + (uintptr_t)lo * ES;
-    const uintptr_t B = reinterpret_cast<uintptr_t>(rowp) + (uintptr_t)hi * ES;
-    const uintptr_t Afl = A & ~(uintptr_t)15, Ace = (A + 15) & ~(uintptr_t)15, Bfl = B & ~(uintptr_t)15,
-                    Bce = (B + 15) & ~(uintptr_t)15;
-    R.slice = smem + p.off_slice;
-    R.head = (uint32_t)(A - Afl);
-    R.lo = lo;
-    R.hi = hi;
-    R.nvec = hi > lo ? (int)((Bce - Afl) / 16) : 0;
-    R.T = T;
-    R.identity = identity;
-    const bool use_hist = mode == MODE_FILTER && p.W > 0 && p.hist != nullptr;
-    R.ht = reinterpret_cast<uint32_t*>(smem + p.off_ht);
-    R.htv = reinterpret_cast<float*>(smem + p.off_htv);
-    R.slots = use_hist ? p.ht_slots : 0;
-    const bool bulk = hi > lo && Ace < Bfl;
     if (tid == 0) {
-        ctl->cand_n = 0;
-        ctl->list_n = 0;
-        ctl->overflow = 0;
-        ctl->err = 0;
-        ctl->gather_n = 0;
-        ctl->kn = 0;
-        mbar_init(&ctl->bar, 1);
+        for (int s = 0; s < p.nstage; ++s) {
+            mbar_init(&ctl->bar[s], 1);
+            ctl->consumed[s] = 0u;
+        }
         fence_mbar_init();
-        if (bulk) {
-            const uint32_t bytes = (uint32_t)(Bfl - Ace);
-            mbar_arrive_expect_tx(&ctl->bar, bytes);
-            const uint32_t chunk = 32768;
-            for (uint32_t o = 0; o < bytes; o += chunk)
-                bulk_g2s(R.slice + (Ace - Afl) + o, reinterpret_cast<const void*>(Ace + o), min(chunk, bytes - o),
-                         &ctl->bar);
-        }
-    }
-    // scalar head / tail elements (or the whole slice when it has no aligned interior)
-    if (hi > lo) {
-        const int base = lo;
-        if (!bulk) {
-            for (int i = lo + tid; i < hi; i += NT)
-                if (ES == 4) *reinterpret_cast<float*>(R.slice + R.off(i)) = Elem<E>::gld(rowp, i);
-                else *reinterpret_cast<uint16_t*>(R.slice + R.off(i)) = __ldg(reinterpret_cast<const unsigned short*>(rowp) + i);
-        } else {
-            const int nh = (int)((Ace - A) / ES), nt = (int)((B - Bfl) / ES);
-            if (tid < nh) {
-                const int i = base + tid;
-                if (ES == 4) *reinterpret_cast<float*>(R.slice + R.off(i)) = Elem<E>::gld(rowp, i);
-                else *reinterpret_cast<uint16_t*>(R.slice + R.off(i)) = __ldg(reinterpret_cast<const unsigned short*>(rowp) + i);
-            } else if (tid >= 32 && tid < 32 + nt) {
-                const int i = hi - nt + (tid - 32);
-                if (ES == 4) *reinterpret_cast<float*>(R.slice + R.off(i)) = Elem<E>::gld(rowp, i);
-                else *reinterpret_cast<uint16_t*>(R.slice + R.off(i)) = __ldg(reinterpret_cast<const unsigned short*>(rowp) + i);
-            }
-        }
-    }
-    if (use_hist) {
-        for (uint32_t s = tid; s < R.slots; s += NT) R.ht[s] = HT_EMPTY;
-    }
-    __syncthreads();
-    if (use_hist) {
-        const int64_t* h = p.hist + (int64_t)r * p.hstride;
-        for (int j = tid; j < p.W; j += NT) {
-            if (h[j] < 0) continue;  // PAD
-            const int64_t id = h[j] - p.id_off;
-            if (id < 0 || id >= V) {
-                // a shard ignores ids of the other shards; an unsharded row flags ids >= vocab
-                if (!p.cout_n && crank == 0) set_status(p, B2S_STATUS_HISTORY_RANGE);
-                continue;
-            }
-            if (id < lo || id >= hi) continue;
-            ht_insert(R.ht, R.slots, (uint32_t)(id - lo));
-        }
-    }
-    bool ok = true;
-    if (bulk) ok = mbar_wait_bounded(&ctl->bar, 0);
-    if (!ok) {
-        ctl->err = 1;  // benign race: every failing thread writes 1
-        set_status(p, B2S_STATUS_WAIT_TIMEOUT);
-        mbar_wait_bounded(&ctl->bar, 0);  // give in-flight copies a second bounded chance before reuse
     }
     __syncthreads();
 
-    // ---------------- history ids: exact processed values, then -inf in the slice
-    const float* alpha = p.alpha ? p.alpha + (int64_t)r * p.alpha_stride : nullptr;
-    if (use_hist) {
-        for (uint32_t s = tid; s < R.slots; s += NT) {
-            uint32_t w = R.ht[s];
-            if (w == HT_EMPTY) continue;
-            const int i = lo + (int)(w >> HT_CNT_BITS);
+    // 16-byte-aligned interior of row r: head elements before it, vectors in it
+    auto geometry = [&](int r, int& nh, int& nvec, const uint4*& gvec) {
+        const unsigned char* rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
+        const uintptr_t a = reinterpret_cast<uintptr_t>(rowp);
+        const uintptr_t b = a + (uintptr_t)V * ES;
+        const uintptr_t ace = (a + 15) & ~(uintptr_t)15, bfl = b & ~(uintptr_t)15;
+        if (ace < bfl) {
+            nh = (int)((ace - a) / ES);
+            nvec = (int)((bfl - ace) / 16);
+        } else {
+            nh = V;
+            nvec = 0;
+        }
+        gvec = reinterpret_cast<const uint4*>(ace);
+    };
+    // fill the stage of chunk c of a row (one thread)
+    auto issue_chunk = [&](const uint4* gvec, int nvec, int c) {
+        const int s = c % p.nstage;
+        const uint32_t bytes = (uint32_t)min(VPC, nvec - c * VPC) * 16u;
+        mbar_arrive_expect_tx(&ctl->bar[s], bytes);
+        bulk_g2s(ring + (size_t)s * CHUNK, gvec + (size_t)c * VPC, bytes, &ctl->bar[s]);
+    };
+    bool prefetched = false;  // this row's first stages were issued while the previous row finished
+
+    for (int r = blockIdx.x; r < p.rows; r += gridDim.x) {
+        // ---------------- geometry; issue the first ring fills before anything else
+        Row<E> R;
+        R.rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
+        R.V = V;
+        geometry(r, R.nh, R.nvec, R.gvec);
+        R.e0 = R.nh;
+        const int nchunks = (R.nvec + VPC - 1) / VPC;
+        R.resident = nchunks <= p.nstage;
+        R.ring = ring;
+        auto issue = [&](int c) { issue_chunk(R.gvec, R.nvec, c); };
+        if (tid == 0) {
+            ctl->err = 0;
+            if (!prefetched)
+                for (int c = 0; c < min(nchunks, p.nstage); ++c) issue(c);
+        }
+
+        // ---------------- row parameters and mode (global loads overlap the stream)
+        const int64_t step = p.steps ? p.steps[r] : 0;
+        const bool is_live = (p.active ? p.active[r] != 0 : true) && !(p.finished ? p.finished[r] != 0 : false);
+        const bool identity = p.sem == B2S_SEM_IDENTITY;
+        const bool hf = p.sem == B2S_SEM_HF;
+        const float T = p.rT ? p.rT[r] : p.T;
+        const float top_p = p.rP ? p.rP[r] : p.top_p;
+        const int top_k = p.rK ? p.rK[r] : p.top_k;
+        const bool eos_ok = !identity && p.eos >= 0 && p.eos < V;
+        const bool masked_eos = eos_ok && step < p.min_new;
+        int mode;
+        if (!p.proc && !p.cout_n && !is_live) mode = MODE_SKIP;
+        else if (identity) mode = MODE_FULL;
+        else if (step >= p.max_new - 1) mode = MODE_FORCED;
+        else if (hf && step <= 0) mode = MODE_FULL;
+        else mode = MODE_FILTER;
+        int k = 0;
+        if (mode == MODE_FILTER) {
+            k = min(max(top_k, max(p.min_keep, 1)), V);
+            if (k > p.kbuf) {
+                mode = MODE_FAIL;
+                if (tid == 0) set_status(p, B2S_STATUS_TOPK_LIMIT);
+            }
+        }
+        if (p.cout_n && mode != MODE_FILTER) mode = MODE_FAIL;
+        const bool topk_only = (p.flags & B2S_FLAG_TOPK_ONLY) != 0;
+        if (tid == 32) {  // one thread: the row's uniform (read after the next barrier)
+            ctl->u = (p.rng == B2S_RNG_UNIFORM || !p.seeds) ? (p.uvals ? p.uvals[r] : 0.0f)
+                     : p.rng == B2S_RNG_PHILOX ? uniform_philox(p.seeds[r], step, p.requests ? p.requests[r] : 0)
+                                               : uniform_counter(p.seeds[r], step);
+        }
+        R.T = T;
+        R.identity = identity;
+        const int64_t* hrow = p.hist ? p.hist + (int64_t)r * p.hstride : nullptr;
+        const bool pen_hist = mode == MODE_FILTER && p.W > 0 && hrow != nullptr;
+        const bool censor = mode == MODE_FILTER && !hf && masked_eos;  // omni: EOS is -inf before anything else
+        const bool use_ht = pen_hist || censor;
+        R.bits = use_ht ? bits : nullptr;
+        R.ht = ht;
+        R.htv = htv;
+        R.slots = p.ht_slots;
+        R.censor = censor ? p.eos : -1;
+
+        // ---------------- prologue: stage the history and the penalty table (asynchronous copies), hash the
+        // history ids, and fetch their raw values into registers (consumed after the stream)
+        const bool stage_hist = hrow && p.W > 0 && (pen_hist || p.hist_out);
+        if (stage_hist)
+            for (int j = tid; j < p.W; j += NT) cp_async8(&hstage[j], &hrow[j]);
+        const float* alpha = p.alpha ? p.alpha + (int64_t)r * p.alpha_stride : nullptr;
+        if (pen_hist && alpha)
+            for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], &alpha[j]);
+        if (use_ht) {
+            for (uint32_t w = tid; w < p.bitwords; w += NT) bits[w] = 0;
+            for (uint32_t s = tid; s < p.ht_slots; s += NT) ht[s] = HT_EMPTY;
+        }
+        uint32_t* hcnt = hist;  // candidate histogram during the stream (NBH buckets above tau0)
+        for (int b = tid; b < NBH; b += NT) hcnt[b] = 0;
+        if (tid == 0) {
+            ctl->cand_n = 0;
+            ctl->ref_n = 0;
+            ctl->tau_key = 0u;
+            ctl->thr = f_ninf();
+            ctl->red_u[0] = 0u;
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        // history id of position j (or -1 when it has no value here: PAD, another shard, out of range)
+        auto hist_id = [&](int j) -> int {
+            const int64_t hv = hstage[j];
+            const int64_t id = hv - p.id_off;
+            return (hv >= 0 && id >= 0 && id < V) ? (int)id : -1;
+        };
+        if (use_ht) {
+            if (pen_hist) {
+                // HB positions per thread at a time, their probes interleaved (independent shared atomics)
+                constexpr int HB = 4;
+                for (int j0 = 0; j0 < p.W; j0 += HB * NT) {
+                    int id[HB];
+                    uint32_t hs[HB];
+                    bool todo[HB];
+#pragma unroll
+                    for (int u = 0; u < HB; ++u) {
+                        const int j = j0 + u * NT + tid;
+                        id[u] = j < p.W ? hist_id(j) : -1;
+                        // a vocabulary shard ignores ids of the other shards; an unsharded row flags ids >= vocab
+                        if (j < p.W && id[u] < 0 && hstage[j] >= 0 && !p.cout_n) set_status(p, B2S_STATUS_HISTORY_RANGE);
+                        todo[u] = id[u] >= 0;
+                        hs[u] = todo[u] ? ht_slot((uint32_t)id[u], p.ht_slots) : 0u;
+                        if (todo[u]) atomicOr(&bits[id[u] >> 5], 1u << (id[u] & 31));
+                    }
+                    for (uint32_t probe = 0; probe < p.ht_slots; ++probe) {
+                        uint32_t cur[HB];
+#pragma unroll
+                        for (int u = 0; u < HB; ++u)
+                            cur[u] = todo[u] ? atomicCAS(&ht[hs[u]], HT_EMPTY, ((uint32_t)id[u] << HT_CNT_BITS) | 1u) : 0u;
+                        bool any = false;
+#pragma unroll
+                        for (int u = 0; u < HB; ++u) {
+                            if (!todo[u]) continue;
+                            if (cur[u] == HT_EMPTY) {
+                                todo[u] = false;  // new slot, count 1
+                            } else if ((cur[u] >> HT_CNT_BITS) == (uint32_t)id[u]) {
+                                atomicAdd(&ht[hs[u]], 1u);
+                                todo[u] = false;
+                            } else {
+                                hs[u] = (hs[u] + 1) & (p.ht_slots - 1);
+                                any = true;
+                            }
+                        }
+                        if (!any) break;
+                    }
+                }
+            }
+            if (censor && tid == 0) {
+                ht_insert(ht, p.ht_slots, (uint32_t)p.eos, 0u);
+                atomicOr(&bits[p.eos >> 5], 1u << (p.eos & 31));
+            }
+        }
+        __syncthreads();
+        // raw value of history position j: the aligned 4-byte word holding it, copied asynchronously into
+        // hraw[j] (positions tid + u * NT, u < HPT, one per chunk so the gathers do not queue up together)
+        const uintptr_t row_lo = reinterpret_cast<uintptr_t>(R.rowp), row_hi = row_lo + (uintptr_t)V * ES;
+        auto gather_hist = [&](int j) {
+            if (!pen_hist || j >= p.W) return;
+            const int id = hist_id(j);
+            if (id < 0) return;
+            const uintptr_t wa = (row_lo + (uintptr_t)id * ES) & ~(uintptr_t)3;
+            if (wa >= row_lo && wa + 4 <= row_hi) cp_async4(&hraw[j], reinterpret_cast<const void*>(wa));
+        };
+        // processed value of a hashed id with raw value x
+        auto hist_value = [&](uint32_t w, float x) {
+            const int id = (int)(w >> HT_CNT_BITS);
             int n = (int)(w & ((1u << HT_CNT_BITS) - 1));
-            if (n >= p.alpha_len) {
+            if (n >= p.alpha_len && n > 0) {
                 set_status(p, B2S_STATUS_COUNT_LIMIT);
                 n = p.alpha_len - 1;
             }
-            const float x = R.raw(i);
-            float P;
-            if (hf) {
-                P = pen(__fdiv_rn(x, T), n, alpha);
-            } else {
-                float z = (masked_eos && i == p.eos) ? f_ninf() : x;
-                float v = pen(z, n, alpha);
-                if (n > 0) {
-                    v = __fsub_rn(v, p.presence);
-                    v = __fsub_rn(v, __fmul_rn(p.frequency, (float)n));
-                }
-                P = __fdiv_rn(v, T);
+            const float a = n > 0 ? atab[n] : 1.0f;
+            if (hf) return pen_a(__fdiv_rn(x, T), n, a);
+            const float z = (censor && id == p.eos) ? f_ninf() : x;
+            float v = pen_a(z, n, a);
+            if (n > 0) {
+                v = __fsub_rn(v, p.presence);
+                v = __fsub_rn(v, __fmul_rn(p.frequency, (float)n));
             }
-            R.htv[s] = P;
-            Elem<E>::st_ninf(R.slice, R.off(i));
-        }
-    }
-    // omni censors EOS before everything else; hf frame-0 rows drop it from the draw
-    if (tid == 0 && masked_eos && p.eos >= lo && p.eos < hi && (!hf || mode == MODE_FULL)) {
-        if (R.find(p.eos) < 0) Elem<E>::st_ninf(R.slice, R.off(p.eos));
-    }
-    __syncthreads();
+            return __fdiv_rn(v, T);
+        };
 
-    // ---------------- per-thread maximum of the raw slice (history slots are -inf now)
-    float tmax = f_ninf();
-    for (int v = tid; v < R.nvec; v += NT) {
-        uint4 q = reinterpret_cast<const uint4*>(R.slice)[v];
-        if (v == 0 || v == R.nvec - 1) {
-            const int b = R.vbase(v);
-#pragma unroll
-            for (int j = 0; j < 16 / ES; ++j) {
-                const int i = b + j;
-                if (i >= lo && i < hi) tmax = fmaxf(tmax, Elem<E>::at(q, j));
+        // ---------------- stream.  Candidate path: every warp runs through the ring on its own; a stage is
+        // refilled by the last warp to release it.  tau (a raw value, lower bound of the row's k-th largest
+        // non-history raw value) starts from the first chunk: the minimum over warps of each warp's
+        // ceil(k / 16)-th largest per-thread maximum (16 * ceil(k / 16) >= k distinct elements clear it).
+        // Every non-history element >= tau (less a margin for collisions of fl(x / T)) goes to the candidate
+        // list and to a histogram of keys above tau0; the warp that releases a stage raises tau to the lower
+        // edge of the highest bucket with >= k candidates at or above it.
+        const bool cand_path = mode == MODE_FILTER && k <= KFAST && !(p.flags & B2S_FLAG_FORCE_GENERAL) &&
+                               T >= 1e-6f && T <= 1e6f;
+        bool ovf = !cand_path;
+        bool ok = true;
+        float tau_low = f_inf();
+        uint32_t tau_key = 0u;  // okey(tau_low)
+        uint32_t k0 = 0u;       // histogram origin (key) and scale
+        int sh = 0;
+        auto margin = [](float t) { return t - fmaxf(fabsf(t) * 9.5367431640625e-7f, 1e-30f); };
+        auto push = [&](float x, int id) {
+            const int pos = atomicAdd(&ctl->cand_n, 1);
+            if (pos < p.lcap) {
+                cand_v[pos] = x;
+                cand_i[pos] = id;
             }
-        } else {
-            tmax = fmaxf(tmax, Elem<E>::vmax(q));
-        }
-    }
-
-    // ---------------- hf rows with a filter: full-row logsumexp of the penalised values
-    float lse = 0.0f;
-    if (mode == MODE_FILTER && hf) {
-        float hm = f_ninf();
-        for (uint32_t s = tid; s < R.slots; s += NT)
-            if (R.ht[s] != HT_EMPTY) hm = fmaxf(hm, R.htv[s]);
-        float bm = block_max(fmaxf(R.f(tmax), hm), ctl->red_f);
-        if (tid == 0) ctl->xmax1 = bm;
-        cluster.sync();
-        float m = f_ninf();
-        for (int c = 0; c < C; ++c) m = fmaxf(m, cluster.map_shared_rank(ctl, c)->xmax1);
-        const float mu = (m == f_inf() || m == f_ninf()) ? 0.0f : m;
-        double s = 0.0;
-        for (int v = tid; v < R.nvec; v += NT) {
-            uint4 q = reinterpret_cast<const uint4*>(R.slice)[v];
-            const int b = R.vbase(v);
+            atomicAdd(&hcnt[min((okey(x) - k0) >> sh, (uint32_t)(NBH - 1))], 1u);
+        };
+        constexpr int ITS = VPC / NT;
+        static_assert(ITS == 4, "4 vectors per thread per chunk");
+        for (int c = 0; c < nchunks; ++c) {
+            const int s = c % p.nstage;
+            if (c < HPT) gather_hist(tid + c * NT);
+            if (!mbar_wait_bounded(&ctl->bar[s], (phase_bits >> s) & 1u)) ok = false;
+            phase_bits ^= 1u << s;
+            const uint4* st = reinterpret_cast<const uint4*>(ring + (size_t)s * CHUNK);
+            const int vn = min(VPC, R.nvec - c * VPC);
+            const int cbase = R.e0 + c * VPC * EPV;
+            uint4 q[ITS];
 #pragma unroll
-            for (int j = 0; j < 16 / ES; ++j) {
-                const int i = b + j;
-                if (i >= lo && i < hi) s += (double)b2s_expf(__fsub_rn(R.f(Elem<E>::at(q, j)), mu));
+            for (int it = 0; it < ITS; ++it) {
+                const int vl = it * NT + tid;
+                q[it] = vl < vn ? st[vl] : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
             }
-        }
-        for (uint32_t sl = tid; sl < R.slots; sl += NT)
-            if (R.ht[sl] != HT_EMPTY) s += (double)b2s_expf(__fsub_rn(R.htv[sl], mu));
-        double bs = block_sum(s, ctl->red_d);
-        if (tid == 0) ctl->xsum1 = bs;
-        cluster.sync();
-        double tot = 0.0;
-        for (int c = 0; c < C; ++c) tot += cluster.map_shared_rank(ctl, c)->xsum1;
-        lse = __fadd_rn((float)log((double)(float)tot), mu);
-    }
-
-    const float u = (p.rng == B2S_RNG_UNIFORM || !p.seeds) ? (p.uvals ? p.uvals[r] : 0.0f)
-                    : p.rng == B2S_RNG_PHILOX ? uniform_philox(p.seeds[r], step, p.requests ? p.requests[r] : 0)
-                                              : uniform_counter(p.seeds[r], step);
-    float thr = f_ninf();
-    bool exact = mode == MODE_FILTER;  // exact radix select needed (cleared when the candidate path succeeds)
-    int64_t token = V - 1;
-
-    // ---------------- candidate path
-    if (mode == MODE_FILTER && k <= KFAST && !(p.flags & B2S_FLAG_FORCE_GENERAL) &&
-        (identity || (T >= 1e-6f && T <= 1e6f))) {
-        // lower bound on the row's k-th largest non-history raw value
-        uint32_t* tkeys = reinterpret_cast<uint32_t*>(cand_v);
-        tkeys[tid] = okey(tmax);
-        __syncthreads();
-        const float t_raw = okey_to_f(block_kth_largest(NT, k, [&](int i) { return tkeys[i]; }, hist, ctl->rctl));
-        const bool usable = t_raw != f_ninf() && t_raw == t_raw && R.f(t_raw) != f_inf();
-        if (usable) {
-            const float t_low = t_raw - fmaxf(fabsf(t_raw) * 9.5367431640625e-7f, 1e-30f);
-            const float p_low = R.f(t_low);
-            for (int v = tid; v < R.nvec; v += NT) {
-                uint4 q = reinterpret_cast<const uint4*>(R.slice)[v];
-                if (Elem<E>::vmax(q) < t_low) continue;
-                const int b = R.vbase(v);
+            if (c == 0) {
+                if (cand_path) {
+                    // per-thread maximum over the non-history elements of this chunk
+                    float vm0 = f_ninf();
 #pragma unroll
-                for (int j = 0; j < 16 / ES; ++j) {
-                    const int i = b + j;
-                    const float x = Elem<E>::at(q, j);
-                    if (i >= lo && i < hi && x >= t_low) {
-                        int pos = atomicAdd(&ctl->cand_n, 1);
-                        if (pos < p.candcap) { cand_v[pos] = R.f(x); cand_i[pos] = i; }
+                    for (int it = 0; it < ITS; ++it) {
+                        const int vl = it * NT + tid;
+                        if (vl >= vn) continue;
+                        const uint32_t hb = R.hbits(cbase + vl * EPV, EPV);
+                        if (hb == 0u) {
+                            vm0 = fmaxf(vm0, Elem<E>::vmax(q[it]));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < EPV; ++j)
+                                if (!((hb >> j) & 1u)) vm0 = fmaxf(vm0, Elem<E>::at(q[it], j));
+                        }
+                    }
+                    // the warp's jw largest per-thread maxima (distinct lanes): take the maximum out jw times
+                    const int jw = (k + NWARP - 1) / NWARP;
+                    float v = vm0;
+                    for (int t = 0; t < jw; ++t) {
+                        const float mj = warp_max(v);
+                        const unsigned who = __ballot_sync(0xffffffffu, v == mj);
+                        if (who && lane == __ffs(who) - 1) v = f_ninf();
+                        if (lane == 0) kv[(tid >> 5) * jw + t] = mj;
                     }
                 }
-            }
-            for (uint32_t s = tid; s < R.slots; s += NT) {
-                uint32_t w = R.ht[s];
-                if (w != HT_EMPTY && R.htv[s] >= p_low) {
-                    int pos = atomicAdd(&ctl->cand_n, 1);
-                    if (pos < p.candcap) { cand_v[pos] = R.htv[s]; cand_i[pos] = lo + (int)(w >> HT_CNT_BITS); }
+                __syncthreads();
+                if (cand_path) {
+                    // tau0 = the k-th largest of the gathered values (each one a distinct element)
+                    const int ng = NWARP * ((k + NWARP - 1) / NWARP);
+                    if (tid < ng) {
+                        const float x = kv[tid];
+                        int gt = 0, eq = 0;
+                        for (int j = 0; j < ng; ++j) {
+                            const float y = kv[j];
+                            gt += y > x;
+                            eq += y == x;
+                        }
+                        if (x > f_ninf() && gt < k && k <= gt + eq) ctl->thr = x;
+                        if (gt == 0 && x == x) ctl->red_u[0] = okey(x);
+                    }
                 }
-            }
-        }
-        __syncthreads();
-        const int nc = ctl->cand_n;
-        bool ovf = !usable || nc > p.candcap;
-        if (!ovf) {
-            uint32_t kth = 0;
-            if (nc >= k) kth = block_kth_largest(nc, k, [&](int i) { return okey(cand_v[i]); }, hist, ctl->rctl);
-            for (int i = tid; i < nc; i += NT) {
-                if (okey(cand_v[i]) >= kth) {
-                    int pos = atomicAdd(&ctl->list_n, 1);
-                    if (pos < p.lcap) { list_v[pos] = cand_v[i]; list_i[pos] = cand_i[i]; }
-                }
-            }
-            __syncthreads();
-            if (ctl->list_n > p.lcap) ovf = true;
-        }
-        if (tid == 0) ctl->overflow = ovf ? 1 : 0;
-        cluster.sync();  // lists published
-        bool any_ovf = false, any_err = false;
-        for (int c = 0; c < C; ++c) {
-            Ctl* rc = cluster.map_shared_rank(ctl, c);
-            any_ovf |= rc->overflow != 0;
-            any_err |= rc->err != 0;
-        }
-        int nm = 0;
-        if (!any_ovf && leader) {
-            // merge every CTA's list into the candidate buffer (no longer needed by this CTA)
-            for (int c = 0; c < C; ++c) {
-                Ctl* rc = cluster.map_shared_rank(ctl, c);
-                const int n = rc->list_n;
-                const float* lv = cluster.map_shared_rank(list_v, c);
-                const int* li = cluster.map_shared_rank(list_i, c);
-                for (int i = tid; i < n; i += NT) { cand_v[nm + i] = lv[i]; cand_i[nm + i] = li[i]; }
-                nm += n;
-            }
-        }
-        cluster.sync();  // lists consumed: non-leader shared memory may be reused from here on
-        if (!any_ovf) {
-            exact = false;
-            if (leader) {
-                const Scr sc{hist, ctl->rctl, &ctl->gather_n, &ctl->kn, &ctl->thr, ctl->red_d, ctl->red_f, ctl->red_i};
-                if (p.cout_n) {
-                    // vocabulary shard: hand out every merged item >= this shard's k-th value
-                    const uint32_t kthg =
-                        block_kth_largest(nm, k, [&](int i) { return okey(cand_v[i]); }, hist, ctl->rctl);
-                    if (tid == 0) ctl->kn = 0;
-                    __syncthreads();
-                    for (int i = tid; i < nm; i += NT) {
-                        if (okey(cand_v[i]) >= kthg) {
-                            const int pos = atomicAdd(&ctl->kn, 1);
-                            if (pos < p.ccap) {
-                                p.cout_v[(int64_t)r * p.ccap + pos] = cand_v[i];
-                                p.cout_i[(int64_t)r * p.ccap + pos] = (int32_t)(cand_i[i] + p.id_off);
+                __syncthreads();
+                if (cand_path) {
+                    const float t0 = ctl->thr;
+                    const uint32_t kmax = ctl->red_u[0];
+                    if (!(t0 > f_ninf()) || t0 == f_inf() || R.f(t0) == f_inf()) {
+                        ovf = true;
+                    } else {
+                        tau_low = margin(t0);
+                        tau_key = okey(tau_low);
+                        k0 = tau_key;
+                        const uint32_t span = kmax > k0 ? kmax - k0 : 0u;
+                        const int nb = 32 - __clz(span);
+                        sh = nb > NBH_BITS - 2 ? nb - (NBH_BITS - 2) : 0;  // tau0 .. max0 spans a quarter
+                        // the ragged head (thread 0) and tail (thread 1) of the row
+                        if (tid < 2) {
+                            const int a0 = tid == 0 ? 0 : R.e0 + R.nvec * EPV, a1 = tid == 0 ? R.nh : V;
+                            for (int i = a0; i < a1; ++i) {
+                                const float x = Elem<E>::gld(R.rowp, i);
+                                if (x >= tau_low && !R.hbit(i)) push(x, i);
                             }
                         }
                     }
-                    __syncthreads();
-                    if (tid == 0) p.cout_n[r] = any_err ? -1 : ctl->kn;
-                } else {
-                    thr = list_threshold(cand_v, nm, k, hf, lse, top_p, min_keep, topk_only, vals, sc);
-                    token = list_draw(cand_v, cand_i, nm, thr, masked_eos ? p.eos : -1, u, V, cand_v + p.mcap,
-                                      cand_i + p.mcap, list_v, list_i, sc);
-                    if (any_err) token = PAD;
-                    if (p.proc && tid == 0)
-                        for (int c = 1; c < C; ++c) cluster.map_shared_rank(ctl, c)->thr = thr;
+                }
+            } else if (!ovf) {
+                const uint32_t tk = *reinterpret_cast<volatile uint32_t*>(&ctl->tau_key);
+                if (tk > tau_key) {
+                    tau_key = tk;
+                    tau_low = okey_to_f(tk);
                 }
             }
-            if (p.proc) {
-                cluster.sync();  // threshold broadcast
-                thr = ctl->thr;
-            }
-        }
-    }
-
-    // ---------------- exact path: cluster-wide radix select of the k-th processed value
-    if (exact) {
-        for (int shift = 24; shift >= 0; shift -= 8) {
-            const uint32_t mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
-            const uint32_t prefix = shift == 24 ? 0u : ctl->prefix;
-            for (int i = tid; i < 256; i += NT) hist[i] = 0;
-            __syncthreads();
-            auto count = [&](float P) {
-                const uint32_t kk = okey(P);
-                if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255u], 1u);
-            };
-            for (int v = tid; v < R.nvec; v += NT) {
-                uint4 q = reinterpret_cast<const uint4*>(R.slice)[v];
-                const int b = R.vbase(v);
+            if (!ovf && Elem<E>::vmax4(q) >= tau_low) {
+                // rare: this thread holds candidates (history ids excluded through the bitmap)
 #pragma unroll
-                for (int j = 0; j < 16 / ES; ++j) {
-                    const int i = b + j;
-                    if (i < lo || i >= hi) continue;
-                    const float x = Elem<E>::at(q, j);
-                    if (x == f_ninf() && R.find(i) >= 0) continue;  // history id: counted from the hash
-                    count(R.f(x));
+                for (int it = 0; it < ITS; ++it) {
+                    if (Elem<E>::vmax(q[it]) >= tau_low) {
+                        const int b = cbase + (it * NT + tid) * EPV;
+                        const uint32_t hb = R.hbits(b, EPV);
+#pragma unroll
+                        for (int j = 0; j < EPV; ++j) {
+                            const float x = Elem<E>::at(q[it], j);
+                            if (x >= tau_low && !((hb >> j) & 1u)) push(x, b + j);
+                        }
+                    }
                 }
             }
-            for (uint32_t s = tid; s < R.slots; s += NT)
-                if (R.ht[s] != HT_EMPTY) count(R.htv[s]);
-            cluster.sync();  // every CTA's histogram is complete
-            if (leader && tid < 32) {
-                const int krem = shift == 24 ? k : ctl->krem;
-                uint32_t c8[8];
-                uint32_t s = 0;
+            // release the stage; the last warp refills it and raises tau
+            __syncwarp();
+            uint32_t last = 0u;
+            if (lane == 0) {
+                __threadfence_block();
+                last = (atomicAdd(&ctl->consumed[s], 1u) % (uint32_t)NWARP) == (uint32_t)(NWARP - 1);
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                __threadfence_block();
+                if (lane == 0 && !R.resident && c + p.nstage < nchunks) issue(c + p.nstage);
+            }
+            if (last && !ovf && c + 1 < nchunks) {
+                const int nn = *reinterpret_cast<volatile int*>(&ctl->cand_n);
+                if (nn == *reinterpret_cast<volatile int*>(&ctl->ref_n)) last = 0u;  // nothing new since the last one
+                __syncwarp();
+                if (lane == 0 && last) ctl->ref_n = nn;
+            }
+            if (last && !ovf && c + 1 < nchunks) {
+                // lane l sums buckets 8l .. 8l + 7; suffix sums over lanes; highest bucket with >= k at or above
+                uint32_t cb[NBH / 32];
+                uint32_t sum = 0;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    uint32_t t = 0;
-                    for (int c = 0; c < C; ++c) t += cluster.map_shared_rank(hist, c)[255 - 8 * tid - j];
-                    c8[j] = t;
-                    s += t;
+                for (int t = 0; t < NBH / 32; ++t) {
+                    cb[t] = *reinterpret_cast<volatile uint32_t*>(&hcnt[lane * (NBH / 32) + t]);
+                    sum += cb[t];
                 }
-                uint32_t incl = s;
+                uint32_t suf = sum;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
-                    uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (tid >= o) incl += t;
+                    const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
+                    if (lane + o < 32) suf += t;
                 }
-                const uint32_t excl = incl - s;
-                if (excl < (uint32_t)krem && (uint32_t)krem <= incl) {
-                    uint32_t cum = excl;
-                    for (int j = 0; j < 8; ++j) {
-                        if (cum + c8[j] >= (uint32_t)krem) {
-                            const uint32_t np = prefix | ((uint32_t)(255 - 8 * tid - j) << shift);
-                            for (int c = 0; c < C; ++c) {
-                                Ctl* rc = cluster.map_shared_rank(ctl, c);
-                                rc->prefix = np;
-                                rc->krem = krem - (int)cum;
+                const unsigned ge = __ballot_sync(0xffffffffu, suf >= (uint32_t)k);
+                if (ge) {
+                    const int L = 31 - __clz(ge);
+                    if (lane == L) {
+                        uint32_t acc = suf - sum;  // buckets above this lane
+                        int e = lane * (NBH / 32);
+#pragma unroll
+                        for (int t = NBH / 32 - 1; t >= 0; --t) {
+                            acc += cb[t];
+                            if (acc >= (uint32_t)k) {
+                                e = lane * (NBH / 32) + t;
+                                break;
                             }
-                            break;
                         }
-                        cum += c8[j];
+                        const float te = okey_to_f(k0 + ((uint32_t)e << sh));
+                        const uint32_t nk = okey(margin(te));
+                        if (nk > tau_key) atomicMax(&ctl->tau_key, nk);
                     }
                 }
             }
-            cluster.sync();  // prefix broadcast; histograms may be cleared again
         }
-        const uint32_t kth = ctl->prefix;
-        if (p.cout_n) {
-            // vocabulary shard: every element >= the shard's k-th value, counted in the leader
-            int* lkn = &cluster.map_shared_rank(ctl, 0)->kn;
-            auto emit = [&](float P, int i) {
-                const int pos = atomicAdd(lkn, 1);
-                if (pos < p.ccap) {
-                    p.cout_v[(int64_t)r * p.ccap + pos] = P;
-                    p.cout_i[(int64_t)r * p.ccap + pos] = (int32_t)(i + p.id_off);
+        // processed values of the history ids
+        if (pen_hist) {
+            for (int u = nchunks; u < HPT; ++u) gather_hist(tid + u * NT);  // short rows
+            cp_async_wait_all();  // this thread's copies
+            for (int j = tid; j < p.W; j += NT) {
+                const int id = hist_id(j);
+                if (id < 0) continue;
+                const uintptr_t ea = row_lo + (uintptr_t)id * ES, wa = ea & ~(uintptr_t)3;
+                float x;
+                if (j < HPT * NT && wa >= row_lo && wa + 4 <= row_hi) {
+                    const uint32_t w = __float_as_uint(hraw[j]);
+                    x = ES == 4 ? __uint_as_float(w) : bf16_bits_to_f((uint16_t)(w >> (8 * (unsigned)(ea - wa))));
+                } else {
+                    x = Elem<E>::gld(R.rowp, id);
                 }
-            };
-            for (int v = tid; v < R.nvec; v += NT) {
-                uint4 q = reinterpret_cast<const uint4*>(R.slice)[v];
-                const int b = R.vbase(v);
-#pragma unroll
-                for (int j = 0; j < 16 / ES; ++j) {
-                    const int i = b + j;
-                    if (i < lo || i >= hi) continue;
-                    const float x = Elem<E>::at(q, j);
-                    if (x == f_ninf() && R.find(i) >= 0) continue;
-                    const float P = R.f(x);
-                    if (okey(P) >= kth) emit(P, i);
-                }
-            }
-            for (uint32_t s2 = tid; s2 < R.slots; s2 += NT)
-                if (R.ht[s2] != HT_EMPTY && okey(R.htv[s2]) >= kth) emit(R.htv[s2], lo + (int)(R.ht[s2] >> HT_CNT_BITS));
-            cluster.sync();  // every CTA has emitted
-            if (leader && tid == 0) {
-                bool err = false;
-                for (int c = 0; c < C; ++c) err |= cluster.map_shared_rank(ctl, c)->err != 0;
-                p.cout_n[r] = err ? -1 : ctl->kn;
-            }
-            cluster.sync();  // the leader has read every CTA's error flag
-            return;
-        }
-        // values above the k-th: gathered into the leader (fewer than k of them)
-        float* lvals = cluster.map_shared_rank(vals, 0);
-        int* lgn = &cluster.map_shared_rank(ctl, 0)->gather_n;
-        for (int v = tid; v < R.nvec; v += NT) {
-            uint4 q = reinterpret_cast<const uint4*>(R.slice)[v];
-            const int b = R.vbase(v);
-#pragma unroll
-            for (int j = 0; j < 16 / ES; ++j) {
-                const int i = b + j;
-                if (i < lo || i >= hi) continue;
-                const float x = Elem<E>::at(q, j);
-                if (x == f_ninf() && R.find(i) >= 0) continue;
-                const float P = R.f(x);
-                if (okey(P) > kth) lvals[atomicAdd(lgn, 1)] = P;
+                const int sl = ht_find(ht, p.ht_slots, (uint32_t)id);
+                htv[sl] = hist_value(ht[sl], x);  // repeated ids write the same value
             }
         }
-        for (uint32_t s = tid; s < R.slots; s += NT)
-            if (R.ht[s] != HT_EMPTY && okey(R.htv[s]) > kth) lvals[atomicAdd(lgn, 1)] = R.htv[s];
-        cluster.sync();  // gathered
-        if (leader) {
-            const int ng = ctl->gather_n;
-            // bitonic sort of vals[0 .. pow2) descending, padded with -inf
-            int n2 = 1;
-            while (n2 < ng) n2 <<= 1;
-            for (int i = ng + tid; i < n2; i += NT) vals[i] = f_ninf();
-            __syncthreads();
-            for (int size = 2; size <= n2; size <<= 1) {
-                for (int stride = size >> 1; stride > 0; stride >>= 1) {
-                    for (int i = tid; i < n2; i += NT) {
-                        const int j = i ^ stride;
-                        if (j > i) {
-                            const bool desc = (i & size) == 0;
-                            const float a = vals[i], b = vals[j];
-                            if (desc ? (a < b) : (a > b)) { vals[i] = b; vals[j] = a; }
-                        }
-                    }
-                    __syncthreads();
-                }
-            }
-            for (int i = ng + tid; i < k; i += NT) vals[i] = okey_to_f(kth);
-            __syncthreads();
-            // probabilities of the k values, ordered prefix (contiguous chunk per thread)
-            const int per_t = (k + NT - 1) / NT;
-            const int i0 = min(k, tid * per_t), i1 = min(k, i0 + per_t);
-            const float m = vals[0];
-            float sf = 1.0f;
-            if (!hf) {
-                double es = 0.0;
-                for (int i = i0; i < i1; ++i) es += (double)b2s_expf(__fsub_rn(vals[i], m));
-                sf = (float)block_sum(es, ctl->red_d);
-            }
-            auto pk = [&](int i) {
-                return hf ? b2s_expf(__fsub_rn(vals[i], lse)) : __fdiv_rn(b2s_expf(__fsub_rn(vals[i], m)), sf);
-            };
-            double ls = 0.0;
-            for (int i = i0; i < i1; ++i) ls += (double)pk(i);
-            double total;
-            double acc = block_excl_scan(ls, ctl->red_d, &total);
-            int cnt = 0;
-            for (int i = i0; i < i1; ++i) {
-                const float pi = pk(i);
-                acc += (double)pi;
-                cnt += __fsub_rn((float)acc, pi) < top_p;
-            }
-            cnt = block_sum_i(cnt, ctl->red_i);
-            const int kept = topk_only ? k : max(min(min_keep, k), min(cnt, k));
-            const float t = vals[kept - 1];
-            if (tid == 0)
-                for (int c = 0; c < C; ++c) cluster.map_shared_rank(ctl, c)->thr = t;
-        }
-        cluster.sync();  // threshold broadcast
-        thr = ctl->thr;
-    }
-
-    // hf rows with a filter: the censored EOS leaves the kept set only after the filter
-    const bool drop_eos_late = mode == MODE_FILTER && hf && masked_eos && p.eos >= lo && p.eos < hi;
-    if (drop_eos_late && (exact || p.proc)) {
-        if (tid == 0) {
-            int s = R.find(p.eos);
-            if (s >= 0) R.htv[s] = f_ninf();
-            else Elem<E>::st_ninf(R.slice, R.off(p.eos));
+        if (censor && tid == 0) htv[ht_find(ht, p.ht_slots, (uint32_t)p.eos)] = f_ninf();  // omni: EOS is -inf
+        if (!ok) {
+            ctl->err = 1;
+            set_status(p, B2S_STATUS_WAIT_TIMEOUT);
         }
         __syncthreads();
-    }
-
-    // ---------------- distributed draw over the kept set (exact path and full rows)
-    if (mode == MODE_FULL || exact) {
-        const bool full = mode == MODE_FULL;
-        auto keptP = [&](float P) { return full || P >= thr; };
-        // D1: max over the kept set
-        float lm = f_ninf();
-        for (int v = tid; v < R.nvec; v += NT) {
-            uint4 q = reinterpret_cast<const uint4*>(R.slice)[v];
-            const int b = R.vbase(v);
-#pragma unroll
-            for (int j = 0; j < 16 / ES; ++j) {
-                const int i = b + j;
-                if (i < lo || i >= hi) continue;
-                const float P = R.P(i, Elem<E>::at(q, j));
-                if (keptP(P)) lm = fmaxf(lm, P);
-            }
+        const bool row_err = ctl->err != 0;
+        if (cand_path && !ovf && ctl->cand_n > p.lcap) ovf = true;
+        // a streamed row is done with the ring (later passes read global memory): start the next row's fills
+        prefetched = !R.resident && r + (int)gridDim.x < p.rows;
+        if (prefetched && tid == 0) {
+            int nh2, nvec2;
+            const uint4* g2;
+            geometry(r + (int)gridDim.x, nh2, nvec2, g2);
+            for (int c = 0; c < min((nvec2 + VPC - 1) / VPC, p.nstage); ++c) issue_chunk(g2, nvec2, c);
         }
-        float bm = block_max(lm, ctl->red_f);
-        if (tid == 0) ctl->xmax2 = bm;
-        cluster.sync();
-        float m = f_ninf();
-        for (int c = 0; c < C; ++c) m = fmaxf(m, cluster.map_shared_rank(ctl, c)->xmax2);
-        // contiguous element range per thread (index order for the final scan)
-        const int len = hi - lo;
-        const int per_t = (len + NT - 1) / NT;
-        const int e0 = lo + min(len, tid * per_t), e1 = lo + min(len, tid * per_t + per_t);
-        auto ex = [&](int i, float& P) {
-            P = R.P(i, R.raw(i));
-            return keptP(P) ? b2s_expf(__fsub_rn(P, m)) : 0.0f;
+
+        // state epilogue (tok_drawn == PAD: the row failed on the device -> PAD out, state unchanged)
+        auto finish_row = [&](int64_t tok_drawn) {
+            const bool adv = is_live && tok_drawn != PAD;
+            const int64_t tok = adv ? tok_drawn : PAD;
+            if (tid == 0) {
+                if (p.tokens) p.tokens[r] = tok;
+                if (p.steps_out) p.steps_out[r] = step + (adv ? 1 : 0);
+                if (p.fin_out) {
+                    const bool f0 = p.finished ? p.finished[r] != 0 : false;
+                    p.fin_out[r] = (uint8_t)(f0 || (adv && tok == (int64_t)p.eos));
+                }
+            }
+            if (p.hist_out && p.W > 0) {
+                int64_t* ho = p.hist_out + (int64_t)r * p.hostride;
+                // the old row was staged before any write (history_out may alias history)
+                for (int j = tid; j < p.W; j += NT) ho[j] = adv ? (j + 1 < p.W ? hstage[j + 1] : tok) : hstage[j];
+            }
         };
-        double es = 0.0;
-        for (int i = e0; i < e1; ++i) { float P; es += (double)ex(i, P); }
-        double bs = block_sum(es, ctl->red_d);
-        if (tid == 0) ctl->xsum2 = bs;
-        cluster.sync();
-        double stot = 0.0;
-        for (int c = 0; c < C; ++c) stot += cluster.map_shared_rank(ctl, c)->xsum2;
-        const float sf = (float)stot;
-        double qs = 0.0;
-        for (int i = e0; i < e1; ++i) { float P; qs += (double)__fdiv_rn(ex(i, P), sf); }
-        double qtot;
-        double off = block_excl_scan(qs, ctl->red_d, &qtot);
-        if (tid == 0) ctl->xq = qtot;
-        cluster.sync();
-        double before = 0.0, all = 0.0;
-        for (int c = 0; c < C; ++c) {
-            const double qc = cluster.map_shared_rank(ctl, c)->xq;
-            if (c < crank) before += qc;
-            all += qc;
-        }
-        const float target = __fmul_rn(u, (float)all);
-        double acc = before + off;
-        int first = 0x7fffffff;
-        for (int i = e0; i < e1; ++i) {
-            float P;
-            const float pi = __fdiv_rn(ex(i, P), sf);
-            if (pi == 0.0f) continue;
-            acc += (double)pi;
-            if ((float)acc > target) { first = i; break; }
-        }
-        int fm = first;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) fm = min(fm, __shfl_xor_sync(0xffffffffu, fm, o));
-        __syncthreads();
-        if ((tid & 31) == 0) ctl->red_i[tid >> 5] = fm;
-        __syncthreads();
-        int best = 0x7fffffff;
-        for (int w = 0; w < NWARP; ++w) best = min(best, ctl->red_i[w]);
-        if (tid == 0) { ctl->xfirst = best; }
-        cluster.sync();
-        if (leader) {
-            int tokc = 0x7fffffff;
-            bool err = false;
-            for (int c = 0; c < C; ++c) {
-                Ctl* rc = cluster.map_shared_rank(ctl, c);
-                tokc = min(tokc, rc->xfirst);
-                err |= rc->err != 0;
-            }
-            token = tokc == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)tokc;
-            if (err) token = PAD;
-        }
-        cluster.sync();  // the leader has read every CTA's exchange slots
-    }
 
-    // ---------------- processed row
-    if (p.proc) {
-        float* out = p.proc + (int64_t)r * p.pstride;
-        const bool full = mode == MODE_FULL;
-        for (int i = lo + tid; i < hi; i += NT) {
-            const float P = R.P(i, R.raw(i));
-            out[i] = (full || P >= thr) ? P : f_ninf();
+        float thr = f_ninf();
+        int64_t token = V - 1;
+        bool exact = mode == MODE_FILTER;
+        bool full = mode == MODE_FULL;
+        float lse = 0.0f;
+        const bool wants_draw = p.tokens || p.hist_out || p.steps_out || p.fin_out;
+
+        // ---------------- candidate list: the items >= the final tau (processed), plus the history ids whose
+        // processed value clears f(tau)
+        int n = 0;
+        if (cand_path && !ovf && !row_err) {
+            const uint32_t tk = max(tau_key, ctl->tau_key);
+            const float tl = okey_to_f(tk);
+            const int n0 = ctl->cand_n;
+            if (tid == 0) ctl->kn = 0;
+            __syncthreads();
+            for (int i = tid; i < n0; i += NT) {
+                if (cand_v[i] >= tl) {
+                    const int pos = atomicAdd(&ctl->kn, 1);
+                    if (pos < p.lcap) {
+                        kv[pos] = R.f(cand_v[i]);
+                        ki[pos] = cand_i[i];
+                    }
+                }
+            }
+            if (use_ht) {
+                const float p_low = R.f(tl);
+                for (uint32_t sl = tid; sl < p.ht_slots; sl += NT) {
+                    const uint32_t w = ht[sl];
+                    if (w != HT_EMPTY && htv[sl] >= p_low) {
+                        const int pos = atomicAdd(&ctl->kn, 1);
+                        if (pos < p.lcap) {
+                            kv[pos] = htv[sl];
+                            ki[pos] = (int)(w >> HT_CNT_BITS);
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            n = ctl->kn;
+            if (n <= p.lcap)
+                for (int i = tid; i < n; i += NT) {
+                    cand_v[i] = kv[i];
+                    cand_i[i] = ki[i];
+                }
+            __syncthreads();
+            if (n > p.lcap || n < k) ovf = true;
         }
+
+        if (mode == MODE_FILTER && hf && !row_err) {
+            // full-row logsumexp of the penalised values (talker_sampler.py:112); the row maximum is a candidate
+            float lm = f_ninf();
+            if (cand_path && !ovf) {
+                for (int i = tid; i < n; i += NT) lm = fmaxf(lm, cand_v[i]);
+            } else {
+                row_visit<E>(R, [&](int i, float x) { lm = fmaxf(lm, R.P(i, x)); });
+            }
+            const float m = block_max(lm, ctl->red_f);
+            const float mu = (m == f_inf() || m == f_ninf()) ? 0.0f : m;
+            double sacc = 0.0;
+            row_visit<E>(R, [&](int i, float x) { sacc += (double)b2s_expf(__fsub_rn(R.P(i, x), mu)); });
+            lse = __fadd_rn((float)log((double)(float)block_sum(sacc, ctl->red_d)), mu);
+        }
+
+        // ---------------- candidate path: finish from the candidate list
+        if (cand_path && !ovf && !row_err) {
+            if (n > 256) {
+                // narrow to the items >= the k-th largest processed value (ties kept)
+                const uint32_t kk = kth_key_bucket(n, k, [&](int i) { return okey(cand_v[i]); }, hist, ctl);
+                if (tid == 0) ctl->kn = 0;
+                __syncthreads();
+                for (int i = tid; i < n; i += NT)
+                    if (okey(cand_v[i]) >= kk) {
+                        const int pos = atomicAdd(&ctl->kn, 1);
+                        kv[pos] = cand_v[i];
+                        ki[pos] = cand_i[i];
+                    }
+                __syncthreads();
+                n = ctl->kn;
+                for (int i = tid; i < n; i += NT) { cand_v[i] = kv[i]; cand_i[i] = ki[i]; }
+                __syncthreads();
+            }
+            exact = false;
+            if (p.cout_n) {
+                // vocabulary shard: every candidate >= this shard's k-th value
+                list_topk_values(cand_v, n, k, vals, sc);
+                const float kth = vals[k - 1];
+                if (tid == 0) ctl->kn = 0;
+                __syncthreads();
+                for (int i = tid; i < n; i += NT) {
+                    if (cand_v[i] >= kth) {
+                        const int pos = atomicAdd(&ctl->kn, 1);
+                        if (pos < p.ccap) {
+                            p.cout_v[(int64_t)r * p.ccap + pos] = cand_v[i];
+                            p.cout_i[(int64_t)r * p.ccap + pos] = (int32_t)(cand_i[i] + p.id_off);
+                        }
+                    }
+                }
+                __syncthreads();
+                if (tid == 0) p.cout_n[r] = ctl->kn;
+            } else {
+                thr = list_threshold(cand_v, n, k, hf, lse, top_p, p.min_keep, topk_only, vals, sc);
+                if (wants_draw)
+                    token = list_draw(cand_v, cand_i, n, thr, (hf && masked_eos) ? p.eos : -1, ctl->u, V, kv, ki, sv,
+                                      si, sc);
+            }
+        }
+
+        // ---------------- exact path: radix select of the k-th processed key over the row
+        if (exact && !row_err && mode == MODE_FILTER) {
+            const uint32_t kth = row_kth_key<E>(R, k, hist, ctl);
+            if (p.cout_n) {
+                if (tid == 0) ctl->kn = 0;
+                __syncthreads();
+                row_visit<E>(R, [&](int i, float x) {
+                    const float P = R.P(i, x);
+                    if (okey(P) >= kth) {
+                        const int pos = atomicAdd(&ctl->kn, 1);
+                        if (pos < p.ccap) {
+                            p.cout_v[(int64_t)r * p.ccap + pos] = P;
+                            p.cout_i[(int64_t)r * p.ccap + pos] = (int32_t)(i + p.id_off);
+                        }
+                    }
+                });
+                __syncthreads();
+                if (tid == 0) p.cout_n[r] = ctl->kn;
+            } else {
+                // values above the k-th (fewer than k), sorted, then k - count copies of the k-th
+                if (tid == 0) ctl->gather_n = 0;
+                __syncthreads();
+                row_visit<E>(R, [&](int i, float x) {
+                    const float P = R.P(i, x);
+                    if (okey(P) > kth) vals[atomicAdd(&ctl->gather_n, 1)] = P;
+                });
+                __syncthreads();
+                const int ng = ctl->gather_n;
+                int n2 = 1;
+                while (n2 < ng) n2 <<= 1;
+                for (int i = ng + tid; i < n2; i += NT) vals[i] = f_ninf();
+                __syncthreads();
+                for (int size = 2; size <= n2; size <<= 1) {
+                    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                        for (int i = tid; i < n2; i += NT) {
+                            const int j = i ^ stride;
+                            if (j > i) {
+                                const bool desc = (i & size) == 0;
+                                const float a = vals[i], b = vals[j];
+                                if (desc ? (a < b) : (a > b)) { vals[i] = b; vals[j] = a; }
+                            }
+                        }
+                        __syncthreads();
+                    }
+                }
+                for (int i = ng + tid; i < k; i += NT) vals[i] = okey_to_f(kth);
+                __syncthreads();
+                // top-p over the k values, prefix in order (contiguous chunk per thread)
+                const int per_t = (k + NT - 1) / NT;
+                const int a0 = min(k, tid * per_t), a1 = min(k, a0 + per_t);
+                const float m = vals[0];
+                float sf = 1.0f;
+                if (!hf) {
+                    double es = 0.0;
+                    for (int i = a0; i < a1; ++i) es += (double)b2s_expf(__fsub_rn(vals[i], m));
+                    sf = (float)block_sum(es, ctl->red_d);
+                }
+                auto pk = [&](int i) {
+                    return hf ? b2s_expf(__fsub_rn(vals[i], lse)) : __fdiv_rn(b2s_expf(__fsub_rn(vals[i], m)), sf);
+                };
+                double ls = 0.0;
+                for (int i = a0; i < a1; ++i) ls += (double)pk(i);
+                double total;
+                double acc = block_excl_scan(ls, ctl->red_d, &total);
+                int cnt = 0;
+                for (int i = a0; i < a1; ++i) {
+                    const float pi = pk(i);
+                    acc += (double)pi;
+                    cnt += __fsub_rn((float)acc, pi) < top_p;
+                }
+                cnt = block_sum_i(cnt, ctl->red_i);
+                const int kept = topk_only ? k : max(min(p.min_keep, k), min(cnt, k));
+                thr = vals[kept - 1];
+                __syncthreads();
+                full = true;  // draw by the ordered scan over the elements >= thr
+            }
+        }
+
+        if (mode == MODE_FORCED) token = eos_ok ? (int64_t)p.eos : (int64_t)(V - 1);
+        if (full && !row_err && wants_draw) {
+            const bool filt = mode == MODE_FILTER;
+            const int drop = (hf && masked_eos) ? p.eos : -1;
+            token = ordered_draw<E>(R, [&](int i, float P) { return i != drop && (!filt || P >= thr); }, ctl->u, ctl);
+        }
+
+        // ---------------- processed row
+        if (p.proc && !p.cout_n) {
+            float* out = p.proc + (int64_t)r * p.pstride;
+            const int drop = (hf && masked_eos) ? p.eos : -1;
+            if (mode == MODE_FORCED) {
+                for (int i = tid; i < V; i += NT) out[i] = (eos_ok && i == p.eos) ? 0.0f : f_ninf();
+            } else {
+                const bool filt = mode == MODE_FILTER;
+                row_visit<E>(R, [&](int i, float x) {
+                    const float P = R.P(i, x);
+                    out[i] = (i == drop || (filt && !(P >= thr))) ? f_ninf() : P;
+                });
+            }
+        }
+        if (p.cout_n && (mode != MODE_FILTER || row_err) && tid == 0) p.cout_n[r] = -1;
+        if (!p.cout_n) finish_row((row_err || mode == MODE_SKIP || mode == MODE_FAIL) ? PAD : token);
+        __syncthreads();  // the row's shared state is dead: the next row may reuse it
     }
-    if (leader) finish_row(token);
 }
 
 // ---------------------------------------------------------------- greedy argmax
@@ -975,7 +1211,7 @@ __global__ void __launch_bounds__(NT) penalty_kernel(const void* x, int V, int64
             if (blockIdx.x == 0 && status) atomicOr(status, B2S_STATUS_HISTORY_RANGE);
             continue;
         }
-        if (id >= lo && id < hi) ht_insert(ht, slots, (uint32_t)(id - lo));
+        if (id >= lo && id < hi) ht_insert(ht, slots, (uint32_t)(id - lo), 1u);
     }
     __syncthreads();
     const float* al = alpha + (int64_t)r * alpha_stride;
@@ -1028,16 +1264,6 @@ int sm_count() {
         if (n <= 0) n = 148;
     }
     return n;
-}
-
-// Cluster size: enough CTAs per row that each slice stays within ~80 KB (two CTAs per SM), and for
-// small batches enough CTAs to spread the rows over the SMs.
-int choose_cluster(int rows, int64_t row_bytes, int requested) {
-    if (requested) return requested;
-    int C = 1;
-    while (C < 8 && row_bytes / C > 80 * 1024) C <<= 1;
-    while (C < 8 && (int64_t)rows * C * 2 <= sm_count() && row_bytes / (C * 2) >= 8 * 1024) C <<= 1;
-    return C;
 }
 
 template <typename K>
@@ -1096,15 +1322,7 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     if (a->history_out && (a->window <= 0 ? false : a->history_out_row_stride < a->window)) return B2S_ERR_INVALID;
     if (a->processed && a->processed_row_stride < a->vocab) return B2S_ERR_INVALID;
     const int es = a->logits_dtype == B2S_DTYPE_BF16 ? 2 : 4;
-    int C = choose_cluster(a->rows, (int64_t)a->vocab * es, a->cluster);
-    if (C != 1 && C != 2 && C != 4 && C != 8) return B2S_ERR_INVALID;
-    int per = (a->vocab + C - 1) / C;
-    per = (per + 15) / 16 * 16;
-    while (C > 1 && (int64_t)per * (C - 1) >= a->vocab) {  // every CTA must own at least one element
-        C >>= 1;
-        per = ((a->vocab + C - 1) / C + 15) / 16 * 16;
-    }
-    if (per >= (1 << 18)) return B2S_ERR_UNSUPPORTED;
+    if (!identity && a->window > 0 && a->vocab > (1 << 18)) return B2S_ERR_UNSUPPORTED;  // packed hash ids
 
     Params p;
     memset(&p, 0, sizeof(p));
@@ -1154,48 +1372,61 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
         p.ccap = so->cap;
         p.id_off = so->offset;
     }
-    p.C = C;
-    p.per = per;
     int kmax = a->max_top_k > 0 ? a->max_top_k : a->top_k;
     kmax = identity ? 1 : kmax;
     kmax = kmax < a->min_keep ? a->min_keep : kmax;
     kmax = kmax > a->vocab ? a->vocab : kmax;
     kmax = kmax < 1 ? 1 : kmax;
     const int kfast = kmax < KFAST ? kmax : KFAST;
-    p.lcap = next_pow2(2 * kfast + 32);
-    if (p.lcap > 512) p.lcap = 512;
-    p.mcap = C * p.lcap;
-    p.candcap = CAP > 2 * p.mcap ? CAP : 2 * p.mcap;
-    if (p.candcap < NT) p.candcap = NT;
-    // vals: [0, KFAST) sorted top-k of the candidate path, [KFAST, 2*KFAST) its gather area; the exact path
-    // sorts up to next_pow2(kmax) values from offset 0
+    // candidates pushed during the stream: ~k from the first chunk, then ~k / (c + 1) from chunk c as the
+    // threshold rises, plus the values sharing its histogram bucket; more means heavy ties
+    p.lcap = next_pow2(8 * kfast + 256);
+    if (p.lcap > 2048) p.lcap = 2048;
     p.kbuf = kmax;
-    const int nvals = next_pow2(kmax) > 2 * KFAST ? next_pow2(kmax) : 2 * KFAST;
-    const int hist_ids = a->window < per ? a->window : per;
-    p.ht_slots = identity || a->window <= 0 ? 0u : (uint32_t)next_pow2(2 * hist_ids > 32 ? 2 * hist_ids : 32);
+    p.nvals = next_pow2(kmax) > 2 * KFAST ? next_pow2(kmax) : 2 * KFAST;
+    const bool hashed = !identity && (a->window > 0 || (a->eos >= 0 && a->eos < a->vocab));
+    const int hist_ids = (a->window < a->vocab ? a->window : a->vocab) + 1;
+    p.ht_slots = hashed ? (uint32_t)next_pow2(hist_ids + hist_ids / 4 + 1 > 32 ? hist_ids + hist_ids / 4 + 1 : 32) : 0u;
+    p.bitwords = hashed ? (uint32_t)((a->vocab + 31) / 32) : 0u;
     uint32_t off = 0;
     p.off_ctl = off;
     off = align_up(off + (uint32_t)sizeof(Ctl), 128);
-    p.off_slice = off;
-    off = align_up(off + (uint32_t)per * es + 32, 128);
+    p.off_bits = off;
+    off = align_up(off + p.bitwords * 4, 16);
     p.off_ht = off;
     off = align_up(off + p.ht_slots * 4, 16);
     p.off_htv = off;
     off = align_up(off + p.ht_slots * 4, 16);
+    p.off_hraw = off;  // the 4-byte word holding the raw value of each of the first 4 * NT history positions
+    off = align_up(off + (uint32_t)(identity ? 0 : (a->window < 4 * NT ? a->window : 4 * NT)) * 4, 16);
+    p.off_hstage = off;
+    off = align_up(off + (uint32_t)(identity ? 0 : a->window) * 8, 16);
+    p.off_atab = off;
+    off = align_up(off + (uint32_t)(identity || a->window <= 0 ? 0 : a->alpha_len) * 4, 16);
     p.off_cand = off;
-    off = align_up(off + (uint32_t)p.candcap * 4, 16);
+    off = align_up(off + (uint32_t)p.lcap * 4, 16);
     p.off_candi = off;
-    off = align_up(off + (uint32_t)p.candcap * 4, 16);
-    p.off_list = off;
-    off = align_up(off + (uint32_t)(p.lcap > p.mcap ? p.lcap : p.mcap) * 4, 16);
-    p.off_listi = off;
-    off = align_up(off + (uint32_t)(p.lcap > p.mcap ? p.lcap : p.mcap) * 4, 16);
+    off = align_up(off + (uint32_t)p.lcap * 4, 16);
+    p.off_lst = off;
+    off = align_up(off + (uint32_t)p.lcap * 16, 16);
     p.off_vals = off;
-    off = align_up(off + (uint32_t)nvals * 4, 16);
+    off = align_up(off + (uint32_t)p.nvals * 4, 16);
     p.off_hist = off;
-    off = align_up(off + 256 * 4, 16);
+    off = align_up(off + NBUCKET * 4, 16);
+    p.off_ring = off;
+    // the ring: the whole 16-byte interior when it fits (later passes then read shared memory), else a
+    // streaming ring of 4 stages
+    const uint32_t limit = 227 * 1024;
+    if (off + 2 * CHUNK > limit) return B2S_ERR_UNSUPPORTED;
+    const int max_stage_fit = (int)((limit - off) / CHUNK);
+    const int row_chunks = (int)(((int64_t)a->vocab * es + CHUNK - 1) / CHUNK);
+    int nstage;
+    if (row_chunks <= MAXSTAGE && row_chunks <= max_stage_fit) nstage = row_chunks < 1 ? 1 : row_chunks;
+    else nstage = max_stage_fit < 4 ? max_stage_fit : 4;
+    p.nstage = nstage;
+    off = align_up(off + (uint32_t)nstage * CHUNK, 16);
     p.smem_total = off;
-    if (p.smem_total > 227 * 1024) return B2S_ERR_UNSUPPORTED;
+    if (p.smem_total > limit) return B2S_ERR_UNSUPPORTED;
 
     cudaError_t e;
     void (*kern)(const Params) = a->logits_dtype == B2S_DTYPE_BF16 ? sample_kernel<__nv_bfloat16> : sample_kernel<float>;
@@ -1217,17 +1448,12 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     }
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3((unsigned)(a->rows * C), 1, 1);
+    cfg.gridDim = dim3((unsigned)(a->rows < 65535 * 16 ? a->rows : 65535 * 16), 1, 1);
     cfg.blockDim = dim3(NT, 1, 1);
     cfg.dynamicSmemBytes = p.smem_total;
     cfg.stream = (cudaStream_t)stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)C;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.attrs = nullptr;
+    cfg.numAttrs = 0;
     e = cudaLaunchKernelEx(&cfg, kern, p);
     if (e != cudaSuccess) return cuda_fail(e);
     return B2S_OK;
