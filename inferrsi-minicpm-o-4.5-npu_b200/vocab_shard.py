@@ -92,13 +92,22 @@ def sample_sharded(logits: torch.Tensor, offset: int, vocab: int, history: Optio
 
     cap = cap or default_cap(cfg)
     v, i, n = shard_candidates(logits, offset, history, steps, cfg, cap=cap, status=status)
-    mine = pack(v, i, n)
+    vv, ii, nn = exchange(v, i, n, group=group)
+    return merge_candidates(vv, ii, nn, vocab, steps, seeds, cfg, uniform_values=uniform_values, requests=requests,
+                            rng=rng, status=status)
+
+
+def exchange(values: torch.Tensor, ids: torch.Tensor, counts: torch.Tensor, *, group=None):
+    """Every shard's candidate lists on every rank: one ``all_gather_into_tensor`` of the packed buffer.
+    Returns (values [S, B, cap], ids [S, B, cap], counts [S, B]) in rank order.  Works on any backend that
+    gathers into one tensor (NCCL on the GPUs; gloo on the CPU for the host-side tests)."""
+    import torch.distributed as dist
+
+    mine = pack(values, ids, counts)
     world = dist.get_world_size(group)
     allb = torch.empty((world * mine.shape[0], mine.shape[1]), dtype=torch.int32, device=mine.device)
     dist.all_gather_into_tensor(allb, mine, group=group)
-    vv, ii, nn = unpack(allb, world, mine.shape[0], cap)
-    return merge_candidates(vv, ii, nn, vocab, steps, seeds, cfg, uniform_values=uniform_values, requests=requests,
-                            rng=rng, status=status)
+    return unpack(allb, world, mine.shape[0], values.shape[1])
 
 
 def shard_bounds(vocab: int, shards: int) -> Sequence[int]:

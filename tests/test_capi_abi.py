@@ -1,0 +1,86 @@
+"""The C-ABI boundary without a GPU: ``libb2s.so`` loads, exports every function ``include/b2s_sampler.h``
+declares, the ctypes mirror of ``b2s_sample_args`` has the C layout (checked against gcc's own offsets),
+and the calls that need no device answer.  The CUDA extension must exist: there is no CPU fallback."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "b2s_sampler.h"
+
+
+def _declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(b2s_\w+)\s*\(", text, flags=re.M)))
+
+
+def _struct_fields():
+    body = re.search(r"typedef struct b2s_sample_args \{(.*?)\} b2s_sample_args;", HEADER.read_text(), re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", re.sub(r"//[^\n]*", "", body), flags=re.S)
+    return re.findall(r"([A-Za-z_][A-Za-z0-9_]*)\s*;", body)
+
+
+def test_header_declares_the_abi():
+    names = _declared_functions()
+    assert {"b2s_sample", "b2s_argmax", "b2s_uniform", "b2s_shard_candidates", "b2s_shard_merge",
+            "b2s_repetition_penalty", "b2s_error_string", "b2s_last_cuda_error", "b2s_abi_version"} <= set(names)
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg._native.capi()
+    for name in _declared_functions():
+        assert hasattr(lib, name), name
+    # the ctypes signatures cover exactly the header's functions
+    assert sorted(pkg._native.CAPI_SIGNATURES) == _declared_functions()
+
+
+def test_host_only_calls(pkg):
+    lib = pkg._native.capi()
+    assert lib.b2s_abi_version() >= 1
+    for code in range(0, 6):
+        s = lib.b2s_error_string(code)
+        assert isinstance(s, bytes) and len(s) > 0
+    assert b"unknown" in lib.b2s_error_string(-12345).lower() or len(lib.b2s_error_string(-12345)) > 0
+
+
+def test_sample_args_layout_matches_c(pkg, tmp_path):
+    """Offsets of every field of b2s_sample_args as gcc lays them out == the ctypes mirror's."""
+    fields = _struct_fields()
+    mirror = pkg._native.SampleArgs
+    assert [f[0] for f in mirror._fields_] == fields
+    src = tmp_path / "layout.c"
+    lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void) {",
+             '  printf("size %zu\\n", sizeof(b2s_sample_args));']
+    lines += [f'  printf("{f} %zu\\n", offsetof(b2s_sample_args, {f}));' for f in fields]
+    lines += ["  return 0;", "}"]
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-x", "c", str(src), "-o", str(exe)], check=True)
+    out = dict(l.split() for l in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                 text=True).stdout.splitlines())
+    assert int(out["size"]) == ctypes.sizeof(mirror)
+    for f in fields:
+        assert int(out[f]) == getattr(mirror, f).offset, f
+
+
+def test_torch_op_library_registers_ops(pkg):
+    import torch
+
+    pkg._native.ops()
+    for op in ("sample", "sample_state_", "argmax", "uniform", "repetition_penalty", "shard_candidates",
+               "shard_merge"):
+        assert hasattr(torch.ops.minicpmo_sampler, op), op
+
+
+def test_product_path_refuses_cpu_tensors(pkg):
+    import torch
+
+    x = torch.zeros(2, 16)
+    with pytest.raises(ValueError):
+        pkg.thinker_sampler.argmax(x)
