@@ -146,6 +146,9 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
     cfg = orc.Cfg(temperature=w["temperature"], top_p=w["top_p"], top_k=w["top_k"], repetition_penalty=w["penalty"],
                   window=w["window"], min_new_tokens=0, max_new_tokens=1 << 40, min_keep=1, semantics="omni")
     seeds = np.arange(rows, dtype=np.int64)
+    # one untimed call: loads the library and builds the penalty table
+    orc.sample(x, hist, np.zeros(rows, np.int64), seeds, -1, cfg, rng=orc.RNG_PHILOX, requests=np.zeros(rows, np.int64),
+               want_processed=False, threads=threads)
     done = 0
     t0 = time.perf_counter()
     step = 0
@@ -162,16 +165,44 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
                       f"(oracle/sampler_oracle.c, OpenMP)"}
 
 
+def metric_of(w) -> str:
+    return (f"sampled rows/s at B={w['rows']} x V={w['vocab']} per GPU "
+            "(fused penalty+temperature+top-k+top-p+draw)")
+
+
+def dtype_of(w) -> str:
+    return "bf16->f32" if w["dtype"] == "bf16" else "f32"
+
+
+def rotating_buffers(w) -> int:
+    """Distinct logits buffers: one sweep exceeds twice the L2 and 640 MiB (>= 32 thinker steps)."""
+    buf = w["rows"] * w["vocab"] * (2 if w["dtype"] == "bf16" else 4)
+    return max(2, min(8192, math.ceil(max(2 * L2_BYTES, 640 * 2**20) / buf)))
+
+
+def config_of(args, w, world: int) -> dict:
+    """The workload as both arms report it."""
+    B, V = w["rows"], w["vocab"]
+    nbuf = rotating_buffers(w)
+    return {"workload": args.workload, "rows_per_gpu": B, "global_batch": B * world, "vocab": V,
+            "logits_dtype": w["dtype"], "window": w["window"], "temperature": w["temperature"], "top_k": w["top_k"],
+            "top_p": w["top_p"], "repetition_penalty": w["penalty"], "order": "omni", "rng": "philox",
+            "parallelism": f"rows x{world}",
+            "l2": f"{nbuf} rotating logits buffers ({nbuf * B * V * (2 if w['dtype'] == 'bf16' else 4) / 2**20:.0f}"
+                  " MiB > L2)",
+            "cuda_graph_steps": 0 if args.eager else min(args.steps, 1000)}
+
+
 def run_reference(args, w, rank: int):
+    """The reference algorithm on the host cores (the C restatement, all threads); rank 0 only."""
     if rank != 0:
         return
     cb = cpu_baseline(w, seconds=args.cpu_seconds)
-    line = {"impl": "reference", "metric": f"sampled rows/s at B={w['rows']} x V={w['vocab']}", "value": cb["value"],
-            "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "dtype": "f32" if w["dtype"] == "f32" else "bf16->f32",
-            "data": "synthetic", "config": {"workload": args.workload, **{k: w[k] for k in w}},
-            "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "rows/s", "h2d_bytes_per_step": 0,
-                                        "d2h_bytes_per_step": 0}}
+    line = {"impl": "reference", "metric": metric_of(w), "value": cb["value"], "unit": "rows/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype_of(w), "data": "synthetic",
+            "config": config_of(args, w, args.gpus), "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
 
@@ -211,8 +242,7 @@ def main():
     tdt = torch.bfloat16 if w["dtype"] == "bf16" else torch.float32
     row_bytes = bytes_per_row(w)
     step_bytes = B * row_bytes
-    # enough distinct logits buffers that one sweep over them exceeds twice the L2
-    nbuf = max(2, math.ceil(2 * L2_BYTES / (B * V * (2 if tdt == torch.bfloat16 else 4))))
+    nbuf = rotating_buffers(w)
     logits_h, hist_h = make_inputs(w, B, 1000 + rank)
     base = torch.from_numpy(logits_h).to(dev).to(tdt)
     bufs = []
@@ -326,16 +356,11 @@ def main():
         return
     traffic = profiled_traffic(args.workload)
     line = {
-        "metric": f"sampled rows/s at B={B} x V={V} per GPU (fused penalty+temperature+top-k+top-p+draw)",
+        "metric": metric_of(w),
         "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16->f32" if tdt == torch.bfloat16 else "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "rows_per_gpu": B, "global_batch": B * world, "vocab": V,
-                   "logits_dtype": w["dtype"], "window": W, "temperature": w["temperature"], "top_k": w["top_k"],
-                   "top_p": w["top_p"], "repetition_penalty": w["penalty"], "order": "omni", "rng": "philox",
-                   "parallelism": f"rows x{world}", "l2": f"{nbuf} rotating logits buffers "
-                   f"({nbuf * B * V * (2 if tdt == torch.bfloat16 else 4) / 2**20:.0f} MiB > L2)",
-                   "cuda_graph_steps": 0 if args.eager else G},
+        "dtype": dtype_of(w), "data": "synthetic",
+        "config": config_of(args, w, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "bytes_per_row": row_bytes, "peak_source": peak_kind},
         "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": host.numel() * host.element_size(),

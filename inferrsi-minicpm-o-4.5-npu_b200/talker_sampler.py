@@ -177,6 +177,21 @@ def repetition_penalty(x: torch.Tensor, history: torch.Tensor, penalty: float) -
     return _native.ops().repetition_penalty(x, history, alpha_table(float(penalty), history.shape[-1] + 1, x.device))
 
 
+def top_p_filter(x: torch.Tensor, top_p: float, min_keep: int) -> torch.Tensor:
+    """The two-pass nucleus filter over the fully sorted row (``talker_sampler.py:87-92``): drop the
+    ascending prefix whose cumulative softmax mass is <= 1 - top_p, never the last ``min_keep``.
+
+    The reference keeps this form only as the test oracle of the fused filters; it is kept here as the
+    same device torch ops (sort, softmax, cumsum, scatter) and is not on the sampling path, which uses the
+    fused kernels.  Where values tie across the cut, which copies survive follows the sort's order."""
+    _need_cuda(x)
+    s, idx = torch.sort(x, descending=False, dim=-1)
+    cum = s.softmax(dim=-1).cumsum(dim=-1)
+    remove = cum <= (1 - top_p)
+    remove[..., -min_keep:] = False
+    return x.masked_fill(remove.scatter(1, idx, remove), float("-inf"))
+
+
 def top_k_filter(x: torch.Tensor, top_k: int, min_keep: int) -> torch.Tensor:
     """Keep values >= the k-th largest, k = min(max(top_k, min_keep), V) (``talker_sampler.py:95-98``)."""
     _need_cuda(x)

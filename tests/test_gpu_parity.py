@@ -291,6 +291,25 @@ def test_filters_match_oracle_forms(pkg):
             assert len(H.compare_processed(want, got)) == 0, sem
 
 
+def test_two_pass_top_p_filter_is_the_reference_form(pkg):
+    """top_p_filter (the reference's full-sort form, talker_sampler.py:87-92) on the device == the same
+    formula on CPU torch, except where a cumulative mass sits within float rounding of the cut."""
+    ts = pkg.talker_sampler
+    g = torch.Generator().manual_seed(19)
+    for scale in (0.3, 1.0, 3.0, 8.0):
+        x = torch.randn(64, I.TALKER_V, generator=g) * scale
+        s, idx = torch.sort(x, descending=False, dim=-1)
+        cum = s.softmax(dim=-1).cumsum(dim=-1)
+        remove = cum <= (1 - 0.85)
+        remove[..., -3:] = False
+        want = x.masked_fill(remove.scatter(1, idx, remove), float("-inf"))
+        got = ts.top_p_filter(x.to(DEV), 0.85, 3).cpu()
+        # rows whose cumulative mass sits within rounding of the cut may differ by that one element
+        near = ((cum - (1 - 0.85)).abs() < 1e-5).any(dim=-1)
+        same = (torch.isinf(want) == torch.isinf(got)).all(dim=-1)
+        assert bool((same | near).all())
+
+
 def test_status_flags_and_pad_rows(pkg):
     ts = pkg.talker_sampler
     cfg = ts.TalkerSampling(semantics="omni", rng="counter", min_new_tokens=0)
