@@ -1,21 +1,18 @@
 // B200 (sm_100a) token-sampling kernels for MiniCPM-o 4.5 and their C-ABI launchers.
 //
-// One CTA owns one logits row (a persistent loop when the batch is larger than the grid).  The row's
-// 16-byte-aligned interior streams through a ring of shared-memory stages filled by 1-D bulk copies
-// (cp.async.bulk, no multicast, one mbarrier per stage); the ragged head / tail elements are plain loads.
-// When the interior fits the ring the row stays resident and later passes read shared memory; otherwise
-// later passes re-read global memory (the row is hot in L2).  Everything else the row needs -- parameters,
-// the RNG inputs, the history ids, the penalty table and the raw values of the history ids -- is fetched
-// while the stream is in flight.
+// One 512-thread CTA owns one logits row (a loop over rows when the batch is larger than the grid).  The
+// row's 16-byte-aligned interior streams through registers: each iteration a thread holds 4 x 16 bytes of
+// the row while the next 4 x 16 bytes are in flight (plain 16-byte loads, not kept in L1); the ragged head
+// and tail elements are single loads.  Everything else the row needs -- parameters, the RNG input, the
+// history ids (hashed in shared memory), the penalty table and the raw values of the history ids -- is
+// fetched alongside.  Later passes over the row (the exact path, hf's logsumexp, processed output) read it
+// again from L2.
 //
-//   prologue: history ids -> bitmap + hash (id -> count) -> exact processed value of every history id
-//   stream:   each thread keeps its 4 largest non-history raw values (and their ids)
-//   candidate path (top_k <= 128): two rounds of a 1024-bucket histogram over the keys of the offered
-//       values give T <= the k-th largest offered value; every non-history element >= T (the offered
-//       ones, plus a rescan by threads whose 4th value clears T) and every history id whose processed
-//       value clears f(T) are the candidates; their top-k values, the top-p cut (one warp), the value
-//       threshold and the draw in vocabulary order (one warp) finish the row
-//   exact path (top_k > 128 or too many candidates): radix select of the k-th processed key over the row,
+//   prologue: history ids -> bitmap + hash (id -> count); penalty table
+//   stream:   per-thread maxima; tau0 from the first chunk; every non-history element >= tau goes to the
+//             candidate list (one atomic per warp); warp 0 raises tau from a histogram of the candidates
+//   list stage (top_k <= 128): top-k values, top-p cut (one warp), value threshold, draw in vocabulary order
+//   exact path (top_k > 128 or an overflowing list): radix select of the k-th processed key over the row,
 //       sorted top-k values, top-p, and an ordered scan of the kept mass; frame-0 hf rows and draw() go
 //       straight to the ordered scan over the whole row
 //
@@ -38,9 +35,11 @@ namespace cg = cooperative_groups;
 namespace b2s {
 
 constexpr int KFAST = KLIST;     // largest top_k served by the candidate path
-constexpr int CHUNK = 32768;     // bytes per ring stage
-constexpr int VPC = CHUNK / 16;  // 16-byte vectors per stage
-constexpr int MAXSTAGE = 8;
+#ifndef B2S_CHUNK_BYTES
+#define B2S_CHUNK_BYTES 32768
+#endif
+constexpr int CHUNK = B2S_CHUNK_BYTES;  // bytes of the row a CTA takes per stream iteration
+constexpr int VPC = CHUNK / 16;         // 16-byte vectors per stream iteration
 constexpr int NBUCKET = 1024;    // buckets per threshold round
 constexpr int NBH_BITS = 8, NBH = 1 << NBH_BITS;  // candidate histogram buckets during the stream
 constexpr int HPT = 4;           // history positions per thread gathered during the stream
@@ -85,23 +84,20 @@ struct Params {
     int ccap;
     int64_t id_off;  // global id of column 0 of these rows (history ids are global)
     // geometry and shared-memory layout (bytes)
-    int nstage, lcap, kbuf, nvals;
+    int lcap, kbuf, nvals;
     uint32_t ht_slots, bitwords;
-    uint32_t off_ctl, off_ring, off_bits, off_ht, off_htv, off_hstage, off_atab, off_cand, off_candi, off_lst,
+    uint32_t off_ctl, off_bits, off_ht, off_htv, off_hstage, off_atab, off_cand, off_candi, off_lst,
         off_vals, off_hist, off_hraw;
     uint32_t smem_total;
 };
 
 struct Ctl {
-    uint64_t bar[MAXSTAGE];
     int cand_n, err, gather_n, kn;
     uint32_t rctl[2];
     uint32_t klo, kcnt;
     float thr;
     float u;
-    uint32_t consumed[MAXSTAGE];  // warps done with a stage (mod NWARP: the last one refills it)
     uint32_t tau_key;             // okey of the stream threshold (raised with atomicMax)
-    int ref_n;                    // candidates counted at the last threshold raise
     double red_d[NWARP + 1];
     float red_f[NWARP + 1];
     int red_i[NWARP + 1];
@@ -126,8 +122,12 @@ struct Elem<float> {
     }
     static constexpr uint32_t NEG = 0xff800000u;  // -inf in every element of a word
     static __device__ __forceinline__ void st_ninf(unsigned char* s) { *reinterpret_cast<uint32_t*>(s) = NEG; }
-    static __device__ __forceinline__ float vmax4(const uint4* q) {
-        return fmaxf(fmaxf(vmax(q[0]), vmax(q[1])), fmaxf(vmax(q[2]), vmax(q[3])));
+    template <int N>
+    static __device__ __forceinline__ float vmaxn(const uint4* q) {
+        float m = vmax(q[0]);
+#pragma unroll
+        for (int t = 1; t < N; ++t) m = fmaxf(m, vmax(q[t]));
+        return m;
     }
 };
 template <>
@@ -151,18 +151,19 @@ struct Elem<__nv_bfloat16> {
     }
     static constexpr uint32_t NEG = 0xff80ff80u;
     static __device__ __forceinline__ void st_ninf(unsigned char* s) { *reinterpret_cast<uint16_t*>(s) = (uint16_t)0xff80u; }
-    // max of 4 x 8 bf16 values in packed bf16x2 arithmetic
-    static __device__ __forceinline__ float vmax4(const uint4* q) {
-        __nv_bfloat162 m[4];
+    // max of N x 8 bf16 values in packed bf16x2 arithmetic
+    template <int N>
+    static __device__ __forceinline__ float vmaxn(const uint4* q) {
+        __nv_bfloat162 r;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < N; ++t) {
             const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&q[t].x);
             const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&q[t].y);
             const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&q[t].z);
             const __nv_bfloat162 d = *reinterpret_cast<const __nv_bfloat162*>(&q[t].w);
-            m[t] = __hmax2(__hmax2(a, b), __hmax2(c, d));
+            const __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
+            r = t == 0 ? m : __hmax2(r, m);
         }
-        const __nv_bfloat162 r = __hmax2(__hmax2(m[0], m[1]), __hmax2(m[2], m[3]));
         return fmaxf(__low2float(r), __high2float(r));
     }
 };
@@ -210,9 +211,7 @@ template <typename E>
 struct Row {
     const unsigned char* rowp;  // element 0 in global memory
     const uint4* gvec;          // interior vector 0 in global memory
-    const unsigned char* ring;  // stage buffers (vector v of a resident row at ring + 16 v)
     int V, nh, nvec, e0;        // head elements [0, nh); interior vectors; first interior element e0 == nh
-    bool resident;
     const uint32_t* bits;       // history bitmap (nullptr: no history ids)
     const uint32_t* ht;
     const float* htv;
@@ -231,18 +230,13 @@ struct Row {
         if (o + n > 32) b |= bits[w + 1] << (32 - o);
         return b & ((1u << n) - 1u);
     }
-    __device__ __forceinline__ float raw(int i) const {
-        if (resident && i >= e0 && i < e0 + nvec * Elem<E>::EPV) return Elem<E>::sld(ring + (size_t)(i - e0) * Elem<E>::SZ);
-        return Elem<E>::gld(rowp, i);
-    }
+    __device__ __forceinline__ float raw(int i) const { return Elem<E>::gld(rowp, i); }
     // processed value of element i (history ids and the censored EOS carry their own value)
     __device__ __forceinline__ float P(int i, float x) const {
         if (hbit(i)) return htv[ht_find(ht, slots, (uint32_t)i)];
         return f(x);
     }
-    __device__ __forceinline__ uint4 vec(int v) const {
-        return resident ? reinterpret_cast<const uint4*>(ring)[v] : __ldg(gvec + v);
-    }
+    __device__ __forceinline__ uint4 vec(int v) const { return __ldg(gvec + v); }
 };
 
 // Visit every element of the row as (index, raw value): interior vectors round-robin over the threads,
@@ -443,7 +437,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31;
     Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
-    unsigned char* ring = smem + p.off_ring;
     uint32_t* bits = reinterpret_cast<uint32_t*>(smem + p.off_bits);
     uint32_t* ht = reinterpret_cast<uint32_t*>(smem + p.off_ht);
     float* htv = reinterpret_cast<float*>(smem + p.off_htv);
@@ -461,16 +454,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     constexpr int ES = Elem<E>::SZ, EPV = Elem<E>::EPV;
     const int V = p.V;
     const Scr sc{hist, ctl->rctl, &ctl->gather_n, &ctl->kn, &ctl->thr, ctl->red_d, ctl->red_f, ctl->red_i};
-    uint32_t phase_bits = 0;  // parity of every stage barrier, flipped per completed fill
-
-    if (tid == 0) {
-        for (int s = 0; s < p.nstage; ++s) {
-            mbar_init(&ctl->bar[s], 1);
-            ctl->consumed[s] = 0u;
-        }
-        fence_mbar_init();
-    }
-    __syncthreads();
 
     // 16-byte-aligned interior of row r: head elements before it, vectors in it
     auto geometry = [&](int r, int& nh, int& nvec, const uint4*& gvec) {
@@ -487,31 +470,29 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         }
         gvec = reinterpret_cast<const uint4*>(ace);
     };
-    // fill the stage of chunk c of a row (one thread)
-    auto issue_chunk = [&](const uint4* gvec, int nvec, int c) {
-        const int s = c % p.nstage;
-        const uint32_t bytes = (uint32_t)min(VPC, nvec - c * VPC) * 16u;
-        mbar_arrive_expect_tx(&ctl->bar[s], bytes);
-        bulk_g2s(ring + (size_t)s * CHUNK, gvec + (size_t)c * VPC, bytes, &ctl->bar[s]);
-    };
-    bool prefetched = false;  // this row's first stages were issued while the previous row finished
-
     for (int r = blockIdx.x; r < p.rows; r += gridDim.x) {
-        // ---------------- geometry; issue the first ring fills before anything else
+        // ---------------- geometry; the first chunk's loads go out before anything else
         Row<E> R;
         R.rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
         R.V = V;
         geometry(r, R.nh, R.nvec, R.gvec);
         R.e0 = R.nh;
         const int nchunks = (R.nvec + VPC - 1) / VPC;
-        R.resident = nchunks <= p.nstage;
-        R.ring = ring;
-        auto issue = [&](int c) { issue_chunk(R.gvec, R.nvec, c); };
-        if (tid == 0) {
-            ctl->err = 0;
-            if (!prefetched)
-                for (int c = 0; c < min(nchunks, p.nstage); ++c) issue(c);
-        }
+        // chunk c of the stream: vectors c * VPC + it * NT + tid, it < ITS, loaded straight into registers
+        // (16-byte loads that skip L1; the row stays in L2 for any later pass); -inf past the row's end
+        constexpr int ITS = VPC / NT;
+        auto load_chunk = [&](int c, uint4* q) {
+            const int vn = min(VPC, R.nvec - c * VPC);
+            const uint4* g = R.gvec + (size_t)c * VPC;
+#pragma unroll
+            for (int it = 0; it < ITS; ++it) {
+                const int vl = it * NT + tid;
+                q[it] = vl < vn ? ldg_stream(g + vl) : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
+            }
+        };
+        uint4 nq[ITS];  // the next chunk, in flight while the current one is processed
+        if (nchunks > 0) load_chunk(0, nq);
+        if (tid == 0) ctl->err = 0;
 
         // ---------------- row parameters and mode (global loads overlap the stream)
         const int64_t step = p.steps ? p.steps[r] : 0;
@@ -568,11 +549,23 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             for (uint32_t w = tid; w < p.bitwords; w += NT) bits[w] = 0;
             for (uint32_t s = tid; s < p.ht_slots; s += NT) ht[s] = HT_EMPTY;
         }
+        // the ragged head (thread NT-1) and tail (thread NT-2) elements: at most 7 each (16-byte interior)
+        int edge_i[8];
+        float edge_x[8];
+        {
+            const int a0 = tid == NT - 1 ? 0 : R.e0 + R.nvec * EPV, a1 = tid == NT - 1 ? R.nh : V;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const int i = a0 + t;
+                const bool has = tid >= NT - 2 && i < a1;
+                edge_i[t] = has ? i : -1;
+                edge_x[t] = has ? Elem<E>::gld(R.rowp, i) : 0.0f;
+            }
+        }
         uint32_t* hcnt = hist;  // candidate histogram during the stream (NBH buckets above tau0)
         for (int b = tid; b < NBH; b += NT) hcnt[b] = 0;
         if (tid == 0) {
             ctl->cand_n = 0;
-            ctl->ref_n = 0;
             ctl->tau_key = 0u;
             ctl->thr = f_ninf();
             ctl->red_u[0] = 0u;
@@ -661,13 +654,12 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             return __fdiv_rn(v, T);
         };
 
-        // ---------------- stream.  Candidate path: every warp runs through the ring on its own; a stage is
-        // refilled by the last warp to release it.  tau (a raw value, lower bound of the row's k-th largest
-        // non-history raw value) starts from the first chunk: the minimum over warps of each warp's
-        // ceil(k / 16)-th largest per-thread maximum (16 * ceil(k / 16) >= k distinct elements clear it).
-        // Every non-history element >= tau (less a margin for collisions of fl(x / T)) goes to the candidate
-        // list and to a histogram of keys above tau0; the warp that releases a stage raises tau to the lower
-        // edge of the highest bucket with >= k candidates at or above it.
+        // ---------------- stream.  Candidate path: every warp runs through the row on its own.  tau (a raw
+        // value, lower bound of the row's k-th largest non-history raw value) starts from the first chunk: the
+        // k-th largest of the warps' ceil(k / 16) largest per-thread maxima (distinct elements).  Every
+        // non-history element >= tau (less a margin for collisions of fl(x / T)) goes to the candidate list and
+        // to a histogram of keys above tau0; warp 0 raises tau to the lower edge of the highest bucket with
+        // >= k candidates at or above it.
         const bool cand_path = mode == MODE_FILTER && k <= KFAST && !(p.flags & B2S_FLAG_FORCE_GENERAL) &&
                                T >= 1e-6f && T <= 1e6f;
         bool ovf = !cand_path;
@@ -677,30 +669,62 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         uint32_t k0 = 0u;       // histogram origin (key) and scale
         int sh = 0;
         auto margin = [](float t) { return t - fmaxf(fabsf(t) * 9.5367431640625e-7f, 1e-30f); };
-        auto push = [&](float x, int id) {
-            const int pos = atomicAdd(&ctl->cand_n, 1);
+        // candidate (raw value x, id) at a reserved list position
+        auto place = [&](float x, int id, int pos) {
             if (pos < p.lcap) {
                 cand_v[pos] = x;
                 cand_i[pos] = id;
             }
             atomicAdd(&hcnt[min((okey(x) - k0) >> sh, (uint32_t)(NBH - 1))], 1u);
         };
-        constexpr int ITS = VPC / NT;
-        static_assert(ITS == 4, "4 vectors per thread per chunk");
+        auto push = [&](float x, int id) { place(x, id, atomicAdd(&ctl->cand_n, 1)); };
+        // warp 0: raise tau to the lower edge of the highest histogram bucket with >= k candidates at or above
+        // it (lane l sums buckets 8l .. 8l + 7; suffix sums over lanes); only when candidates arrived since
+        auto raise_tau = [&](int& ref_n) {
+            const int nn = __shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&ctl->cand_n), 0);  // uniform
+            if (nn == ref_n) return;
+            ref_n = nn;
+            uint32_t cb[NBH / 32];
+            uint32_t sum = 0;
+#pragma unroll
+            for (int t = 0; t < NBH / 32; ++t) {
+                cb[t] = *reinterpret_cast<volatile uint32_t*>(&hcnt[lane * (NBH / 32) + t]);
+                sum += cb[t];
+            }
+            uint32_t suf = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
+                if (lane + o < 32) suf += t;
+            }
+            const unsigned ge = __ballot_sync(0xffffffffu, suf >= (uint32_t)k);
+            if (ge && lane == 31 - __clz(ge)) {
+                uint32_t acc = suf - sum;  // buckets above this lane
+                int e = lane * (NBH / 32);
+#pragma unroll
+                for (int t = NBH / 32 - 1; t >= 0; --t) {
+                    acc += cb[t];
+                    if (acc >= (uint32_t)k) {
+                        e = lane * (NBH / 32) + t;
+                        break;
+                    }
+                }
+                const float te = okey_to_f(k0 + ((uint32_t)e << sh));
+                const uint32_t nk = okey(margin(te));
+                if (nk > tau_key) atomicMax(&ctl->tau_key, nk);
+            }
+        };
+        static_assert(ITS >= 1 && ITS * NT == VPC, "whole vectors per thread per chunk");
+        int ref_n = 0;  // warp 0: candidates counted at its last threshold raise
         for (int c = 0; c < nchunks; ++c) {
-            const int s = c % p.nstage;
+            if (c > 0 && tid < 32 && !ovf) raise_tau(ref_n);  // warp 0 raises tau from the candidate histogram
             if (c < HPT) gather_hist(tid + c * NT);
-            if (!mbar_wait_bounded(&ctl->bar[s], (phase_bits >> s) & 1u)) ok = false;
-            phase_bits ^= 1u << s;
-            const uint4* st = reinterpret_cast<const uint4*>(ring + (size_t)s * CHUNK);
             const int vn = min(VPC, R.nvec - c * VPC);
             const int cbase = R.e0 + c * VPC * EPV;
             uint4 q[ITS];
 #pragma unroll
-            for (int it = 0; it < ITS; ++it) {
-                const int vl = it * NT + tid;
-                q[it] = vl < vn ? st[vl] : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
-            }
+            for (int it = 0; it < ITS; ++it) q[it] = nq[it];
+            if (c + 1 < nchunks) load_chunk(c + 1, nq);
             if (c == 0) {
                 if (cand_path) {
                     // per-thread maximum over the non-history elements of this chunk
@@ -757,13 +781,11 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                         const uint32_t span = kmax > k0 ? kmax - k0 : 0u;
                         const int nb = 32 - __clz(span);
                         sh = nb > NBH_BITS - 2 ? nb - (NBH_BITS - 2) : 0;  // tau0 .. max0 spans a quarter
-                        // the ragged head (thread 0) and tail (thread 1) of the row
-                        if (tid < 2) {
-                            const int a0 = tid == 0 ? 0 : R.e0 + R.nvec * EPV, a1 = tid == 0 ? R.nh : V;
-                            for (int i = a0; i < a1; ++i) {
-                                const float x = Elem<E>::gld(R.rowp, i);
-                                if (x >= tau_low && !R.hbit(i)) push(x, i);
-                            }
+                        // the ragged head / tail of the row (fetched in the prologue by the last warp)
+                        if (tid >= NT - 2) {
+#pragma unroll
+                            for (int t = 0; t < 8; ++t)
+                                if (edge_i[t] >= 0 && edge_x[t] >= tau_low && !R.hbit(edge_i[t])) push(edge_x[t], edge_i[t]);
                         }
                     }
                 }
@@ -774,71 +796,42 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                     tau_low = okey_to_f(tk);
                 }
             }
-            if (!ovf && Elem<E>::vmax4(q) >= tau_low) {
-                // rare: this thread holds candidates (history ids excluded through the bitmap)
+            if (!ovf) {
+                const bool maybe = Elem<E>::template vmaxn<ITS>(q) >= tau_low;
+                if (__any_sync(0xffffffffu, maybe)) {
+                    // rare: lanes of this warp hold candidates.  Each lane marks its elements >= tau (history
+                    // ids excluded through the bitmap) in a bit mask; one atomic per warp reserves the slots.
+                    static_assert(ITS * EPV <= 32, "one mask bit per element of a lane's chunk share");
+                    uint32_t hm = 0u;
+                    if (maybe) {
 #pragma unroll
-                for (int it = 0; it < ITS; ++it) {
-                    if (Elem<E>::vmax(q[it]) >= tau_low) {
-                        const int b = cbase + (it * NT + tid) * EPV;
-                        const uint32_t hb = R.hbits(b, EPV);
+                        for (int it = 0; it < ITS; ++it) {
+                            if (Elem<E>::vmax(q[it]) >= tau_low) {
+                                const uint32_t hb = R.hbits(cbase + (it * NT + tid) * EPV, EPV);
 #pragma unroll
-                        for (int j = 0; j < EPV; ++j) {
-                            const float x = Elem<E>::at(q[it], j);
-                            if (x >= tau_low && !((hb >> j) & 1u)) push(x, b + j);
-                        }
-                    }
-                }
-            }
-            // release the stage; the last warp refills it and raises tau
-            __syncwarp();
-            uint32_t last = 0u;
-            if (lane == 0) {
-                __threadfence_block();
-                last = (atomicAdd(&ctl->consumed[s], 1u) % (uint32_t)NWARP) == (uint32_t)(NWARP - 1);
-            }
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-                __threadfence_block();
-                if (lane == 0 && !R.resident && c + p.nstage < nchunks) issue(c + p.nstage);
-            }
-            if (last && !ovf && c + 1 < nchunks) {
-                const int nn = *reinterpret_cast<volatile int*>(&ctl->cand_n);
-                if (nn == *reinterpret_cast<volatile int*>(&ctl->ref_n)) last = 0u;  // nothing new since the last one
-                __syncwarp();
-                if (lane == 0 && last) ctl->ref_n = nn;
-            }
-            if (last && !ovf && c + 1 < nchunks) {
-                // lane l sums buckets 8l .. 8l + 7; suffix sums over lanes; highest bucket with >= k at or above
-                uint32_t cb[NBH / 32];
-                uint32_t sum = 0;
-#pragma unroll
-                for (int t = 0; t < NBH / 32; ++t) {
-                    cb[t] = *reinterpret_cast<volatile uint32_t*>(&hcnt[lane * (NBH / 32) + t]);
-                    sum += cb[t];
-                }
-                uint32_t suf = sum;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
-                    if (lane + o < 32) suf += t;
-                }
-                const unsigned ge = __ballot_sync(0xffffffffu, suf >= (uint32_t)k);
-                if (ge) {
-                    const int L = 31 - __clz(ge);
-                    if (lane == L) {
-                        uint32_t acc = suf - sum;  // buckets above this lane
-                        int e = lane * (NBH / 32);
-#pragma unroll
-                        for (int t = NBH / 32 - 1; t >= 0; --t) {
-                            acc += cb[t];
-                            if (acc >= (uint32_t)k) {
-                                e = lane * (NBH / 32) + t;
-                                break;
+                                for (int j = 0; j < EPV; ++j)
+                                    if (Elem<E>::at(q[it], j) >= tau_low && !((hb >> j) & 1u)) hm |= 1u << (it * EPV + j);
                             }
                         }
-                        const float te = okey_to_f(k0 + ((uint32_t)e << sh));
-                        const uint32_t nk = okey(margin(te));
-                        if (nk > tau_key) atomicMax(&ctl->tau_key, nk);
+                    }
+                    const int cnt = __popc(hm);
+                    int incl = cnt;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                        if (lane >= o) incl += t;
+                    }
+                    int base = 0;
+                    if (lane == 31) base = atomicAdd(&ctl->cand_n, incl);
+                    int pos = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
+#pragma unroll
+                    for (int it = 0; it < ITS; ++it) {
+                        uint32_t m = (hm >> (it * EPV)) & ((1u << EPV) - 1u);
+                        while (m) {
+                            const int j = __ffs(m) - 1;
+                            m &= m - 1u;
+                            place(Elem<E>::at(q[it], j), cbase + (it * NT + tid) * EPV + j, pos++);
+                        }
                     }
                 }
             }
@@ -870,14 +863,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         __syncthreads();
         const bool row_err = ctl->err != 0;
         if (cand_path && !ovf && ctl->cand_n > p.lcap) ovf = true;
-        // a streamed row is done with the ring (later passes read global memory): start the next row's fills
-        prefetched = !R.resident && r + (int)gridDim.x < p.rows;
-        if (prefetched && tid == 0) {
-            int nh2, nvec2;
-            const uint4* g2;
-            geometry(r + (int)gridDim.x, nh2, nvec2, g2);
-            for (int c = 0; c < min((nvec2 + VPC - 1) / VPC, p.nstage); ++c) issue_chunk(g2, nvec2, c);
-        }
 
         // state epilogue (tok_drawn == PAD: the row failed on the device -> PAD out, state unchanged)
         auto finish_row = [&](int64_t tok_drawn) {
@@ -1413,18 +1398,7 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     off = align_up(off + (uint32_t)p.nvals * 4, 16);
     p.off_hist = off;
     off = align_up(off + NBUCKET * 4, 16);
-    p.off_ring = off;
-    // the ring: the whole 16-byte interior when it fits (later passes then read shared memory), else a
-    // streaming ring of 4 stages
     const uint32_t limit = 227 * 1024;
-    if (off + 2 * CHUNK > limit) return B2S_ERR_UNSUPPORTED;
-    const int max_stage_fit = (int)((limit - off) / CHUNK);
-    const int row_chunks = (int)(((int64_t)a->vocab * es + CHUNK - 1) / CHUNK);
-    int nstage;
-    if (row_chunks <= MAXSTAGE && row_chunks <= max_stage_fit) nstage = row_chunks < 1 ? 1 : row_chunks;
-    else nstage = max_stage_fit < 4 ? max_stage_fit : 4;
-    p.nstage = nstage;
-    off = align_up(off + (uint32_t)nstage * CHUNK, 16);
     p.smem_total = off;
     if (p.smem_total > limit) return B2S_ERR_UNSUPPORTED;
 
