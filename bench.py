@@ -37,6 +37,9 @@ WORKLOADS = {
     "large": dict(rows=1024, vocab=151_936, dtype="f32", window=2048, temperature=1.0, top_k=50, top_p=0.95,
                   penalty=1.1),
     "talker": dict(rows=8, vocab=6562, dtype="bf16", window=64, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05),
+    # the Thinker greedy step (argmax over the head's logits, first index on ties) on the thinker shape
+    "greedy": dict(rows=64, vocab=151_936, dtype="bf16", window=0, temperature=0.0, top_k=1, top_p=1.0, penalty=1.0,
+                   op="argmax"),
 }
 L2_BYTES = 126 * 1024 * 1024
 
@@ -146,6 +149,18 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
     cfg = orc.Cfg(temperature=w["temperature"], top_p=w["top_p"], top_k=w["top_k"], repetition_penalty=w["penalty"],
                   window=w["window"], min_new_tokens=0, max_new_tokens=1 << 40, min_keep=1, semantics="omni")
     seeds = np.arange(rows, dtype=np.int64)
+    if w.get("op") == "argmax":
+        orc.argmax(x)
+        done, t0, step = 0, time.perf_counter(), 0
+        while True:
+            orc.argmax(x)
+            done += rows
+            step += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+        return {"value": done / el, "unit": "rows/s", "cores": 1, "kind": "port",
+                "sample": f"{step} x {rows} rows argmax (oracle/sampler_oracle.c, one thread)"}
     # one untimed call: loads the library and builds the penalty table
     orc.sample(x, hist, np.zeros(rows, np.int64), seeds, -1, cfg, rng=orc.RNG_PHILOX, requests=np.zeros(rows, np.int64),
                want_processed=False, threads=threads)
@@ -166,6 +181,8 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
 
 
 def metric_of(w) -> str:
+    if w.get("op") == "argmax":
+        return f"greedy rows/s at B={w['rows']} x V={w['vocab']} per GPU (argmax, first index on ties)"
     return (f"sampled rows/s at B={w['rows']} x V={w['vocab']} per GPU "
             "(fused penalty+temperature+top-k+top-p+draw)")
 
@@ -251,15 +268,18 @@ def main():
         perm = torch.randperm(V, device=dev, generator=g)
         bufs.append(base[:, perm].contiguous())
     del base
-    cfg = ts.TalkerSampling(temperature=w["temperature"], top_p=w["top_p"], top_k=w["top_k"],
+    greedy = w.get("op") == "argmax"
+    cfg = ts.TalkerSampling(temperature=w["temperature"] if not greedy else 1.0, top_p=w["top_p"], top_k=w["top_k"],
                             repetition_penalty=w["penalty"], window=W, min_new_tokens=0, max_new_tokens=1 << 62,
                             semantics="omni", rng="counter")
     state = ts.DecodeState.new(list(range(rank * B, rank * B + B)), cfg, device=dev)
     state.history.copy_(torch.from_numpy(hist_h).to(dev))
-    kw = ts._cfg_kwargs(cfg, state.history, dev)
+    kw = None if greedy else ts._cfg_kwargs(cfg, state.history, dev)
     ops = pkg._native.ops()
 
     def one_step(i):
+        if greedy:
+            return ops.argmax(bufs[i % nbuf])
         return ops.sample_state_(bufs[i % nbuf], state.history, state.steps, state.finished, state.seeds, None,
                                  state.active, kw["alpha"], None, kw["temperature"], cfg.top_p, cfg.top_k, 1,
                                  cfg.min_new_tokens, cfg.max_new_tokens, -1, ts.SEM_OMNI, ts.RNG_PHILOX,
@@ -323,9 +343,14 @@ def main():
     hist_e = state.history.clone()
     steps_e = torch.zeros(B, dtype=torch.int64, device=dev)
     seeds_e = state.seeds.clone()
+    def api_step():
+        if greedy:
+            return pkg.thinker_sampler.argmax(dbuf)
+        return ts.sample(dbuf, hist_e, steps_e, seeds_e, -1, cfg, rng="philox")
+
     for i in range(3 if args.e2e_steps else 0):
         dbuf.copy_(host, non_blocking=True)
-        tok = ts.sample(dbuf, hist_e, steps_e, seeds_e, -1, cfg, rng="philox")
+        tok = api_step()
         tok_h.copy_(tok, non_blocking=True)
     torch.cuda.synchronize()
     if world > 1:
@@ -334,7 +359,7 @@ def main():
     e0.record()
     for i in range(e2e_steps):
         dbuf.copy_(host, non_blocking=True)
-        tok = ts.sample(dbuf, hist_e, steps_e, seeds_e, -1, cfg, rng="philox")
+        tok = api_step()
         tok_h.copy_(tok, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()

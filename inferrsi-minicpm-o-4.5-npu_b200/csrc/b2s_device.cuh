@@ -124,12 +124,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
-// 16-byte load of read-only data that is not kept in L1 (it stays in L2 for a later pass over the row).
+// 16-byte load of data that stays read-only for the whole kernel, not kept in L1 (it stays in L2 for a later
+// pass over the row).  Not volatile: the compiler may batch several of them ahead of their uses.
 __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
     uint4 q;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
-                 : "l"(p));
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
+        : "l"(p));
     return q;
 }
 

@@ -115,6 +115,49 @@ __device__ __forceinline__ float list_threshold(const float* cv, int n, int k, b
     return *sc.thr;
 }
 
+// Warp 0: the draw over kn <= 128 items whose values sv[0..kn) are in vocabulary order -- softmax over them,
+// fp64 prefix of the probabilities (rounded to fp32 per prefix), the first position whose prefix exceeds
+// u * total (talker_sampler.py:168-172).  Returns that position in every lane, or 0x7fffffff when none does.
+__device__ __forceinline__ int warp_draw_sorted(const float* sv, int kn, float u) {
+    const int lane = threadIdx.x & 31;
+    float pv[4];
+    float lm = __int_as_float(0xff800000);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = lane * 4 + j;
+        pv[j] = i < kn ? sv[i] : __int_as_float(0xff800000);
+        lm = fmaxf(lm, pv[j]);
+    }
+    const float m = warp_max(lm);
+    float e[4];
+    double es = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        e[j] = (lane * 4 + j < kn) ? b2s_expf(__fsub_rn(pv[j], m)) : 0.0f;
+        es += (double)e[j];
+    }
+    const float sf = (float)warp_sum(es);
+    double ps = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        e[j] = (lane * 4 + j < kn) ? __fdiv_rn(e[j], sf) : 0.0f;
+        ps += (double)e[j];
+    }
+    const double incl = warp_incl_scan(ps);
+    const double total = __shfl_sync(0xffffffffu, incl, 31);
+    const float target = __fmul_rn(u, (float)total);
+    double acc = incl - ps;
+    int first = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        acc += (double)e[j];
+        if (first == 0x7fffffff && lane * 4 + j < kn && (float)acc > target) first = lane * 4 + j;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+    return first;
+}
+
 // Draw over the items >= thr (minus `drop_id` when >= 0): softmax over them, cumulative mass in vocabulary
 // order (fp64, rounded per prefix), first id whose mass exceeds u * total, else V - 1
 // (talker_sampler.py:168-172).  kv/ki and sv/si: scratch of >= n items each.  Result in every thread.
@@ -141,45 +184,9 @@ __device__ __forceinline__ int64_t list_draw(const float* cv, const int* ci, int
     }
     __syncthreads();
     if (kn <= 128) {
-        // warp 0, 4 consecutive items per lane (index order)
-        if (tid < 32) {
-            float pv[4];
-            float lm = __int_as_float(0xff800000);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int i = tid * 4 + j;
-                pv[j] = i < kn ? sv[i] : __int_as_float(0xff800000);
-                lm = fmaxf(lm, pv[j]);
-            }
-            const float m = warp_max(lm);
-            float e[4];
-            double es = 0.0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                e[j] = (tid * 4 + j < kn) ? b2s_expf(__fsub_rn(pv[j], m)) : 0.0f;
-                es += (double)e[j];
-            }
-            const float sf = (float)warp_sum(es);
-            double ps = 0.0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                e[j] = (tid * 4 + j < kn) ? __fdiv_rn(e[j], sf) : 0.0f;
-                ps += (double)e[j];
-            }
-            const double incl = warp_incl_scan(ps);
-            const double total = __shfl_sync(0xffffffffu, incl, 31);
-            const float target = __fmul_rn(u, (float)total);
-            double acc = incl - ps;
-            int first = 0x7fffffff;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                acc += (double)e[j];
-                if (first == 0x7fffffff && tid * 4 + j < kn && (float)acc > target) first = tid * 4 + j;
-            }
-#pragma unroll
-            for (int o = 16; o; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
-            if (tid == 0) *sc.kn = first;
-        }
+        int first = 0x7fffffff;
+        if (tid < 32) first = warp_draw_sorted(sv, kn, u);
+        if (tid == 0) *sc.kn = first;
         __syncthreads();
         const int best = *sc.kn;
         return best == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)si[best];

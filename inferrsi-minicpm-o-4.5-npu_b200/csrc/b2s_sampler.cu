@@ -41,7 +41,6 @@ constexpr int KFAST = KLIST;     // largest top_k served by the candidate path
 constexpr int CHUNK = B2S_CHUNK_BYTES;  // bytes of the row a CTA takes per stream iteration
 constexpr int VPC = CHUNK / 16;         // 16-byte vectors per stream iteration
 constexpr int NBUCKET = 1024;    // buckets per threshold round
-constexpr int NBH_BITS = 8, NBH = 1 << NBH_BITS;  // candidate histogram buckets during the stream
 constexpr int HPT = 4;           // history positions per thread gathered during the stream
 constexpr int MODE_FILTER = 0, MODE_FULL = 1, MODE_FORCED = 2, MODE_SKIP = 3, MODE_FAIL = 4;
 constexpr int64_t PAD = -1;
@@ -87,12 +86,14 @@ struct Params {
     int lcap, kbuf, nvals;
     uint32_t ht_slots, bitwords;
     uint32_t off_ctl, off_bits, off_ht, off_htv, off_hstage, off_atab, off_cand, off_candi, off_lst,
-        off_vals, off_hist, off_hraw;
+        off_vals, off_hist, off_hraw, off_tmaxc;
+    int tmc_chunks;  // chunks whose per-thread maxima fit (rows with more take the exact path)
     uint32_t smem_total;
 };
 
 struct Ctl {
     int cand_n, err, gather_n, kn;
+    int wcnt[NWARP];  // candidates each warp pushed into its segment of the list
     uint32_t rctl[2];
     uint32_t klo, kcnt;
     float thr;
@@ -442,6 +443,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     float* htv = reinterpret_cast<float*>(smem + p.off_htv);
     int64_t* hstage = reinterpret_cast<int64_t*>(smem + p.off_hstage);
     float* hraw = reinterpret_cast<float*>(smem + p.off_hraw);  // raw words of the history positions
+    float* tmaxc = reinterpret_cast<float*>(smem + p.off_tmaxc);  // [chunk][thread] maximum of the pass 1
     float* atab = reinterpret_cast<float*>(smem + p.off_atab);
     float* cand_v = reinterpret_cast<float*>(smem + p.off_cand);
     int* cand_i = reinterpret_cast<int*>(smem + p.off_candi);
@@ -470,6 +472,21 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         }
         gvec = reinterpret_cast<const uint4*>(ace);
     };
+    // chunk c of a row's stream: vectors c * VPC + it * NT + tid, it < ITS, loaded straight into registers
+    // (16-byte loads that skip L1; the row stays in L2 for any later pass); -inf past the row's end
+    constexpr int ITS = VPC / NT;
+    auto load_chunk_of = [&](const uint4* gvec, int nvec, int c, uint4* q) {
+        const int vn = min(VPC, nvec - c * VPC);
+        const uint4* g = gvec + (size_t)c * VPC;
+#pragma unroll
+        for (int it = 0; it < ITS; ++it) {
+            const int vl = it * NT + tid;
+            q[it] = vl < vn ? ldg_stream(g + vl) : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
+        }
+    };
+    uint4 nq[ITS];           // the next chunk, in flight while the current one is processed
+    bool next_row_in = false;  // nq already holds chunk 0 of this CTA's next row
+
     for (int r = blockIdx.x; r < p.rows; r += gridDim.x) {
         // ---------------- geometry; the first chunk's loads go out before anything else
         Row<E> R;
@@ -478,20 +495,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         geometry(r, R.nh, R.nvec, R.gvec);
         R.e0 = R.nh;
         const int nchunks = (R.nvec + VPC - 1) / VPC;
-        // chunk c of the stream: vectors c * VPC + it * NT + tid, it < ITS, loaded straight into registers
-        // (16-byte loads that skip L1; the row stays in L2 for any later pass); -inf past the row's end
-        constexpr int ITS = VPC / NT;
-        auto load_chunk = [&](int c, uint4* q) {
-            const int vn = min(VPC, R.nvec - c * VPC);
-            const uint4* g = R.gvec + (size_t)c * VPC;
-#pragma unroll
-            for (int it = 0; it < ITS; ++it) {
-                const int vl = it * NT + tid;
-                q[it] = vl < vn ? ldg_stream(g + vl) : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
-            }
-        };
-        uint4 nq[ITS];  // the next chunk, in flight while the current one is processed
-        if (nchunks > 0) load_chunk(0, nq);
+        auto load_chunk = [&](int c, uint4* q) { load_chunk_of(R.gvec, R.nvec, c, q); };
+        if (!next_row_in && nchunks > 0) load_chunk(0, nq);
+        next_row_in = false;
         if (tid == 0) ctl->err = 0;
 
         // ---------------- row parameters and mode (global loads overlap the stream)
@@ -562,8 +568,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 edge_x[t] = has ? Elem<E>::gld(R.rowp, i) : 0.0f;
             }
         }
-        uint32_t* hcnt = hist;  // candidate histogram during the stream (NBH buckets above tau0)
-        for (int b = tid; b < NBH; b += NT) hcnt[b] = 0;
         if (tid == 0) {
             ctl->cand_n = 0;
             ctl->tau_key = 0u;
@@ -580,11 +584,12 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         };
         if (use_ht) {
             if (pen_hist) {
-                // HB positions per thread at a time, their probes interleaved (independent shared atomics)
+                // HB positions per thread at a time, their probes interleaved (independent shared atomics); equal
+                // ids within a warp are counted once by their lowest lane (repeated tokens are the common case)
                 constexpr int HB = 4;
                 for (int j0 = 0; j0 < p.W; j0 += HB * NT) {
                     int id[HB];
-                    uint32_t hs[HB];
+                    uint32_t hs[HB], cnt[HB];
                     bool todo[HB];
 #pragma unroll
                     for (int u = 0; u < HB; ++u) {
@@ -592,7 +597,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                         id[u] = j < p.W ? hist_id(j) : -1;
                         // a vocabulary shard ignores ids of the other shards; an unsharded row flags ids >= vocab
                         if (j < p.W && id[u] < 0 && hstage[j] >= 0 && !p.cout_n) set_status(p, B2S_STATUS_HISTORY_RANGE);
-                        todo[u] = id[u] >= 0;
+                        const unsigned same = __match_any_sync(0xffffffffu, id[u]);
+                        cnt[u] = (uint32_t)__popc(same);
+                        todo[u] = id[u] >= 0 && lane == __ffs(same) - 1;
                         hs[u] = todo[u] ? ht_slot((uint32_t)id[u], p.ht_slots) : 0u;
                         if (todo[u]) atomicOr(&bits[id[u] >> 5], 1u << (id[u] & 31));
                     }
@@ -600,15 +607,15 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                         uint32_t cur[HB];
 #pragma unroll
                         for (int u = 0; u < HB; ++u)
-                            cur[u] = todo[u] ? atomicCAS(&ht[hs[u]], HT_EMPTY, ((uint32_t)id[u] << HT_CNT_BITS) | 1u) : 0u;
+                            cur[u] = todo[u] ? atomicCAS(&ht[hs[u]], HT_EMPTY, ((uint32_t)id[u] << HT_CNT_BITS) | cnt[u]) : 0u;
                         bool any = false;
 #pragma unroll
                         for (int u = 0; u < HB; ++u) {
                             if (!todo[u]) continue;
                             if (cur[u] == HT_EMPTY) {
-                                todo[u] = false;  // new slot, count 1
+                                todo[u] = false;  // new slot with this warp's count
                             } else if ((cur[u] >> HT_CNT_BITS) == (uint32_t)id[u]) {
-                                atomicAdd(&ht[hs[u]], 1u);
+                                atomicAdd(&ht[hs[u]], cnt[u]);
                                 todo[u] = false;
                             } else {
                                 hs[u] = (hs[u] + 1) & (p.ht_slots - 1);
@@ -654,188 +661,193 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             return __fdiv_rn(v, T);
         };
 
-        // ---------------- stream.  Candidate path: every warp runs through the row on its own.  tau (a raw
-        // value, lower bound of the row's k-th largest non-history raw value) starts from the first chunk: the
-        // k-th largest of the warps' ceil(k / 16) largest per-thread maxima (distinct elements).  Every
-        // non-history element >= tau (less a margin for collisions of fl(x / T)) goes to the candidate list and
-        // to a histogram of keys above tau0; warp 0 raises tau to the lower edge of the highest bucket with
-        // >= k candidates at or above it.
+        // ---------------- candidate path, in two passes over the row.
+        //   pass 1 (HBM, every element once): each thread's largest non-history value, and the largest value
+        //           (history included) of each of its chunks, kept in shared memory;
+        //   tau:    the k-th largest of the warps' ceil(k / 16) largest per-thread maxima -- k distinct
+        //           non-history elements are >= tau, so tau is a lower bound of the row's k-th largest
+        //           non-history raw value;
+        //   pass 2 (L2, only the thread-chunks whose maximum clears tau): every non-history element >= tau, less
+        //           a margin for collisions of fl(x / T), goes to the candidate list.
         const bool cand_path = mode == MODE_FILTER && k <= KFAST && !(p.flags & B2S_FLAG_FORCE_GENERAL) &&
-                               T >= 1e-6f && T <= 1e6f;
+                               T >= 1e-6f && T <= 1e6f && nchunks <= p.tmc_chunks;
         bool ovf = !cand_path;
         bool ok = true;
         float tau_low = f_inf();
         uint32_t tau_key = 0u;  // okey(tau_low)
-        uint32_t k0 = 0u;       // histogram origin (key) and scale
-        int sh = 0;
         auto margin = [](float t) { return t - fmaxf(fabsf(t) * 9.5367431640625e-7f, 1e-30f); };
-        // candidate (raw value x, id) at a reserved list position
-        auto place = [&](float x, int id, int pos) {
-            if (pos < p.lcap) {
-                cand_v[pos] = x;
-                cand_i[pos] = id;
-            }
-            atomicAdd(&hcnt[min((okey(x) - k0) >> sh, (uint32_t)(NBH - 1))], 1u);
-        };
-        auto push = [&](float x, int id) { place(x, id, atomicAdd(&ctl->cand_n, 1)); };
-        // warp 0: raise tau to the lower edge of the highest histogram bucket with >= k candidates at or above
-        // it (lane l sums buckets 8l .. 8l + 7; suffix sums over lanes); only when candidates arrived since
-        auto raise_tau = [&](int& ref_n) {
-            const int nn = __shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&ctl->cand_n), 0);  // uniform
-            if (nn == ref_n) return;
-            ref_n = nn;
-            uint32_t cb[NBH / 32];
-            uint32_t sum = 0;
-#pragma unroll
-            for (int t = 0; t < NBH / 32; ++t) {
-                cb[t] = *reinterpret_cast<volatile uint32_t*>(&hcnt[lane * (NBH / 32) + t]);
-                sum += cb[t];
-            }
-            uint32_t suf = sum;
+        // Each warp appends to its own segment of the candidate list (seg entries at cand_v + warp * seg), with
+        // a warp-uniform count in a register: no returning atomic.
+        const int seg = p.lcap / NWARP;
+        float* wv = cand_v + (tid >> 5) * seg;
+        int* wi = cand_i + (tid >> 5) * seg;
+        int wn = 0;  // this warp's candidates (same in every lane)
+        // every lane of the warp calls it with its own count; returns the lane's first position
+        auto seg_reserve = [&](int cnt) {
+            int incl = cnt;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
-                if (lane + o < 32) suf += t;
+                const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += t;
             }
-            const unsigned ge = __ballot_sync(0xffffffffu, suf >= (uint32_t)k);
-            if (ge && lane == 31 - __clz(ge)) {
-                uint32_t acc = suf - sum;  // buckets above this lane
-                int e = lane * (NBH / 32);
-#pragma unroll
-                for (int t = NBH / 32 - 1; t >= 0; --t) {
-                    acc += cb[t];
-                    if (acc >= (uint32_t)k) {
-                        e = lane * (NBH / 32) + t;
-                        break;
-                    }
-                }
-                const float te = okey_to_f(k0 + ((uint32_t)e << sh));
-                const uint32_t nk = okey(margin(te));
-                if (nk > tau_key) atomicMax(&ctl->tau_key, nk);
+            const int first = wn + incl - cnt;
+            wn += __shfl_sync(0xffffffffu, incl, 31);
+            return first;
+        };
+        auto place = [&](float x, int id, int pos) {
+            if (pos < seg) {
+                wv[pos] = x;
+                wi[pos] = id;
             }
         };
-        static_assert(ITS >= 1 && ITS * NT == VPC, "whole vectors per thread per chunk");
-        int ref_n = 0;  // warp 0: candidates counted at its last threshold raise
-        for (int c = 0; c < nchunks; ++c) {
-            if (c > 0 && tid < 32 && !ovf) raise_tau(ref_n);  // warp 0 raises tau from the candidate histogram
-            if (c < HPT) gather_hist(tid + c * NT);
-            const int vn = min(VPC, R.nvec - c * VPC);
-            const int cbase = R.e0 + c * VPC * EPV;
-            uint4 q[ITS];
+        // bit it * EPV + j: element j of vector it is >= tau_low and not a history id
+        auto hit_mask = [&](const uint4* q, int cbase) {
+            uint32_t hm = 0u;
 #pragma unroll
-            for (int it = 0; it < ITS; ++it) q[it] = nq[it];
-            if (c + 1 < nchunks) load_chunk(c + 1, nq);
-            if (c == 0) {
-                if (cand_path) {
-                    // per-thread maximum over the non-history elements of this chunk
-                    float vm0 = f_ninf();
+            for (int it = 0; it < ITS; ++it) {
+                if (Elem<E>::vmax(q[it]) >= tau_low) {
+                    const uint32_t hb = R.hbits(cbase + (it * NT + tid) * EPV, EPV);
+#pragma unroll
+                    for (int j = 0; j < EPV; ++j)
+                        if (Elem<E>::at(q[it], j) >= tau_low && !((hb >> j) & 1u)) hm |= 1u << (it * EPV + j);
+                }
+            }
+            return hm;
+        };
+        static_assert(ITS >= 1 && ITS * NT == VPC, "whole vectors per thread per chunk");
+        static_assert(ITS * EPV <= 32, "one mask bit per element of a thread's chunk share");
+        float tmax_nh = f_ninf();  // this thread's largest non-history value
+        if (cand_path) {
+            for (int c = 0; c < nchunks; ++c) {
+                if (c < HPT) gather_hist(tid + c * NT);
+                const int vn = min(VPC, R.nvec - c * VPC);
+                const int cbase = R.e0 + c * VPC * EPV;
+                uint4 q[ITS];
+#pragma unroll
+                for (int it = 0; it < ITS; ++it) q[it] = nq[it];
+                if (c + 1 < nchunks) load_chunk(c + 1, nq);
+                const float vm = Elem<E>::template vmaxn<ITS>(q);
+                tmaxc[c * NT + tid] = vm;
+                if (vm > tmax_nh) {
+                    // this chunk may raise the thread's non-history maximum: leave the history ids out
+                    float m = f_ninf();
 #pragma unroll
                     for (int it = 0; it < ITS; ++it) {
                         const int vl = it * NT + tid;
-                        if (vl >= vn) continue;
-                        const uint32_t hb = R.hbits(cbase + vl * EPV, EPV);
+                        const uint32_t hb = vl < vn ? R.hbits(cbase + vl * EPV, EPV) : 0u;
                         if (hb == 0u) {
-                            vm0 = fmaxf(vm0, Elem<E>::vmax(q[it]));
+                            m = fmaxf(m, Elem<E>::vmax(q[it]));
                         } else {
 #pragma unroll
                             for (int j = 0; j < EPV; ++j)
-                                if (!((hb >> j) & 1u)) vm0 = fmaxf(vm0, Elem<E>::at(q[it], j));
+                                if (!((hb >> j) & 1u)) m = fmaxf(m, Elem<E>::at(q[it], j));
                         }
                     }
-                    // the warp's jw largest per-thread maxima (distinct lanes): take the maximum out jw times
-                    const int jw = (k + NWARP - 1) / NWARP;
-                    float v = vm0;
-                    for (int t = 0; t < jw; ++t) {
-                        const float mj = warp_max(v);
-                        const unsigned who = __ballot_sync(0xffffffffu, v == mj);
-                        if (who && lane == __ffs(who) - 1) v = f_ninf();
-                        if (lane == 0) kv[(tid >> 5) * jw + t] = mj;
-                    }
-                }
-                __syncthreads();
-                if (cand_path) {
-                    // tau0 = the k-th largest of the gathered values (each one a distinct element)
-                    const int ng = NWARP * ((k + NWARP - 1) / NWARP);
-                    if (tid < ng) {
-                        const float x = kv[tid];
-                        int gt = 0, eq = 0;
-                        for (int j = 0; j < ng; ++j) {
-                            const float y = kv[j];
-                            gt += y > x;
-                            eq += y == x;
-                        }
-                        if (x > f_ninf() && gt < k && k <= gt + eq) ctl->thr = x;
-                        if (gt == 0 && x == x) ctl->red_u[0] = okey(x);
-                    }
-                }
-                __syncthreads();
-                if (cand_path) {
-                    const float t0 = ctl->thr;
-                    const uint32_t kmax = ctl->red_u[0];
-                    if (!(t0 > f_ninf()) || t0 == f_inf() || R.f(t0) == f_inf()) {
-                        ovf = true;
-                    } else {
-                        tau_low = margin(t0);
-                        tau_key = okey(tau_low);
-                        k0 = tau_key;
-                        const uint32_t span = kmax > k0 ? kmax - k0 : 0u;
-                        const int nb = 32 - __clz(span);
-                        sh = nb > NBH_BITS - 2 ? nb - (NBH_BITS - 2) : 0;  // tau0 .. max0 spans a quarter
-                        // the ragged head / tail of the row (fetched in the prologue by the last warp)
-                        if (tid >= NT - 2) {
-#pragma unroll
-                            for (int t = 0; t < 8; ++t)
-                                if (edge_i[t] >= 0 && edge_x[t] >= tau_low && !R.hbit(edge_i[t])) push(edge_x[t], edge_i[t]);
-                        }
-                    }
-                }
-            } else if (!ovf) {
-                const uint32_t tk = *reinterpret_cast<volatile uint32_t*>(&ctl->tau_key);
-                if (tk > tau_key) {
-                    tau_key = tk;
-                    tau_low = okey_to_f(tk);
+                    tmax_nh = fmaxf(tmax_nh, m);
                 }
             }
-            if (!ovf) {
-                const bool maybe = Elem<E>::template vmaxn<ITS>(q) >= tau_low;
-                if (__any_sync(0xffffffffu, maybe)) {
-                    // rare: lanes of this warp hold candidates.  Each lane marks its elements >= tau (history
-                    // ids excluded through the bitmap) in a bit mask; one atomic per warp reserves the slots.
-                    static_assert(ITS * EPV <= 32, "one mask bit per element of a lane's chunk share");
-                    uint32_t hm = 0u;
-                    if (maybe) {
+            // the ragged head / tail (the last warp's lanes 30, 31)
+            if (tid >= NT - 2)
 #pragma unroll
-                        for (int it = 0; it < ITS; ++it) {
-                            if (Elem<E>::vmax(q[it]) >= tau_low) {
-                                const uint32_t hb = R.hbits(cbase + (it * NT + tid) * EPV, EPV);
-#pragma unroll
-                                for (int j = 0; j < EPV; ++j)
-                                    if (Elem<E>::at(q[it], j) >= tau_low && !((hb >> j) & 1u)) hm |= 1u << (it * EPV + j);
-                            }
-                        }
-                    }
-                    const int cnt = __popc(hm);
-                    int incl = cnt;
-#pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const int t = __shfl_up_sync(0xffffffffu, incl, o);
-                        if (lane >= o) incl += t;
-                    }
-                    int base = 0;
-                    if (lane == 31) base = atomicAdd(&ctl->cand_n, incl);
-                    int pos = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
-#pragma unroll
-                    for (int it = 0; it < ITS; ++it) {
-                        uint32_t m = (hm >> (it * EPV)) & ((1u << EPV) - 1u);
-                        while (m) {
-                            const int j = __ffs(m) - 1;
-                            m &= m - 1u;
-                            place(Elem<E>::at(q[it], j), cbase + (it * NT + tid) * EPV + j, pos++);
-                        }
-                    }
+                for (int t = 0; t < 8; ++t)
+                    if (edge_i[t] >= 0 && !R.hbit(edge_i[t])) tmax_nh = fmaxf(tmax_nh, edge_x[t]);
+            // the warp's jw largest per-thread maxima (distinct lanes): take the maximum out jw times
+            const int jw = (k + NWARP - 1) / NWARP;
+            float v = tmax_nh;
+            for (int t = 0; t < jw; ++t) {
+                const float mj = warp_max(v);
+                const unsigned who = __ballot_sync(0xffffffffu, v == mj);
+                if (who && lane == __ffs(who) - 1) v = f_ninf();
+                if (lane == 0) kv[(tid >> 5) * jw + t] = mj;
+            }
+        } else {
+            for (int u = 0; u < HPT; ++u) gather_hist(tid + u * NT);
+        }
+        // this row's stream is done: start the first chunk of the CTA's next row
+        if (r + (int)gridDim.x < p.rows) {
+            int nh2, nvec2;
+            const uint4* g2;
+            geometry(r + (int)gridDim.x, nh2, nvec2, g2);
+            if (nvec2 > 0) load_chunk_of(g2, nvec2, 0, nq);
+            next_row_in = true;
+        }
+        __syncthreads();
+        if (cand_path) {
+            // tau = the k-th largest of the gathered values (each one a distinct non-history element)
+            const int ng = NWARP * ((k + NWARP - 1) / NWARP);
+            if (tid < ng) {
+                const float x = kv[tid];
+                int gt = 0, eq = 0;
+                for (int j = 0; j < ng; ++j) {
+                    const float y = kv[j];
+                    gt += y > x;
+                    eq += y == x;
                 }
+                if (x > f_ninf() && gt < k && k <= gt + eq) ctl->thr = x;
             }
         }
+        __syncthreads();
+        if (cand_path) {
+            const float t0 = ctl->thr;
+            if (!(t0 > f_ninf()) || t0 == f_inf() || R.f(t0) == f_inf()) {
+                ovf = true;
+            } else {
+                tau_low = margin(t0);
+                tau_key = okey(tau_low);
+            }
+        }
+        if (cand_path && !ovf) {
+            // pass 2: each thread re-reads (from L2) its chunks whose maximum clears tau, two at a time so that
+            // most threads wait for one round trip
+            uint64_t hits = 0ull;
+            for (int c = 0; c < nchunks; ++c) hits |= (uint64_t)(tmaxc[c * NT + tid] >= tau_low) << c;
+            auto load_at = [&](int c, uint4* q) {
+                const int vn = c >= 0 ? min(VPC, R.nvec - c * VPC) : 0;
+#pragma unroll
+                for (int it = 0; it < ITS; ++it) {
+                    const int vl = it * NT + tid;
+                    q[it] = vl < vn ? __ldg(R.gvec + (size_t)c * VPC + vl)
+                                    : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
+                }
+            };
+            auto place_all = [&](const uint4* q, uint32_t hm, int cbase, int pos) {
+#pragma unroll
+                for (int it = 0; it < ITS; ++it) {
+                    uint32_t m = (hm >> (it * EPV)) & ((1u << EPV) - 1u);
+                    while (m) {
+                        const int j = __ffs(m) - 1;
+                        m &= m - 1u;
+                        place(Elem<E>::at(q[it], j), cbase + (it * NT + tid) * EPV + j, pos++);
+                    }
+                }
+            };
+            while (__any_sync(0xffffffffu, hits != 0ull)) {
+                const int c1 = hits ? __ffsll((long long)hits) - 1 : -1;
+                if (hits) hits &= hits - 1ull;
+                const int c2 = hits ? __ffsll((long long)hits) - 1 : -1;
+                if (hits) hits &= hits - 1ull;
+                uint4 q1[ITS], q2[ITS];
+                load_at(c1, q1);
+                load_at(c2, q2);
+                const uint32_t h1 = c1 >= 0 ? hit_mask(q1, R.e0 + c1 * VPC * EPV) : 0u;
+                const uint32_t h2 = c2 >= 0 ? hit_mask(q2, R.e0 + c2 * VPC * EPV) : 0u;
+                const int pos = seg_reserve(__popc(h1) + __popc(h2));
+                if (h1) place_all(q1, h1, R.e0 + c1 * VPC * EPV, pos);
+                if (h2) place_all(q2, h2, R.e0 + c2 * VPC * EPV, pos + __popc(h1));
+            }
+            // the ragged head / tail
+            if ((tid >> 5) == NWARP - 1) {
+                uint32_t em = 0u;
+#pragma unroll
+                for (int t = 0; t < 8; ++t)
+                    if (edge_i[t] >= 0 && edge_x[t] >= tau_low && !R.hbit(edge_i[t])) em |= 1u << t;
+                int pos = seg_reserve(__popc(em));
+#pragma unroll
+                for (int t = 0; t < 8; ++t)
+                    if ((em >> t) & 1u) place(edge_x[t], edge_i[t], pos++);
+            }
+        }
+        if (lane == 0) ctl->wcnt[tid >> 5] = wn;
         // processed values of the history ids
         if (pen_hist) {
             for (int u = nchunks; u < HPT; ++u) gather_hist(tid + u * NT);  // short rows
@@ -862,7 +874,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         }
         __syncthreads();
         const bool row_err = ctl->err != 0;
-        if (cand_path && !ovf && ctl->cand_n > p.lcap) ovf = true;
+        if (cand_path && !ovf)
+            for (int w = 0; w < NWARP; ++w)
+                if (ctl->wcnt[w] > seg) ovf = true;  // a warp's segment overflowed (heavy ties)
 
         // state epilogue (tok_drawn == PAD: the row failed on the device -> PAD out, state unchanged)
         auto finish_row = [&](int64_t tok_drawn) {
@@ -896,11 +910,10 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         if (cand_path && !ovf && !row_err) {
             const uint32_t tk = max(tau_key, ctl->tau_key);
             const float tl = okey_to_f(tk);
-            const int n0 = ctl->cand_n;
             if (tid == 0) ctl->kn = 0;
             __syncthreads();
-            for (int i = tid; i < n0; i += NT) {
-                if (cand_v[i] >= tl) {
+            for (int i = tid; i < p.lcap; i += NT) {
+                if (i % seg < ctl->wcnt[i / seg] && cand_v[i] >= tl) {
                     const int pos = atomicAdd(&ctl->kn, 1);
                     if (pos < p.lcap) {
                         kv[pos] = R.f(cand_v[i]);
@@ -1134,13 +1147,22 @@ __global__ void __launch_bounds__(NT, 2) argmax_kernel(const void* logits, int V
             const uint4* vp = reinterpret_cast<const uint4*>(Ace);
             const int nv = (int)((Bfl - Ace) / 16);
             const int i0 = lo + nh;
-            for (int v = tid; v < nv; v += NT) {
-                uint4 q;
-                asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                             : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
-                             : "l"(vp + v));
+            // 4 loads in flight per thread, then their elements in index order (per thread, increasing v)
+            for (int v0 = 0; v0 < nv; v0 += 4 * NT) {
+                uint4 q[4];
 #pragma unroll
-                for (int j = 0; j < 16 / ES; ++j) upd(Elem<E>::at(q, j), i0 + v * (16 / ES) + j);
+                for (int u = 0; u < 4; ++u) {
+                    const int v = v0 + u * NT + tid;
+                    q[u] = v < nv ? ldg_stream(vp + v) : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int v = v0 + u * NT + tid;
+                    if (v < nv) {
+#pragma unroll
+                        for (int j = 0; j < 16 / ES; ++j) upd(Elem<E>::at(q[u], j), i0 + v * (16 / ES) + j);
+                    }
+                }
             }
         } else {
             for (int i = lo + tid; i < hi; i += NT) upd(Elem<E>::gld(rowp, i), i);
@@ -1161,12 +1183,21 @@ __global__ void __launch_bounds__(NT, 2) argmax_kernel(const void* logits, int V
         ci = bi;
     }
     cluster.sync();
-    if (crank == 0 && tid == 0) {
-        for (int c = 1; c < C; ++c) {
-            const int oi = *cluster.map_shared_rank(&ci, c);
-            if (oi != 0x7fffffff) upd(*cluster.map_shared_rank(&cv, c), oi);
+    if (crank == 0 && tid < 32) {
+        // lane c reads rank c's result (the remote reads overlap), then the warp reduces
+        bv = f_ninf();
+        bi = 0x7fffffff;
+        if (tid < C) {
+            const int oi = *cluster.map_shared_rank(&ci, tid);
+            if (oi != 0x7fffffff) upd(*cluster.map_shared_rank(&cv, tid), oi);
         }
-        tokens[r] = bi == 0x7fffffff ? 0 : bi;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != 0x7fffffff) upd(ov, oi);
+        }
+        if (tid == 0) tokens[r] = bi == 0x7fffffff ? 0 : bi;
     }
     cluster.sync();
 }
@@ -1399,6 +1430,14 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     p.off_hist = off;
     off = align_up(off + NBUCKET * 4, 16);
     const uint32_t limit = 227 * 1024;
+    p.off_tmaxc = off;
+    {
+        const int row_chunks = (int)(((int64_t)a->vocab * es / 16 + VPC - 1) / VPC);
+        int fit = off < limit ? (int)((limit - off) / (NT * 4)) : 0;
+        fit = fit < 64 ? fit : 64;  // pass 2 keeps one bit per chunk
+        p.tmc_chunks = row_chunks < fit ? row_chunks : fit;
+        off = align_up(off + (uint32_t)p.tmc_chunks * NT * 4, 16);
+    }
     p.smem_total = off;
     if (p.smem_total > limit) return B2S_ERR_UNSUPPORTED;
 
