@@ -128,9 +128,10 @@ def measured_peak_gbs():
     return 6650.0, "fallback"
 
 
-def profiled_traffic(workload: str):
-    """DRAM bytes per launch of the sampling kernel from the committed ncu summary, or None."""
-    f = ROOT / "profiles" / f"sample_kernel_{workload}.md"
+def profiled_traffic(workload: str, w) -> float | None:
+    """DRAM bytes per launch of the workload's kernel from the committed ncu summary, or None."""
+    kernel = "argmax_kernel" if w.get("op") == "argmax" else "sample_kernel"
+    f = ROOT / "profiles" / f"{kernel}_{workload}.md"
     if not f.exists():
         return None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
@@ -379,7 +380,7 @@ def main():
         dist.destroy_process_group()
     if rank != 0:
         return
-    traffic = profiled_traffic(args.workload)
+    traffic = profiled_traffic(args.workload, w)
     line = {
         "metric": metric_of(w),
         "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,

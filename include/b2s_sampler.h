@@ -46,7 +46,7 @@ extern "C" {
 /* bits of the device status word */
 #define B2S_STATUS_HISTORY_RANGE 1u /* a history id >= vocab was ignored */
 #define B2S_STATUS_TOPK_LIMIT 2u    /* a row's top_k exceeded max_top_k; the row returned PAD */
-#define B2S_STATUS_WAIT_TIMEOUT 4u  /* a bounded wait for an in-flight copy gave up; the row returned PAD */
+#define B2S_STATUS_WAIT_TIMEOUT 4u  /* reserved: a bounded device wait gave up (the current kernels have none) */
 #define B2S_STATUS_COUNT_LIMIT 8u   /* a token repeated more times than alpha_len-1 in the history */
 #define B2S_STATUS_SHARD_INCOMPLETE 16u /* a shard's candidate list overflowed `cap` or failed; the row returned PAD */
 

@@ -1,5 +1,5 @@
-// Device helpers of the B200 sampler: the sampler numerics spec (exp, order keys), the two RNGs,
-// bulk-copy / mbarrier PTX wrappers and CTA-wide primitives (reductions, scans, radix select).
+// Device helpers of the B200 sampler: the sampler numerics spec (exp, order keys), the two RNGs, load and
+// asynchronous-copy PTX wrappers and CTA-wide primitives (reductions, scans, radix select).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -10,7 +10,6 @@ namespace b2s {
 
 constexpr int NT = 512;        // threads per CTA of the row kernels
 constexpr int NWARP = NT / 32;
-constexpr uint32_t WAIT_LIMIT = 1u << 22;  // bounded spin on an mbarrier (each try_wait also sleeps)
 
 // ---------------------------------------------------------------- numerics spec
 
@@ -97,33 +96,10 @@ __device__ __forceinline__ float uniform_philox(int64_t seed, int64_t step, int6
     return (float)(w >> 8) * (1.0f / 16777216.0f);
 }
 
-// ---------------------------------------------------------------- PTX: mbarrier + bulk copy (no multicast)
+// ---------------------------------------------------------------- PTX: loads and asynchronous copies
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void fence_mbar_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-// Plain arrival (release semantics at CTA scope); the caller does not wait.
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar` (bytes: multiple of 16,
-// both addresses 16-byte aligned).
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
 // 16-byte load of data that stays read-only for the whole kernel, not kept in L1 (it stays in L2 for a later
 // pass over the row).  Not volatile: the compiler may batch several of them ahead of their uses.
 __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
@@ -142,40 +118,6 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// try_wait that suspends the thread until the phase completes or `ns` nanoseconds pass, so waiting warps do
-// not take issue slots and shared-memory bandwidth from the warps still working
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait; returns false when the limit ran out (the caller flags the row and carries on).  At most
-// WAIT_SLEEP_LIMIT suspensions of WAIT_SLEEP_NS each (about 1.3 s).
-constexpr uint32_t WAIT_SLEEP_NS = 5000, WAIT_SLEEP_LIMIT = 1u << 18;
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    for (uint32_t it = 0; it < WAIT_SLEEP_LIMIT; ++it)
-        if (mbar_try_wait_sleep(bar, parity, WAIT_SLEEP_NS)) return true;
-    return false;
-}
-
-// Split cluster barrier (release on arrive, acquire on wait); every thread of every CTA takes part.
-__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- warp / CTA primitives
 

@@ -672,7 +672,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         const bool cand_path = mode == MODE_FILTER && k <= KFAST && !(p.flags & B2S_FLAG_FORCE_GENERAL) &&
                                T >= 1e-6f && T <= 1e6f && nchunks <= p.tmc_chunks;
         bool ovf = !cand_path;
-        bool ok = true;
         float tau_low = f_inf();
         uint32_t tau_key = 0u;  // okey(tau_low)
         auto margin = [](float t) { return t - fmaxf(fabsf(t) * 9.5367431640625e-7f, 1e-30f); };
@@ -868,10 +867,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             }
         }
         if (censor && tid == 0) htv[ht_find(ht, p.ht_slots, (uint32_t)p.eos)] = f_ninf();  // omni: EOS is -inf
-        if (!ok) {
-            ctl->err = 1;
-            set_status(p, B2S_STATUS_WAIT_TIMEOUT);
-        }
         __syncthreads();
         const bool row_err = ctl->err != 0;
         if (cand_path && !ovf)
