@@ -36,7 +36,14 @@ WORKLOADS = {
                     penalty=1.05),
     "large": dict(rows=1024, vocab=151_936, dtype="f32", window=2048, temperature=1.0, top_k=50, top_p=0.95,
                   penalty=1.1),
-    "talker": dict(rows=8, vocab=6562, dtype="bf16", window=64, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05),
+    # batched Talker at streaming concurrency -- per-row T / k / p (row i takes index i mod 3),
+    # EOS (the last column) masked for the first 8 steps, rows shifted by U(-1, 1)
+    "talker": dict(rows=8, vocab=6562, dtype="bf16", window=64, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05,
+                   order="hf", min_keep=3, eos=6561, min_new=8, row_temperature=(0.6, 0.8, 1.0),
+                   row_top_k=(20, 25, 50), row_top_p=(0.7, 0.85, 0.95)),
+    # the single-stream Talker (one row, fp32, hf order, 16-token history)
+    "talker1": dict(rows=1, vocab=6562, dtype="f32", window=16, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05,
+                    order="hf", min_keep=3, eos=6561, min_new=0),
     # the Thinker greedy step (argmax over the head's logits, first index on ties) on the thinker shape
     "greedy": dict(rows=64, vocab=151_936, dtype="bf16", window=0, temperature=0.0, top_k=1, top_p=1.0, penalty=1.0,
                    op="argmax"),
@@ -57,9 +64,18 @@ def make_inputs(w, rows: int, seed: int):
     g = I.rng(seed)
     if w["vocab"] == 151_936 and w["dtype"] == "bf16":
         logits, hist = I.zipf_rows(g, rows, w["vocab"], w["window"])
+    elif w.get("order") == "hf":  # Talker: N(0, 2); several rows also get a per-row shift U(-1, 1)
+        logits = (g.standard_normal((rows, w["vocab"])) * 2.0).astype(np.float32)
+        if rows > 1:
+            logits += g.uniform(-1.0, 1.0, size=(rows, 1)).astype(np.float32)
+        hist = g.integers(0, w["vocab"], size=(rows, w["window"]))
     else:
         logits = (g.standard_normal((rows, w["vocab"])) * 3.0).astype(np.float32)
         hist = g.integers(0, w["vocab"], size=(rows, w["window"]))
+    if w.get("eos", -1) >= 0:
+        # the EOS column stays far below the rest, so that rows stay live over any number of steps (its masking
+        # and forcing rules still run every step)
+        logits[:, w["eos"]] = -30.0
     if w["dtype"] == "bf16":
         logits = I.bf16_bits_to_f32(I.to_bf16_bits(logits))
     return logits, hist.astype(np.int64)
@@ -148,7 +164,13 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
     logits, hist = make_inputs(w, rows, 1234)
     x = I.to_bf16_bits(logits) if w["dtype"] == "bf16" else logits
     cfg = orc.Cfg(temperature=w["temperature"], top_p=w["top_p"], top_k=w["top_k"], repetition_penalty=w["penalty"],
-                  window=w["window"], min_new_tokens=0, max_new_tokens=1 << 40, min_keep=1, semantics="omni")
+                  window=w["window"], min_new_tokens=w.get("min_new", 0), max_new_tokens=1 << 40,
+                  min_keep=w.get("min_keep", 1), semantics=w.get("order", "omni"))
+    rowkw = {}
+    if "row_temperature" in w:
+        rowkw = dict(row_temperature=np.array([w["row_temperature"][i % 3] for i in range(rows)], np.float32),
+                     row_top_p=np.array([w["row_top_p"][i % 3] for i in range(rows)], np.float32),
+                     row_top_k=np.array([w["row_top_k"][i % 3] for i in range(rows)], np.int32))
     seeds = np.arange(rows, dtype=np.int64)
     if w.get("op") == "argmax":
         orc.argmax(x)
@@ -163,14 +185,15 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
         return {"value": done / el, "unit": "rows/s", "cores": 1, "kind": "port",
                 "sample": f"{step} x {rows} rows argmax (oracle/sampler_oracle.c, one thread)"}
     # one untimed call: loads the library and builds the penalty table
-    orc.sample(x, hist, np.zeros(rows, np.int64), seeds, -1, cfg, rng=orc.RNG_PHILOX, requests=np.zeros(rows, np.int64),
-               want_processed=False, threads=threads)
+    eos = w.get("eos", -1)
+    orc.sample(x, hist, np.ones(rows, np.int64), seeds, eos, cfg, rng=orc.RNG_PHILOX, requests=np.zeros(rows, np.int64),
+               want_processed=False, threads=threads, **rowkw)
     done = 0
     t0 = time.perf_counter()
     step = 0
     while True:
-        orc.sample(x, hist, np.full(rows, step, np.int64), seeds, -1, cfg, rng=orc.RNG_PHILOX,
-                   requests=np.zeros(rows, np.int64), want_processed=False, threads=threads)
+        orc.sample(x, hist, np.full(rows, step + 1, np.int64), seeds, eos, cfg, rng=orc.RNG_PHILOX,
+                   requests=np.zeros(rows, np.int64), want_processed=False, threads=threads, **rowkw)
         done += rows
         step += 1
         el = time.perf_counter() - t0
@@ -204,7 +227,9 @@ def config_of(args, w, world: int) -> dict:
     nbuf = rotating_buffers(w)
     return {"workload": args.workload, "rows_per_gpu": B, "global_batch": B * world, "vocab": V,
             "logits_dtype": w["dtype"], "window": w["window"], "temperature": w["temperature"], "top_k": w["top_k"],
-            "top_p": w["top_p"], "repetition_penalty": w["penalty"], "order": "omni", "rng": "philox",
+            "top_p": w["top_p"], "repetition_penalty": w["penalty"], "order": w.get("order", "omni"), "rng": "philox",
+            "min_keep": w.get("min_keep", 1), "eos": w.get("eos", -1), "min_new_tokens": w.get("min_new", 0),
+            "per_row": {k: list(w[k]) for k in ("row_temperature", "row_top_k", "row_top_p") if k in w} or None,
             "parallelism": f"rows x{world}",
             "l2": f"{nbuf} rotating logits buffers ({nbuf * B * V * (2 if w['dtype'] == 'bf16' else 4) / 2**20:.0f}"
                   " MiB > L2)",
@@ -265,26 +290,40 @@ def main():
     base = torch.from_numpy(logits_h).to(dev).to(tdt)
     bufs = []
     g = torch.Generator(device=dev).manual_seed(rank)
-    for i in range(nbuf):  # distinct contents: a per-buffer permutation of the columns of each row
-        perm = torch.randperm(V, device=dev, generator=g)
+    eos = w.get("eos", -1)
+    for i in range(nbuf):  # distinct contents: a per-buffer permutation of the columns (EOS stays in place)
+        perm = torch.randperm(V - 1 if eos >= 0 else V, device=dev, generator=g)
+        if eos >= 0:
+            perm = torch.cat([perm, torch.tensor([V - 1], device=dev)])
         bufs.append(base[:, perm].contiguous())
     del base
     greedy = w.get("op") == "argmax"
     cfg = ts.TalkerSampling(temperature=w["temperature"] if not greedy else 1.0, top_p=w["top_p"], top_k=w["top_k"],
-                            repetition_penalty=w["penalty"], window=W, min_new_tokens=0, max_new_tokens=1 << 62,
-                            semantics="omni", rng="counter")
+                            repetition_penalty=w["penalty"], window=W, min_new_tokens=w.get("min_new", 0),
+                            max_new_tokens=1 << 62, min_keep=w.get("min_keep", 1), semantics=w.get("order", "omni"),
+                            rng="counter")
     state = ts.DecodeState.new(list(range(rank * B, rank * B + B)), cfg, device=dev)
     state.history.copy_(torch.from_numpy(hist_h).to(dev))
-    kw = None if greedy else ts._cfg_kwargs(cfg, state.history, dev)
+    if w.get("order") == "hf":
+        state.steps.fill_(1)  # past frame 0, so the hf filters apply from the first step
+    rp = None
+    if "row_temperature" in w:
+        rp = ts.RowParams(
+            temperature=torch.tensor([w["row_temperature"][i % 3] for i in range(B)], dtype=torch.float32, device=dev),
+            top_p=torch.tensor([w["row_top_p"][i % 3] for i in range(B)], dtype=torch.float32, device=dev),
+            top_k=torch.tensor([w["row_top_k"][i % 3] for i in range(B)], dtype=torch.int32, device=dev),
+            max_top_k=max(w["row_top_k"]))
+    kw = None if greedy else ts._cfg_kwargs(cfg, state.history, dev, rp)
     ops = pkg._native.ops()
 
     def one_step(i):
         if greedy:
             return ops.argmax(bufs[i % nbuf])
         return ops.sample_state_(bufs[i % nbuf], state.history, state.steps, state.finished, state.seeds, None,
-                                 state.active, kw["alpha"], None, kw["temperature"], cfg.top_p, cfg.top_k, 1,
-                                 cfg.min_new_tokens, cfg.max_new_tokens, -1, ts.SEM_OMNI, ts.RNG_PHILOX,
-                                 kw["max_top_k"], 0)
+                                 state.active, kw["alpha"], None, None if rp is None else rp.temperature,
+                                 None if rp is None else rp.top_p, None if rp is None else rp.top_k,
+                                 kw["temperature"], cfg.top_p, cfg.top_k, kw["min_keep"], cfg.min_new_tokens,
+                                 cfg.max_new_tokens, eos, kw["semantics"], ts.RNG_PHILOX, kw["max_top_k"], 0)
 
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.synchronize()
@@ -342,12 +381,12 @@ def main():
     dbuf = torch.empty_like(host, device=dev)
     tok_h = torch.empty(B, dtype=torch.int64).pin_memory()
     hist_e = state.history.clone()
-    steps_e = torch.zeros(B, dtype=torch.int64, device=dev)
+    steps_e = torch.ones(B, dtype=torch.int64, device=dev)
     seeds_e = state.seeds.clone()
     def api_step():
         if greedy:
             return pkg.thinker_sampler.argmax(dbuf)
-        return ts.sample(dbuf, hist_e, steps_e, seeds_e, -1, cfg, rng="philox")
+        return ts.sample(dbuf, hist_e, steps_e, seeds_e, eos, cfg, rng="philox", row_params=rp)
 
     for i in range(3 if args.e2e_steps else 0):
         dbuf.copy_(host, non_blocking=True)

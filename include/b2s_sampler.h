@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define B2S_ABI_VERSION 1
+#define B2S_ABI_VERSION 2
 
 /* return codes */
 #define B2S_OK 0
@@ -102,6 +102,9 @@ typedef struct b2s_sample_args {
     int64_t* steps_out;              /* [rows] (may alias steps) */
     uint8_t* finished_out;           /* [rows] (may alias finished) */
     uint32_t* status;                /* device status word (bits OR-ed), or NULL */
+    /* per-row min_new_tokens / max_new_tokens ([rows] int64) overriding the scalars, or NULL (ABI 2) */
+    const int64_t* row_min_new_tokens;
+    const int64_t* row_max_new_tokens;
 } b2s_sample_args;
 
 /*

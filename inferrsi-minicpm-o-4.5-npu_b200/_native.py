@@ -38,6 +38,7 @@ class SampleArgs(ctypes.Structure):
         ("processed_row_stride", ctypes.c_int64), ("history_out", ctypes.c_void_p),
         ("history_out_row_stride", ctypes.c_int64), ("steps_out", ctypes.c_void_p),
         ("finished_out", ctypes.c_void_p), ("status", ctypes.c_void_p),
+        ("row_min_new_tokens", ctypes.c_void_p), ("row_max_new_tokens", ctypes.c_void_p),
     ]
 
 

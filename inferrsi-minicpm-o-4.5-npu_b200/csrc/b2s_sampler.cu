@@ -62,6 +62,8 @@ struct Params {
     float T, top_p, presence, frequency;
     int top_k, min_keep;
     int64_t min_new, max_new;
+    const int64_t* rminn;  // per-row min_new / max_new, or nullptr
+    const int64_t* rmaxn;
     const float* rT;
     const float* rP;
     const int32_t* rK;
@@ -509,11 +511,12 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         const float top_p = p.rP ? p.rP[r] : p.top_p;
         const int top_k = p.rK ? p.rK[r] : p.top_k;
         const bool eos_ok = !identity && p.eos >= 0 && p.eos < V;
-        const bool masked_eos = eos_ok && step < p.min_new;
+        const int64_t min_new = p.rminn ? p.rminn[r] : p.min_new, max_new = p.rmaxn ? p.rmaxn[r] : p.max_new;
+        const bool masked_eos = eos_ok && step < min_new;
         int mode;
         if (!p.proc && !p.cout_n && !is_live) mode = MODE_SKIP;
         else if (identity) mode = MODE_FULL;
-        else if (step >= p.max_new - 1) mode = MODE_FORCED;
+        else if (step >= max_new - 1) mode = MODE_FORCED;
         else if (hf && step <= 0) mode = MODE_FULL;
         else mode = MODE_FILTER;
         int k = 0;
@@ -1359,6 +1362,8 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     p.min_keep = a->min_keep;
     p.min_new = a->min_new_tokens;
     p.max_new = a->max_new_tokens;
+    p.rminn = a->row_min_new_tokens;
+    p.rmaxn = a->row_max_new_tokens;
     p.rT = a->row_temperature;
     p.rP = a->row_top_p;
     p.rK = a->row_top_k;

@@ -44,7 +44,8 @@ void fill_args(b2s_sample_args& a, const Tensor& logits, const optional<Tensor>&
                const optional<Tensor>& row_top_k, const optional<Tensor>& alpha, const optional<Tensor>& status,
                double temperature, double top_p, int64_t top_k, int64_t min_keep, int64_t min_new, int64_t max_new,
                double presence, double frequency, int64_t eos, int64_t semantics, int64_t rng, int64_t max_top_k,
-               int64_t flags, int64_t cluster) {
+               int64_t flags, int64_t cluster, const optional<Tensor>& row_min_new = c10::nullopt,
+               const optional<Tensor>& row_max_new = c10::nullopt) {
     TORCH_CHECK(logits.is_cuda(), "logits must be a CUDA tensor (this engine has no CPU path)");
     TORCH_CHECK(logits.dim() == 2, "logits must be [rows, vocab]");
     TORCH_CHECK(logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kBFloat16,
@@ -76,6 +77,8 @@ void fill_args(b2s_sample_args& a, const Tensor& logits, const optional<Tensor>&
     a.row_temperature = opt_ptr<float>(row_temperature, at::kFloat, B, logits, "row_temperature");
     a.row_top_p = opt_ptr<float>(row_top_p, at::kFloat, B, logits, "row_top_p");
     a.row_top_k = opt_ptr<int32_t>(row_top_k, at::kInt, B, logits, "row_top_k");
+    a.row_min_new_tokens = opt_ptr<int64_t>(row_min_new, at::kLong, B, logits, "row_min_new");
+    a.row_max_new_tokens = opt_ptr<int64_t>(row_max_new, at::kLong, B, logits, "row_max_new");
     if (alpha.has_value() && alpha->defined()) {
         const Tensor& al = *alpha;
         TORCH_CHECK(al.is_cuda() && al.device() == logits.device() && al.scalar_type() == at::kFloat && al.is_contiguous(),
@@ -109,7 +112,8 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> sample_cuda(
     const Tensor& logits, const optional<Tensor>& history, const optional<Tensor>& steps, const optional<Tensor>& seeds,
     const optional<Tensor>& requests, const optional<Tensor>& uniform_values, const optional<Tensor>& active,
     const optional<Tensor>& finished, const optional<Tensor>& row_temperature, const optional<Tensor>& row_top_p,
-    const optional<Tensor>& row_top_k, const optional<Tensor>& alpha, const optional<Tensor>& status,
+    const optional<Tensor>& row_top_k, const optional<Tensor>& row_min_new, const optional<Tensor>& row_max_new,
+    const optional<Tensor>& alpha, const optional<Tensor>& status,
     double temperature, double top_p, int64_t top_k, int64_t min_keep, int64_t min_new, int64_t max_new,
     double presence, double frequency, int64_t eos, int64_t semantics, int64_t rng, int64_t max_top_k, int64_t flags,
     bool want_tokens, bool want_processed, bool want_state, int64_t cluster) {
@@ -117,7 +121,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> sample_cuda(
     b2s_sample_args a;
     fill_args(a, logits, history, steps, seeds, requests, uniform_values, active, finished, row_temperature, row_top_p,
               row_top_k, alpha, status, temperature, top_p, top_k, min_keep, min_new, max_new, presence, frequency, eos,
-              semantics, rng, max_top_k, flags, cluster);
+              semantics, rng, max_top_k, flags, cluster, row_min_new, row_max_new);
     const int64_t B = logits.size(0), V = logits.size(1);
     auto o64 = logits.options().dtype(at::kLong);
     Tensor tokens = want_tokens ? at::empty({B}, o64) : at::empty({0}, o64);
@@ -151,8 +155,9 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> sample_meta(
     const Tensor& logits, const optional<Tensor>& history, const optional<Tensor>&, const optional<Tensor>&,
     const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
     const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
-    const optional<Tensor>&, double, double, int64_t, int64_t, int64_t, int64_t, double, double, int64_t, int64_t,
-    int64_t, int64_t, int64_t, bool want_tokens, bool want_processed, bool want_state, int64_t) {
+    const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&, double, double, int64_t, int64_t,
+    int64_t, int64_t, double, double, int64_t, int64_t, int64_t, int64_t, int64_t, bool want_tokens,
+    bool want_processed, bool want_state, int64_t) {
     const int64_t B = logits.size(0), V = logits.size(1);
     auto o64 = logits.options().dtype(at::kLong);
     Tensor tokens = at::empty({want_tokens ? B : 0}, o64);
@@ -168,16 +173,17 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> sample_meta(
 Tensor sample_state_cuda(const Tensor& logits, Tensor& history, Tensor& steps, Tensor& finished,
                          const optional<Tensor>& seeds, const optional<Tensor>& uniform_values,
                          const optional<Tensor>& active, const optional<Tensor>& alpha, const optional<Tensor>& status,
-                         double temperature, double top_p, int64_t top_k, int64_t min_keep, int64_t min_new,
-                         int64_t max_new, int64_t eos, int64_t semantics, int64_t rng, int64_t max_top_k,
-                         int64_t cluster) {
+                         const optional<Tensor>& row_temperature, const optional<Tensor>& row_top_p,
+                         const optional<Tensor>& row_top_k, double temperature, double top_p, int64_t top_k,
+                         int64_t min_keep, int64_t min_new, int64_t max_new, int64_t eos, int64_t semantics, int64_t rng,
+                         int64_t max_top_k, int64_t cluster) {
     c10::cuda::CUDAGuard guard(logits.device());
     TORCH_CHECK(steps.is_contiguous() && finished.is_contiguous() && history.is_contiguous(),
                 "state tensors must be contiguous");
     TORCH_CHECK(finished.scalar_type() == at::kBool, "finished must be bool");
     b2s_sample_args a;
-    fill_args(a, logits, history, steps, seeds, c10::nullopt, uniform_values, active, finished, c10::nullopt,
-              c10::nullopt, c10::nullopt, alpha, status, temperature, top_p, top_k, min_keep, min_new, max_new, 0.0,
+    fill_args(a, logits, history, steps, seeds, c10::nullopt, uniform_values, active, finished, row_temperature,
+              row_top_p, row_top_k, alpha, status, temperature, top_p, top_k, min_keep, min_new, max_new, 0.0,
               0.0, eos, semantics, rng, max_top_k, 0, cluster);
     Tensor tokens = at::empty({logits.size(0)}, logits.options().dtype(at::kLong));
     a.tokens = tokens.data_ptr<int64_t>();
@@ -190,6 +196,7 @@ Tensor sample_state_cuda(const Tensor& logits, Tensor& history, Tensor& steps, T
 }
 
 Tensor sample_state_meta(const Tensor& logits, Tensor&, Tensor&, Tensor&, const optional<Tensor>&,
+                         const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
                          const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
                          const optional<Tensor>&, double, double, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
                          int64_t, int64_t, int64_t) {
@@ -337,15 +344,17 @@ TORCH_LIBRARY(minicpmo_sampler, m) {
     m.def(
         "sample(Tensor logits, Tensor? history, Tensor? steps, Tensor? seeds, Tensor? requests, "
         "Tensor? uniform_values, Tensor? active, Tensor? finished, Tensor? row_temperature, Tensor? row_top_p, "
-        "Tensor? row_top_k, Tensor? alpha, Tensor? status, float temperature, float top_p, int top_k, int min_keep, "
+        "Tensor? row_top_k, Tensor? row_min_new, Tensor? row_max_new, Tensor? alpha, Tensor? status, "
+        "float temperature, float top_p, int top_k, int min_keep, "
         "int min_new_tokens, int max_new_tokens, float presence_penalty, float frequency_penalty, int eos, "
         "int semantics, int rng, int max_top_k, int flags, bool want_tokens, bool want_processed, bool want_state, "
         "int cluster) -> (Tensor tokens, Tensor processed, Tensor history_out, Tensor steps_out, Tensor finished_out)");
     m.def(
         "sample_state_(Tensor logits, Tensor(a!) history, Tensor(b!) steps, Tensor(c!) finished, Tensor? seeds, "
-        "Tensor? uniform_values, Tensor? active, Tensor? alpha, Tensor? status, float temperature, float top_p, "
-        "int top_k, int min_keep, int min_new_tokens, int max_new_tokens, int eos, int semantics, int rng, "
-        "int max_top_k, int cluster) -> Tensor tokens");
+        "Tensor? uniform_values, Tensor? active, Tensor? alpha, Tensor? status, Tensor? row_temperature, "
+        "Tensor? row_top_p, Tensor? row_top_k, float temperature, float top_p, int top_k, int min_keep, "
+        "int min_new_tokens, int max_new_tokens, int eos, int semantics, int rng, int max_top_k, int cluster) "
+        "-> Tensor tokens");
     m.def("argmax(Tensor logits) -> Tensor");
     m.def("uniform(Tensor seeds, Tensor steps, Tensor? requests, int rng) -> Tensor");
     m.def("repetition_penalty(Tensor x, Tensor history, Tensor alpha) -> Tensor");

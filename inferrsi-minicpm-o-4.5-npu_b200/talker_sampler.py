@@ -70,6 +70,8 @@ class RowParams:
     top_k: Optional[torch.Tensor] = None        # int32
     repetition_penalty: Optional[Sequence[float]] = None
     max_top_k: int = 0                          # host bound on top_k (0: derived from the cfg / top_k list)
+    min_new_tokens: Optional[torch.Tensor] = None  # int64: EOS masked while steps < min_new_tokens
+    max_new_tokens: Optional[torch.Tensor] = None  # int64: EOS forced once steps >= max_new_tokens - 1
 
 
 # ---------------------------------------------------------------- helpers
@@ -130,9 +132,14 @@ def _run(logits, *, history=None, steps=None, seeds=None, requests=None, uniform
     return _native.ops().sample(
         logits, history, steps, seeds, requests, uniform_values, active, finished,
         None if rp is None else rp.temperature, None if rp is None else rp.top_p, None if rp is None else rp.top_k,
+        None if rp is None else _i64(rp.min_new_tokens), None if rp is None else _i64(rp.max_new_tokens),
         alpha, status, float(temperature), float(top_p), int(top_k), int(min_keep), int(min_new), int(max_new),
         float(presence), float(frequency), int(eos), int(semantics), int(rng), int(max_top_k), int(flags),
         bool(tokens), bool(processed), bool(state), int(cluster))
+
+
+def _i64(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    return None if t is None else t.to(torch.int64)
 
 
 def _cfg_kwargs(cfg: TalkerSampling, history: Optional[torch.Tensor], device, rp: Optional[RowParams] = None) -> dict:
@@ -355,8 +362,12 @@ def step_(state: DecodeState, logits: torch.Tensor, eos: int, cfg: TalkerSamplin
     return _native.ops().sample_state_(
         logits, state.history, state.steps, state.finished, state.seeds,
         None if uniform_values is None else uniform_values.to(torch.float32).contiguous(), state.active, kw["alpha"],
-        status, kw["temperature"], float(cfg.top_p), int(cfg.top_k), int(kw["min_keep"]), int(cfg.min_new_tokens),
-        int(cfg.max_new_tokens), int(eos), int(kw["semantics"]), r, int(kw["max_top_k"]), 0)
+        status, None, None, None, kw["temperature"], float(cfg.top_p), int(cfg.top_k), int(kw["min_keep"]),
+        int(cfg.min_new_tokens), int(cfg.max_new_tokens), int(eos), int(kw["semantics"]), r, int(kw["max_top_k"]), 0)
 
 
 FLAG_TOPK_ONLY = 2
+
+
+# the name the reference's captured graph bodies call (engine/runtime/talker_decode.py:29-31)
+processed_logits_static = processed_logits

@@ -61,7 +61,7 @@ class OrcBatch(ctypes.Structure):
         ("alpha_row_stride", ctypes.c_int32), ("row_temperature", ctypes.c_void_p), ("row_top_p", ctypes.c_void_p),
         ("row_top_k", ctypes.c_void_p), ("rng", ctypes.c_int32), ("threads", ctypes.c_int32),
         ("processed", ctypes.c_void_p), ("tokens", ctypes.c_void_p), ("meta", ctypes.c_void_p),
-        ("bad_history", ctypes.c_void_p),
+        ("bad_history", ctypes.c_void_p), ("row_min_new", ctypes.c_void_p), ("row_max_new", ctypes.c_void_p),
     ]
 
 
@@ -153,8 +153,8 @@ def _as_np(t, dtype=None):
 
 
 def sample(logits, history, steps, seeds, eos: int, cfg, *, uniforms=None, rng: int = RNG_COUNTER, requests=None,
-           penalties=None, row_temperature=None, row_top_p=None, row_top_k=None, want_processed: bool = True,
-           threads: int = 0):
+           penalties=None, row_temperature=None, row_top_p=None, row_top_k=None, row_min_new=None, row_max_new=None,
+           want_processed: bool = True, threads: int = 0):
     """processed_logits + draw for a batch.  ``logits``: [B, V] fp32 array, or bf16 given as a torch
     tensor / uint16 bit array.  ``penalties``: optional per-row repetition penalties.  Returns
     ``(processed [B,V] fp32 or None, tokens [B] int64, meta [B] structured, bad_history flag)``."""
@@ -193,6 +193,8 @@ def sample(logits, history, steps, seeds, eos: int, cfg, *, uniforms=None, rng: 
     rt = _as_np(row_temperature, np.float32).reshape(B) if row_temperature is not None else None
     rp = _as_np(row_top_p, np.float32).reshape(B) if row_top_p is not None else None
     rk = _as_np(row_top_k, np.int32).reshape(B) if row_top_k is not None else None
+    rmin = _as_np(row_min_new, np.int64).reshape(B) if row_min_new is not None else None
+    rmax = _as_np(row_max_new, np.int64).reshape(B) if row_max_new is not None else None
     processed = np.empty((B, V), np.float32) if want_processed else None
     tokens = np.empty(B, np.int64)
     meta = np.zeros(B, META_DTYPE)
@@ -201,7 +203,8 @@ def sample(logits, history, steps, seeds, eos: int, cfg, *, uniforms=None, rng: 
                  history_row_stride=W, steps=_ptr(steps_a), seeds=_ptr(seeds_a), requests=_ptr(req), uniforms=_ptr(uni),
                  alpha=_ptr(alpha), alpha_len=alen, alpha_row_stride=astride, row_temperature=_ptr(rt),
                  row_top_p=_ptr(rp), row_top_k=_ptr(rk), rng=rng, threads=threads, processed=_ptr(processed),
-                 tokens=_ptr(tokens), meta=_ptr(meta), bad_history=_ptr(bad))
+                 tokens=_ptr(tokens), meta=_ptr(meta), bad_history=_ptr(bad), row_min_new=_ptr(rmin),
+                 row_max_new=_ptr(rmax))
     c = _cfg_struct(cfg, V, W, eos)
     lib().orc_sample_batch(ctypes.byref(b), ctypes.byref(c))
     return processed, tokens, meta, bool(bad[0])

@@ -377,6 +377,8 @@ typedef struct {
     int64_t* tokens;        /* [rows] or NULL */
     orc_meta* meta;         /* [rows] or NULL */
     int32_t* bad_history;   /* out flag or NULL */
+    const int64_t* row_min_new; /* per-row min_new_tokens / max_new_tokens overrides or NULL */
+    const int64_t* row_max_new;
 } orc_batch;
 
 static inline float bf16_to_f(uint16_t b) { return f_from_bits((uint32_t)b << 16); }
@@ -410,6 +412,8 @@ int orc_sample_batch(const orc_batch* b, const orc_cfg* cfg) {
             if (b->row_temperature) c.temperature = b->row_temperature[r];
             if (b->row_top_p) c.top_p = b->row_top_p[r];
             if (b->row_top_k) c.top_k = b->row_top_k[r];
+            if (b->row_min_new) c.min_new = b->row_min_new[r];
+            if (b->row_max_new) c.max_new = b->row_max_new[r];
             orc_meta m;
             memset(&m, 0, sizeof(m));
             int32_t bh = 0;

@@ -310,6 +310,38 @@ def test_two_pass_top_p_filter_is_the_reference_form(pkg):
         assert bool((same | near).all())
 
 
+@pytest.mark.parametrize("sem", ["hf", "omni"])
+def test_per_row_min_max_new_tokens(pkg, sem):
+    """Per-row EOS rules (RowParams.min_new_tokens / max_new_tokens) == the oracle with the same per-row
+    values: rows before min_new have EOS masked, rows at max_new - 1 are forced to EOS."""
+    ts = pkg.talker_sampler
+    g = np.random.default_rng(21)
+    B, V, W, eos = 6, I.TALKER_V, 16, I.TALKER_V - 1
+    x = (g.standard_normal((B, V)) * 2.0).astype(np.float32)
+    x[:, eos] = 6.0  # EOS is likely whenever it is allowed
+    hist = g.integers(0, V, size=(B, W)).astype(np.int64)
+    steps = np.array([0, 3, 7, 10, 2040, 2046], np.int64)
+    rmin = np.array([8, 2, 8, 50, 0, 0], np.int64)
+    rmax = np.array([2048, 2048, 8, 12, 2048, 2047], np.int64)
+    u = g.random(B).astype(np.float32)
+    cfg = ts.TalkerSampling(semantics=sem, rng="counter", min_new_tokens=1, max_new_tokens=4096)
+    want_p, want_t, _, _ = orc.sample(x, hist, steps, np.arange(B), eos,
+                                      orc.Cfg(temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
+                                              repetition_penalty=cfg.repetition_penalty, window=W,
+                                              min_new_tokens=1, max_new_tokens=4096, min_keep=cfg.min_keep,
+                                              semantics=sem),
+                                      uniforms=u, row_min_new=rmin, row_max_new=rmax)
+    rp = ts.RowParams(min_new_tokens=torch.from_numpy(rmin).to(DEV), max_new_tokens=torch.from_numpy(rmax).to(DEV))
+    kw = ts._cfg_kwargs(cfg, torch.from_numpy(hist).to(DEV), DEV, rp)
+    got_t, got_p = ts._run(torch.from_numpy(x).to(DEV), history=torch.from_numpy(hist).to(DEV),
+                           steps=torch.from_numpy(steps).to(DEV), uniform_values=torch.from_numpy(u).to(DEV),
+                           eos=eos, rng=ts.RNG_UNIFORM, processed=True, **kw)[:2]
+    assert np.array_equal(got_t.cpu().numpy(), want_t)
+    assert len(H.compare_processed(want_p, got_p.cpu().numpy())) == 0
+    # the rules did apply: rows 2, 5 are forced to EOS, rows 0, 3 have EOS masked
+    assert want_t[2] == eos and want_t[5] == eos and want_t[0] != eos and want_t[3] != eos
+
+
 def test_status_flags_and_pad_rows(pkg):
     ts = pkg.talker_sampler
     cfg = ts.TalkerSampling(semantics="omni", rng="counter", min_new_tokens=0)

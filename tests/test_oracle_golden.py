@@ -102,3 +102,25 @@ def test_history_out_of_range_is_flagged():
     _, _, _, bad = orc.sample(case.logits, hist, case.steps, case.seeds, case.eos, H.oracle_cfg(case),
                               uniforms=case.uniforms)
     assert bad
+
+
+def test_per_row_min_max_new_equals_per_row_calls():
+    """The oracle's per-row min_new / max_new arrays == calling it row by row with scalar values."""
+    g = np.random.default_rng(4)
+    B, V, W, eos = 5, 300, 8, 299
+    x = (g.standard_normal((B, V)) * 2).astype(np.float32)
+    x[:, eos] = 5.0
+    hist = g.integers(0, V, size=(B, W)).astype(np.int64)
+    steps = np.array([0, 2, 5, 9, 14], np.int64)
+    rmin, rmax = np.array([3, 3, 0, 20, 0], np.int64), np.array([100, 3, 100, 100, 15], np.int64)
+    u = g.random(B).astype(np.float32)
+    for sem in ("hf", "omni"):
+        base = dict(temperature=0.9, top_p=0.9, top_k=40, repetition_penalty=1.1, window=W, min_keep=2, semantics=sem)
+        p_all, t_all, _, _ = orc.sample(x, hist, steps, None, eos, orc.Cfg(min_new_tokens=0, max_new_tokens=1, **base),
+                                        uniforms=u, row_min_new=rmin, row_max_new=rmax)
+        for r in range(B):
+            p_r, t_r, _, _ = orc.sample(x[r:r + 1], hist[r:r + 1], steps[r:r + 1], None, eos,
+                                        orc.Cfg(min_new_tokens=int(rmin[r]), max_new_tokens=int(rmax[r]), **base),
+                                        uniforms=u[r:r + 1])
+            assert t_r[0] == t_all[r]
+            assert np.array_equal(p_r[0].view(np.uint32), p_all[r].view(np.uint32))
