@@ -44,6 +44,10 @@ WORKLOADS = {
     # the single-stream Talker (one row, fp32, hf order, 16-token history)
     "talker1": dict(rows=1, vocab=6562, dtype="f32", window=16, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05,
                     order="hf", min_keep=3, eos=6561, min_new=0),
+    # vocabulary-sharded Thinker head -- each rank holds V / N contiguous columns; per-shard
+    # candidates, one NCCL all-gather, the merged draw on every rank.  Tie-heavy bf16 logits (multiples of 1/16)
+    "vocab_shard": dict(rows=256, vocab=151_936, dtype="bf16", window=0, temperature=0.8, top_k=64, top_p=0.9,
+                        penalty=1.0, op="vocab_shard"),
     # the Thinker greedy step (argmax over the head's logits, first index on ties) on the thinker shape
     "greedy": dict(rows=64, vocab=151_936, dtype="bf16", window=0, temperature=0.0, top_k=1, top_p=1.0, penalty=1.0,
                    op="argmax"),
@@ -62,6 +66,8 @@ def make_inputs(w, rows: int, seed: int):
     from tests.golden import inputs as I
 
     g = I.rng(seed)
+    if w.get("op") == "vocab_shard":
+        return I.quantised_rows(g, rows, w["vocab"], sigma=2.0, q=16), np.zeros((rows, 0), np.int64)
     if w["vocab"] == 151_936 and w["dtype"] == "bf16":
         logits, hist = I.zipf_rows(g, rows, w["vocab"], w["window"])
     elif w.get("order") == "hf":  # Talker: N(0, 2); several rows also get a per-row shift U(-1, 1)
@@ -205,6 +211,9 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
 
 
 def metric_of(w) -> str:
+    if w.get("op") == "vocab_shard":
+        return (f"sampled rows/s at B={w['rows']} x V={w['vocab']} over the job's vocabulary shards "
+                "(per-shard candidates + NCCL all-gather + merged draw)")
     if w.get("op") == "argmax":
         return f"greedy rows/s at B={w['rows']} x V={w['vocab']} per GPU (argmax, first index on ties)"
     return (f"sampled rows/s at B={w['rows']} x V={w['vocab']} per GPU "
@@ -234,6 +243,117 @@ def config_of(args, w, world: int) -> dict:
             "l2": f"{nbuf} rotating logits buffers ({nbuf * B * V * (2 if w['dtype'] == 'bf16' else 4) / 2**20:.0f}"
                   " MiB > L2)",
             "cuda_graph_steps": 0 if args.eager else min(args.steps, 1000)}
+
+
+def run_vocab_shard(args, w, rank: int, world: int, local: int):
+    """the same B rows on every rank, each rank holding a contiguous slice of the
+    vocabulary.  A step = shard candidates -> all-gather -> merged draw (identical tokens on every rank).
+    Timed eagerly (no CUDA graph holds the collective); whole-job rows/s, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    pkg = __graft_entry__.load_package()
+    vs, ths = pkg.vocab_shard, pkg.thinker_sampler
+    B, V = w["rows"], w["vocab"]
+    bounds = vs.shard_bounds(V, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    full, _ = make_inputs(w, B, 2024)  # the same rows on every rank
+    shard_bytes = B * (hi - lo) * 2
+    nbuf = max(2, min(4096, math.ceil(max(2 * L2_BYTES, 640 * 2**20) / shard_bytes)))
+    g = np.random.default_rng(7)  # the same row permutations on every rank
+    base = torch.from_numpy(full[:, lo:hi]).to(dev).to(torch.bfloat16)
+    bufs = [base[torch.from_numpy(g.permutation(B)).to(dev)].contiguous() for _ in range(nbuf)]
+    del base
+    cfg = ths.ThinkerSampling(temperature=w["temperature"], top_k=w["top_k"], top_p=w["top_p"], repetition_penalty=1.0,
+                              window=0, rng="philox")
+    cap = 1024  # per-shard list capacity: heavy ties at the shard's 64th value
+    steps = torch.ones(B, dtype=torch.int64, device=dev)
+    seeds = torch.arange(B, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def one_step(x):
+        v, i, n = vs.shard_candidates(x, lo, None, steps, cfg, cap=cap, status=status)
+        if world > 1:
+            vv, ii, nn = vs.exchange(v, i, n)
+        else:
+            vv, ii, nn = v[None], i[None], n[None]
+        return vs.merge_candidates(vv, ii, nn, V, steps, seeds, cfg, rng="philox", status=status)
+
+    for i in range(args.warmup):
+        one_step(bufs[i % nbuf])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(vis.split(",")[local].strip() if vis else local)
+    clocks.start()
+    time.sleep(0.1)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        one_step(bufs[i % nbuf])
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ck = clocks.stop()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ms_per_step = ms / args.steps
+    # end to end: the shard's logits from pinned host memory, the tokens back, every step
+    host = torch.from_numpy(full[:, lo:hi]).to(torch.bfloat16).pin_memory()
+    dbuf = torch.empty_like(host, device=dev)
+    tok_h = torch.empty(B, dtype=torch.int64).pin_memory()
+    e2e_steps = max(1, args.e2e_steps)
+    for _ in range(2):
+        dbuf.copy_(host, non_blocking=True)
+        tok_h.copy_(one_step(dbuf), non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record()
+    for _ in range(e2e_steps):
+        dbuf.copy_(host, non_blocking=True)
+        tok_h.copy_(one_step(dbuf), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    et = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    bad = int(status.item())
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    per_gpu_bytes = B * ((hi - lo) * 2 + 40)
+    peak, peak_kind = measured_peak_gbs()
+    achieved = per_gpu_bytes / (ms_per_step / 1e3) / 1e9
+    line = {
+        "metric": metric_of(w), "value": B * args.steps / (ms / 1e3), "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": dtype_of(w), "data": "synthetic",
+        "config": {**config_of(args, w, world), "parallelism": f"vocab x{world}", "shard_columns": hi - lo,
+                   "shard_list_cap": cap, "cuda_graph_steps": 0},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "bytes_per_gpu_step": per_gpu_bytes, "peak_source": peak_kind},
+        "e2e": {"value": B * e2e_steps / (float(et.item()) / 1e3), "unit": "rows/s",
+                "h2d_bytes_per_step": host.numel() * host.element_size(), "d2h_bytes_per_step": B * 8,
+                "steps": e2e_steps},
+        "gpu_launches": args.steps * 2, "clocks": ck, "status_flags": bad, "cpu_baseline": None,
+    }
+    print(json.dumps(line))
 
 
 def run_reference(args, w, rank: int):
@@ -267,6 +387,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, w, rank)
+    if w.get("op") == "vocab_shard":
+        return run_vocab_shard(args, w, rank, world, local)
 
     import torch
     import torch.distributed as dist
