@@ -55,6 +55,13 @@ __device__ __forceinline__ float okey_to_f(uint32_t k) {
 
 __device__ __forceinline__ float bf16_bits_to_f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
 
+// max(a, b) that returns NaN when either operand is NaN
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
 // ---------------------------------------------------------------- RNG
 
 __device__ __forceinline__ uint32_t mix32(uint32_t x) {
@@ -192,6 +199,28 @@ __device__ __forceinline__ double block_excl_scan(double v, double* red, double*
 #pragma unroll
     for (int i = 0; i < NWARP; ++i) {
         if (i < w) off += red[i];
+        tot += red[i];
+    }
+    *total = tot;
+    return off + incl - v;
+}
+
+// Exclusive scan of one int per thread in thread order; *total = sum.  red: NWARP + 1 shared ints.
+__device__ __forceinline__ int block_excl_scan_i(int v, int* red, int* total) {
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+    }
+    __syncthreads();
+    if (lane == 31) red[w] = incl;
+    __syncthreads();
+    int off = 0, tot = 0;
+#pragma unroll
+    for (int i = 0; i < NWARP; ++i) {
+        off += i < w ? red[i] : 0;
         tot += red[i];
     }
     *total = tot;

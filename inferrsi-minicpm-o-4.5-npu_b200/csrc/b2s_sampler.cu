@@ -86,9 +86,10 @@ struct Params {
     int64_t id_off;  // global id of column 0 of these rows (history ids are global)
     // geometry and shared-memory layout (bytes)
     int lcap, kbuf, nvals;
-    uint32_t ht_slots, bitwords;
-    uint32_t off_ctl, off_bits, off_ht, off_htv, off_hstage, off_atab, off_cand, off_candi, off_lst,
-        off_vals, off_hist, off_hraw, off_tmaxc;
+    int hcap;  // distinct history ids a row can hold (window + the censored EOS)
+    uint32_t bitwords;
+    uint32_t off_ctl, off_bits, off_pref, off_hcnt, off_hid, off_htv, off_smask, off_hstage, off_atab, off_cand,
+        off_candi, off_lst, off_vals, off_hist, off_hraw, off_tmaxc;
     int tmc_chunks;  // chunks whose per-thread maxima fit (rows with more take the exact path)
     uint32_t smem_total;
 };
@@ -123,6 +124,11 @@ struct Elem<float> {
         const uint32_t w = j == 0 ? q.x : j == 1 ? q.y : j == 2 ? q.z : q.w;
         return __uint_as_float(w);
     }
+    // maximum of the 4 elements, NaN if any is NaN
+    static __device__ __forceinline__ float vmax_nan(uint4 q) {
+        return fmax_nan(fmax_nan(__uint_as_float(q.x), __uint_as_float(q.y)),
+                        fmax_nan(__uint_as_float(q.z), __uint_as_float(q.w)));
+    }
     static constexpr uint32_t NEG = 0xff800000u;  // -inf in every element of a word
     static __device__ __forceinline__ void st_ninf(unsigned char* s) { *reinterpret_cast<uint32_t*>(s) = NEG; }
     template <int N>
@@ -151,6 +157,13 @@ struct Elem<__nv_bfloat16> {
     static __device__ __forceinline__ float at(uint4 q, int j) {
         const uint32_t w = (j >> 1) == 0 ? q.x : (j >> 1) == 1 ? q.y : (j >> 1) == 2 ? q.z : q.w;
         return __uint_as_float((j & 1) ? (w & 0xffff0000u) : (w << 16));
+    }
+    // maximum of the 8 elements, NaN if any is NaN (bf16 max is exact)
+    static __device__ __forceinline__ float vmax_nan(uint4 q) {
+        const __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&q.x), b = *reinterpret_cast<__nv_bfloat162*>(&q.y);
+        const __nv_bfloat162 c = *reinterpret_cast<__nv_bfloat162*>(&q.z), d = *reinterpret_cast<__nv_bfloat162*>(&q.w);
+        const __nv_bfloat162 m = __hmax2_nan(__hmax2_nan(a, b), __hmax2_nan(c, d));
+        return fmax_nan(__low2float(m), __high2float(m));
     }
     static constexpr uint32_t NEG = 0xff80ff80u;
     static __device__ __forceinline__ void st_ninf(unsigned char* s) { *reinterpret_cast<uint16_t*>(s) = (uint16_t)0xff80u; }
@@ -216,9 +229,8 @@ struct Row {
     const uint4* gvec;          // interior vector 0 in global memory
     int V, nh, nvec, e0;        // head elements [0, nh); interior vectors; first interior element e0 == nh
     const uint32_t* bits;       // history bitmap (nullptr: no history ids)
-    const uint32_t* ht;
-    const float* htv;
-    uint32_t slots;
+    const uint16_t* pref;       // per bitmap word: the history ids below the word (exclusive popcount prefix)
+    const float* htv;           // processed value of each distinct history id, by rank
     float T;
     bool identity;
     int censor;                 // element whose processed value is -inf regardless (omni censored EOS) or -1
@@ -234,9 +246,13 @@ struct Row {
         return b & ((1u << n) - 1u);
     }
     __device__ __forceinline__ float raw(int i) const { return Elem<E>::gld(rowp, i); }
+    // rank of a history id i among the row's distinct history ids (ascending id order)
+    __device__ __forceinline__ int rank(int i) const {
+        return (int)pref[i >> 5] + __popc(bits[i >> 5] & ((1u << (i & 31)) - 1u));
+    }
     // processed value of element i (history ids and the censored EOS carry their own value)
     __device__ __forceinline__ float P(int i, float x) const {
-        if (hbit(i)) return htv[ht_find(ht, slots, (uint32_t)i)];
+        if (hbit(i)) return htv[rank(i)];
         return f(x);
     }
     __device__ __forceinline__ uint4 vec(int v) const { return __ldg(gvec + v); }
@@ -441,8 +457,11 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     const int tid = threadIdx.x, lane = tid & 31;
     Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
     uint32_t* bits = reinterpret_cast<uint32_t*>(smem + p.off_bits);
-    uint32_t* ht = reinterpret_cast<uint32_t*>(smem + p.off_ht);
+    uint16_t* pref = reinterpret_cast<uint16_t*>(smem + p.off_pref);
+    uint32_t* hcnt = reinterpret_cast<uint32_t*>(smem + p.off_hcnt);  // occurrences of each distinct id, by rank
+    int* hid = reinterpret_cast<int*>(smem + p.off_hid);              // the id of each rank
     float* htv = reinterpret_cast<float*>(smem + p.off_htv);
+    unsigned long long* smask = reinterpret_cast<unsigned long long*>(smem + p.off_smask);  // [thread] chunk bits
     int64_t* hstage = reinterpret_cast<int64_t*>(smem + p.off_hstage);
     float* hraw = reinterpret_cast<float*>(smem + p.off_hraw);  // raw words of the history positions
     float* tmaxc = reinterpret_cast<float*>(smem + p.off_tmaxc);  // [chunk][thread] maximum of the pass 1
@@ -486,7 +505,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             q[it] = vl < vn ? ldg_stream(g + vl) : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
         }
     };
-    uint4 nq[ITS];           // the next chunk, in flight while the current one is processed
+    // Two register buffers in turn: chunk c + 1 is in flight while chunk c is processed.  They are named,
+    // never copied into one another, so a load that has not landed never stalls a register move.
+    uint4 nq[ITS], nq2[ITS];  // even / odd chunks
     bool next_row_in = false;  // nq already holds chunk 0 of this CTA's next row
 
     for (int r = blockIdx.x; r < p.rows; r += gridDim.x) {
@@ -499,6 +520,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         const int nchunks = (R.nvec + VPC - 1) / VPC;
         auto load_chunk = [&](int c, uint4* q) { load_chunk_of(R.gvec, R.nvec, c, q); };
         if (!next_row_in && nchunks > 0) load_chunk(0, nq);
+        if (nchunks > 1) load_chunk(1, nq2);
         next_row_in = false;
         if (tid == 0) ctl->err = 0;
 
@@ -541,13 +563,12 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         const bool censor = mode == MODE_FILTER && !hf && masked_eos;  // omni: EOS is -inf before anything else
         const bool use_ht = pen_hist || censor;
         R.bits = use_ht ? bits : nullptr;
-        R.ht = ht;
+        R.pref = pref;
         R.htv = htv;
-        R.slots = p.ht_slots;
         R.censor = censor ? p.eos : -1;
 
-        // ---------------- prologue: stage the history and the penalty table (asynchronous copies), hash the
-        // history ids, and fetch their raw values into registers (consumed after the stream)
+        // ---------------- prologue: stage the history and the penalty table (asynchronous copies); mark the
+        // history ids in a bitmap and in per-thread slice masks; rank the distinct ids and count them
         const bool stage_hist = hrow && p.W > 0 && (pen_hist || p.hist_out);
         if (stage_hist)
             for (int j = tid; j < p.W; j += NT) cp_async8(&hstage[j], &hrow[j]);
@@ -556,19 +577,21 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], &alpha[j]);
         if (use_ht) {
             for (uint32_t w = tid; w < p.bitwords; w += NT) bits[w] = 0;
-            for (uint32_t s = tid; s < p.ht_slots; s += NT) ht[s] = HT_EMPTY;
+            for (int d = tid; d < p.hcap; d += NT) hcnt[d] = 0u;
         }
-        // the ragged head (thread NT-1) and tail (thread NT-2) elements: at most 7 each (16-byte interior)
-        int edge_i[8];
-        float edge_x[8];
-        {
-            const int a0 = tid == NT - 1 ? 0 : R.e0 + R.nvec * EPV, a1 = tid == NT - 1 ? R.nh : V;
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-                const int i = a0 + t;
-                const bool has = tid >= NT - 2 && i < a1;
-                edge_i[t] = has ? i : -1;
-                edge_x[t] = has ? Elem<E>::gld(R.rowp, i) : 0.0f;
+        smask[tid] = 0ull;
+        // the elements outside the 16-byte interior, one per lane of the last warp's lanes 16..31: the head
+        // (at most 7) in lanes 16..23 and the tail (at most 7) in lanes 24..31 -- or, for a row with no
+        // interior vector (under 32 bytes, so at most 15 elements), the whole row in lanes 16..31
+        int edge_i = -1;
+        float edge_x = 0.0f;
+        if (tid >= NT - 16) {
+            const int t = tid - (NT - 16);
+            const bool whole = R.nvec == 0;
+            const int i = (whole || t < 8) ? t : R.e0 + R.nvec * EPV + (t - 8);
+            if ((!whole && t < 8) ? i < R.nh : i < V) {
+                edge_i = i;
+                edge_x = Elem<E>::gld(R.rowp, i);
             }
         }
         if (tid == 0) {
@@ -585,56 +608,55 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             const int64_t id = hv - p.id_off;
             return (hv >= 0 && id >= 0 && id < V) ? (int)id : -1;
         };
+        // interior element e lies in the pass-1 share of thread v % NT in chunk v / VPC (v: its vector)
+        auto mark_slice = [&](int e) {
+            const int rel = e - R.e0;
+            if (rel < 0) return;
+            const int v = rel / EPV;
+            if (v < R.nvec && v / VPC < 64) atomicOr(&smask[v % NT], 1ull << (v / VPC));
+        };
+        int hd = 0;  // distinct history ids of the row (the censored EOS included)
         if (use_ht) {
-            if (pen_hist) {
-                // HB positions per thread at a time, their probes interleaved (independent shared atomics); equal
-                // ids within a warp are counted once by their lowest lane (repeated tokens are the common case)
-                constexpr int HB = 4;
-                for (int j0 = 0; j0 < p.W; j0 += HB * NT) {
-                    int id[HB];
-                    uint32_t hs[HB], cnt[HB];
-                    bool todo[HB];
-#pragma unroll
-                    for (int u = 0; u < HB; ++u) {
-                        const int j = j0 + u * NT + tid;
-                        id[u] = j < p.W ? hist_id(j) : -1;
+            if (pen_hist)
+                for (int j = tid; j < p.W; j += NT) {
+                    const int id = hist_id(j);
+                    if (id < 0) {
                         // a vocabulary shard ignores ids of the other shards; an unsharded row flags ids >= vocab
-                        if (j < p.W && id[u] < 0 && hstage[j] >= 0 && !p.cout_n) set_status(p, B2S_STATUS_HISTORY_RANGE);
-                        const unsigned same = __match_any_sync(0xffffffffu, id[u]);
-                        cnt[u] = (uint32_t)__popc(same);
-                        todo[u] = id[u] >= 0 && lane == __ffs(same) - 1;
-                        hs[u] = todo[u] ? ht_slot((uint32_t)id[u], p.ht_slots) : 0u;
-                        if (todo[u]) atomicOr(&bits[id[u] >> 5], 1u << (id[u] & 31));
+                        if (hstage[j] >= 0 && !p.cout_n) set_status(p, B2S_STATUS_HISTORY_RANGE);
+                        continue;
                     }
-                    for (uint32_t probe = 0; probe < p.ht_slots; ++probe) {
-                        uint32_t cur[HB];
-#pragma unroll
-                        for (int u = 0; u < HB; ++u)
-                            cur[u] = todo[u] ? atomicCAS(&ht[hs[u]], HT_EMPTY, ((uint32_t)id[u] << HT_CNT_BITS) | cnt[u]) : 0u;
-                        bool any = false;
-#pragma unroll
-                        for (int u = 0; u < HB; ++u) {
-                            if (!todo[u]) continue;
-                            if (cur[u] == HT_EMPTY) {
-                                todo[u] = false;  // new slot with this warp's count
-                            } else if ((cur[u] >> HT_CNT_BITS) == (uint32_t)id[u]) {
-                                atomicAdd(&ht[hs[u]], cnt[u]);
-                                todo[u] = false;
-                            } else {
-                                hs[u] = (hs[u] + 1) & (p.ht_slots - 1);
-                                any = true;
-                            }
-                        }
-                        if (!any) break;
-                    }
+                    atomicOr(&bits[id >> 5], 1u << (id & 31));
+                    mark_slice(id);
                 }
-            }
             if (censor && tid == 0) {
-                ht_insert(ht, p.ht_slots, (uint32_t)p.eos, 0u);
                 atomicOr(&bits[p.eos >> 5], 1u << (p.eos & 31));
+                mark_slice(p.eos);
             }
+            __syncthreads();
+            // rank of an id = the distinct ids below it: exclusive prefix of the bitmap words' popcounts
+            const int wpt = ((int)p.bitwords + NT - 1) / NT;
+            const int w0 = min((int)p.bitwords, tid * wpt), w1 = min((int)p.bitwords, w0 + wpt);
+            int cnt = 0;
+            for (int w = w0; w < w1; ++w) cnt += __popc(bits[w]);
+            int base = block_excl_scan_i(cnt, ctl->red_i, &hd);
+            for (int w = w0; w < w1; ++w) {
+                pref[w] = (uint16_t)base;
+                base += __popc(bits[w]);
+            }
+            __syncthreads();
+            if (pen_hist)
+                for (int j = tid; j < p.W; j += NT) {
+                    const int id = hist_id(j);
+                    if (id < 0) continue;
+                    const int rk = R.rank(id);
+                    atomicAdd(&hcnt[rk], 1u);
+                    hid[rk] = id;  // every occurrence writes the same id
+                }
+            if (censor && tid == 0) hid[R.rank(p.eos)] = p.eos;
+            // hcnt / hid are read after the next barrier
+        } else {
+            __syncthreads();
         }
-        __syncthreads();
         // raw value of history position j: the aligned 4-byte word holding it, copied asynchronously into
         // hraw[j] (positions tid + u * NT, u < HPT, one per chunk so the gathers do not queue up together)
         const uintptr_t row_lo = reinterpret_cast<uintptr_t>(R.rowp), row_hi = row_lo + (uintptr_t)V * ES;
@@ -645,10 +667,8 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             const uintptr_t wa = (row_lo + (uintptr_t)id * ES) & ~(uintptr_t)3;
             if (wa >= row_lo && wa + 4 <= row_hi) cp_async4(&hraw[j], reinterpret_cast<const void*>(wa));
         };
-        // processed value of a hashed id with raw value x
-        auto hist_value = [&](uint32_t w, float x) {
-            const int id = (int)(w >> HT_CNT_BITS);
-            int n = (int)(w & ((1u << HT_CNT_BITS) - 1));
+        // processed value of history id `id`, seen n times, with raw value x
+        auto hist_value = [&](int id, int n, float x) {
             if (n >= p.alpha_len && n > 0) {
                 set_status(p, B2S_STATUS_COUNT_LIMIT);
                 n = p.alpha_len - 1;
@@ -718,41 +738,28 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         };
         static_assert(ITS >= 1 && ITS * NT == VPC, "whole vectors per thread per chunk");
         static_assert(ITS * EPV <= 32, "one mask bit per element of a thread's chunk share");
-        float tmax_nh = f_ninf();  // this thread's largest non-history value
+        // this thread's largest value over its chunk shares that hold no history id (a share that holds one
+        // is left out whole: the value stays a lower bound of a distinct non-history element)
+        float tmax_nh = f_ninf();
         if (cand_path) {
-            for (int c = 0; c < nchunks; ++c) {
+            const unsigned long long hmask = smask[tid];
+            auto pass1_chunk = [&](const uint4* q, int c) {
                 if (c < HPT) gather_hist(tid + c * NT);
-                const int vn = min(VPC, R.nvec - c * VPC);
-                const int cbase = R.e0 + c * VPC * EPV;
-                uint4 q[ITS];
-#pragma unroll
-                for (int it = 0; it < ITS; ++it) q[it] = nq[it];
-                if (c + 1 < nchunks) load_chunk(c + 1, nq);
                 const float vm = Elem<E>::template vmaxn<ITS>(q);
                 tmaxc[c * NT + tid] = vm;
-                if (vm > tmax_nh) {
-                    // this chunk may raise the thread's non-history maximum: leave the history ids out
-                    float m = f_ninf();
-#pragma unroll
-                    for (int it = 0; it < ITS; ++it) {
-                        const int vl = it * NT + tid;
-                        const uint32_t hb = vl < vn ? R.hbits(cbase + vl * EPV, EPV) : 0u;
-                        if (hb == 0u) {
-                            m = fmaxf(m, Elem<E>::vmax(q[it]));
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < EPV; ++j)
-                                if (!((hb >> j) & 1u)) m = fmaxf(m, Elem<E>::at(q[it], j));
-                        }
-                    }
-                    tmax_nh = fmaxf(tmax_nh, m);
+                if (!((hmask >> c) & 1ull)) tmax_nh = fmaxf(tmax_nh, vm);
+            };
+            // chunk c in nq (even) or nq2 (odd); each buffer is refilled right after its chunk is processed
+            for (int c = 0; c < nchunks; c += 2) {
+                pass1_chunk(nq, c);
+                if (c + 2 < nchunks) load_chunk(c + 2, nq);
+                if (c + 1 < nchunks) {
+                    pass1_chunk(nq2, c + 1);
+                    if (c + 3 < nchunks) load_chunk(c + 3, nq2);
                 }
             }
-            // the ragged head / tail (the last warp's lanes 30, 31)
-            if (tid >= NT - 2)
-#pragma unroll
-                for (int t = 0; t < 8; ++t)
-                    if (edge_i[t] >= 0 && !R.hbit(edge_i[t])) tmax_nh = fmaxf(tmax_nh, edge_x[t]);
+            // the ragged head / tail (one element in each of the last warp's lanes 16..31)
+            if (edge_i >= 0 && !R.hbit(edge_i)) tmax_nh = fmaxf(tmax_nh, edge_x);
             // the warp's jw largest per-thread maxima (distinct lanes): take the maximum out jw times
             const int jw = (k + NWARP - 1) / NWARP;
             float v = tmax_nh;
@@ -839,14 +846,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             }
             // the ragged head / tail
             if ((tid >> 5) == NWARP - 1) {
-                uint32_t em = 0u;
-#pragma unroll
-                for (int t = 0; t < 8; ++t)
-                    if (edge_i[t] >= 0 && edge_x[t] >= tau_low && !R.hbit(edge_i[t])) em |= 1u << t;
-                int pos = seg_reserve(__popc(em));
-#pragma unroll
-                for (int t = 0; t < 8; ++t)
-                    if ((em >> t) & 1u) place(edge_x[t], edge_i[t], pos++);
+                const bool eh = edge_i >= 0 && edge_x >= tau_low && !R.hbit(edge_i);
+                const int pos = seg_reserve(eh ? 1 : 0);
+                if (eh) place(edge_x, edge_i, pos);
             }
         }
         if (lane == 0) ctl->wcnt[tid >> 5] = wn;
@@ -865,11 +867,11 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 } else {
                     x = Elem<E>::gld(R.rowp, id);
                 }
-                const int sl = ht_find(ht, p.ht_slots, (uint32_t)id);
-                htv[sl] = hist_value(ht[sl], x);  // repeated ids write the same value
+                const int rk = R.rank(id);
+                htv[rk] = hist_value(id, (int)hcnt[rk], x);  // repeated ids write the same value
             }
         }
-        if (censor && tid == 0) htv[ht_find(ht, p.ht_slots, (uint32_t)p.eos)] = f_ninf();  // omni: EOS is -inf
+        if (censor && tid == 0) htv[R.rank(p.eos)] = f_ninf();  // omni: EOS is -inf
         __syncthreads();
         const bool row_err = ctl->err != 0;
         if (cand_path && !ovf)
@@ -921,13 +923,12 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             }
             if (use_ht) {
                 const float p_low = R.f(tl);
-                for (uint32_t sl = tid; sl < p.ht_slots; sl += NT) {
-                    const uint32_t w = ht[sl];
-                    if (w != HT_EMPTY && htv[sl] >= p_low) {
+                for (int d = tid; d < hd; d += NT) {
+                    if (htv[d] >= p_low) {
                         const int pos = atomicAdd(&ctl->kn, 1);
                         if (pos < p.lcap) {
-                            kv[pos] = htv[sl];
-                            ki[pos] = (int)(w >> HT_CNT_BITS);
+                            kv[pos] = htv[d];
+                            ki[pos] = hid[d];
                         }
                     }
                 }
@@ -1145,22 +1146,55 @@ __global__ void __launch_bounds__(NT, 2) argmax_kernel(const void* logits, int V
             const uint4* vp = reinterpret_cast<const uint4*>(Ace);
             const int nv = (int)((Bfl - Ace) / 16);
             const int i0 = lo + nh;
-            // 4 loads in flight per thread, then their elements in index order (per thread, increasing v)
-            for (int v0 = 0; v0 < nv; v0 += 4 * NT) {
-                uint4 q[4];
+            // Per vector only its NaN-propagating maximum; the thread keeps the first vector holding its best
+            // value (NaN first, then larger; an equal later vector never replaces it) and finds the element in
+            // it at the end.  Vectors of a thread come in increasing index order.
+            constexpr int U = 4, STEP = U * NT;
+            float vb = f_ninf();
+            int vbi = -1;
+            uint4 bq = make_uint4(0u, 0u, 0u, 0u);
+            auto ld = [&](int v0, uint4* q) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < U; ++u) {
                     const int v = v0 + u * NT + tid;
-                    q[u] = v < nv ? ldg_stream(vp + v) : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
+                    q[u] = v < nv ? ldg_stream(vp + v) : make_uint4(0u, 0u, 0u, 0u);
                 }
+            };
+            auto scan = [&](const uint4* q, int v0) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < U; ++u) {
                     const int v = v0 + u * NT + tid;
                     if (v < nv) {
-#pragma unroll
-                        for (int j = 0; j < 16 / ES; ++j) upd(Elem<E>::at(q[u], j), i0 + v * (16 / ES) + j);
+                        const float vm = Elem<E>::vmax_nan(q[u]);
+                        if (vbi < 0 || vm > vb || (vm != vm && vb == vb)) {
+                            vb = vm;
+                            vbi = v;
+                            bq = q[u];
+                        }
                     }
                 }
+            };
+            // two register buffers in turn: one in flight while the other is scanned
+            uint4 qa[U], qb[U];
+            if (nv > 0) ld(0, qa);
+            if (nv > STEP) ld(STEP, qb);
+            for (int v0 = 0; v0 < nv; v0 += 2 * STEP) {
+                scan(qa, v0);
+                if (v0 + 2 * STEP < nv) ld(v0 + 2 * STEP, qa);
+                if (v0 + STEP < nv) {
+                    scan(qb, v0 + STEP);
+                    if (v0 + 3 * STEP < nv) ld(v0 + 3 * STEP, qb);
+                }
+            }
+            if (vbi >= 0) {
+                const bool want_nan = vb != vb;
+                int jb = 16 / ES - 1;
+#pragma unroll
+                for (int j = 16 / ES - 1; j >= 0; --j) {
+                    const float x = Elem<E>::at(bq, j);
+                    if (want_nan ? x != x : x == vb) jb = j;
+                }
+                upd(Elem<E>::at(bq, jb), i0 + vbi * (16 / ES) + jb);
             }
         } else {
             for (int i = lo + tid; i < hi; i += NT) upd(Elem<E>::gld(rowp, i), i);
@@ -1401,18 +1435,24 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     p.kbuf = kmax;
     p.nvals = next_pow2(kmax) > 2 * KFAST ? next_pow2(kmax) : 2 * KFAST;
     const bool hashed = !identity && (a->window > 0 || (a->eos >= 0 && a->eos < a->vocab));
-    const int hist_ids = (a->window < a->vocab ? a->window : a->vocab) + 1;
-    p.ht_slots = hashed ? (uint32_t)next_pow2(hist_ids + hist_ids / 4 + 1 > 32 ? hist_ids + hist_ids / 4 + 1 : 32) : 0u;
+    const int hist_ids = (a->window < a->vocab ? a->window : a->vocab) + 1;  // distinct ids: window + EOS
+    p.hcap = hashed ? hist_ids : 0;
     p.bitwords = hashed ? (uint32_t)((a->vocab + 31) / 32) : 0u;
     uint32_t off = 0;
     p.off_ctl = off;
     off = align_up(off + (uint32_t)sizeof(Ctl), 128);
     p.off_bits = off;
     off = align_up(off + p.bitwords * 4, 16);
-    p.off_ht = off;
-    off = align_up(off + p.ht_slots * 4, 16);
+    p.off_pref = off;  // 16-bit ranks: hcap <= 2^13 + 1
+    off = align_up(off + p.bitwords * 2, 16);
+    p.off_hcnt = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_hid = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
     p.off_htv = off;
-    off = align_up(off + p.ht_slots * 4, 16);
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_smask = off;
+    off = align_up(off + NT * 8, 16);
     p.off_hraw = off;  // the 4-byte word holding the raw value of each of the first 4 * NT history positions
     off = align_up(off + (uint32_t)(identity ? 0 : (a->window < 4 * NT ? a->window : 4 * NT)) * 4, 16);
     p.off_hstage = off;

@@ -143,6 +143,18 @@ def test_argmax_matches_reference(pkg):
     z = torch.randn(2, 1000, device=DEV)
     z[1, 17] = float("nan")
     assert am(z)[1].item() == 17
+    # NaN in several threads' shares, rows of -inf, signed zeros, one value everywhere: first index wins
+    w = torch.randn(6, I.THINKER_V)
+    w[0, [90_001, 40_000, 151_000]] = float("nan")
+    w[1] = float("-inf")
+    w[2] = 0.0
+    w[2, ::3] = -0.0
+    w[3] = 2.5
+    w[4, 5000:] = 7.0
+    w[5, [151_935, 70_000]] = 1e30
+    for dt in (torch.float32, torch.bfloat16):
+        wd = w.to(dt)
+        assert torch.equal(am(wd.to(DEV)).cpu(), wd.float().argmax(-1))
 
 
 def test_sequences_match_reference(pkg):
@@ -340,6 +352,26 @@ def test_per_row_min_max_new_tokens(pkg, sem):
     assert len(H.compare_processed(want_p, got_p.cpu().numpy())) == 0
     # the rules did apply: rows 2, 5 are forced to EOS, rows 0, 3 have EOS masked
     assert want_t[2] == eos and want_t[5] == eos and want_t[0] != eos and want_t[3] != eos
+
+
+@pytest.mark.parametrize("sem", ["hf", "omni"])
+def test_short_rows_head_and_tail_elements(pkg, sem):
+    """Rows of 9..40 bf16 elements stored back to back, so that they start at every 2-byte offset: rows
+    with no 16-byte interior vector at all, and rows with a ragged head and tail around one or two."""
+    ts = pkg.talker_sampler
+    g = I.rng(77)
+    for V in (9, 13, 15, 20, 33, 40):
+        for top_k in (1, 3):
+            B = 16
+            logits = (g.standard_normal((B, V)) * 2).astype(np.float32)
+            hist = g.integers(0, V, size=(B, 6))
+            cfg = C._cfg(semantics=sem, top_k=top_k, top_p=0.9, window=6, min_new_tokens=0, min_keep=1)
+            case = C._case(f"short_{V}_{top_k}", logits, "bf16", hist, np.full(B, 3), -1, cfg, 90 + V)
+            want_p, want_t, _, _ = H.run_oracle(case)
+            got_p, got_t, status = run_gpu(ts, case)
+            assert status == 0
+            assert len(H.compare_processed(want_p, got_p)) == 0, (V, top_k)
+            assert np.array_equal(got_t, want_t), (V, top_k, got_t, want_t)
 
 
 def test_status_flags_and_pad_rows(pkg):
