@@ -95,13 +95,12 @@ struct Params {
 };
 
 struct Ctl {
-    int cand_n, err, gather_n, kn;
+    int err, gather_n, kn;
     int wcnt[NWARP];  // candidates each warp pushed into its segment of the list
     uint32_t rctl[2];
     uint32_t klo, kcnt;
     float thr;
     float u;
-    uint32_t tau_key;             // okey of the stream threshold (raised with atomicMax)
     double red_d[NWARP + 1];
     float red_f[NWARP + 1];
     int red_i[NWARP + 1];
@@ -523,6 +522,15 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         if (nchunks > 1) load_chunk(1, nq2);
         next_row_in = false;
         if (tid == 0) ctl->err = 0;
+        // the history and the penalty table, asynchronously, before the row's parameters are known (a row that
+        // turns out not to need them just does not read them)
+        const int64_t* hrow = p.hist ? p.hist + (int64_t)r * p.hstride : nullptr;
+        const float* alpha = p.alpha ? p.alpha + (int64_t)r * p.alpha_stride : nullptr;
+        if (hrow && p.W > 0) {
+            for (int j = tid; j < p.W; j += NT) cp_async8(&hstage[j], &hrow[j]);
+            if (alpha)
+                for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], &alpha[j]);
+        }
 
         // ---------------- row parameters and mode (global loads overlap the stream)
         const int64_t step = p.steps ? p.steps[r] : 0;
@@ -558,7 +566,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         }
         R.T = T;
         R.identity = identity;
-        const int64_t* hrow = p.hist ? p.hist + (int64_t)r * p.hstride : nullptr;
         const bool pen_hist = mode == MODE_FILTER && p.W > 0 && hrow != nullptr;
         const bool censor = mode == MODE_FILTER && !hf && masked_eos;  // omni: EOS is -inf before anything else
         const bool use_ht = pen_hist || censor;
@@ -567,14 +574,8 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         R.htv = htv;
         R.censor = censor ? p.eos : -1;
 
-        // ---------------- prologue: stage the history and the penalty table (asynchronous copies); mark the
-        // history ids in a bitmap and in per-thread slice masks; rank the distinct ids and count them
-        const bool stage_hist = hrow && p.W > 0 && (pen_hist || p.hist_out);
-        if (stage_hist)
-            for (int j = tid; j < p.W; j += NT) cp_async8(&hstage[j], &hrow[j]);
-        const float* alpha = p.alpha ? p.alpha + (int64_t)r * p.alpha_stride : nullptr;
-        if (pen_hist && alpha)
-            for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], &alpha[j]);
+        // ---------------- prologue: once the staged history has landed, mark its ids in a bitmap and in
+        // per-thread slice masks; rank the distinct ids and count them
         if (use_ht) {
             for (uint32_t w = tid; w < p.bitwords; w += NT) bits[w] = 0;
             for (int d = tid; d < p.hcap; d += NT) hcnt[d] = 0u;
@@ -595,8 +596,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             }
         }
         if (tid == 0) {
-            ctl->cand_n = 0;
-            ctl->tau_key = 0u;
             ctl->thr = f_ninf();
             ctl->red_u[0] = 0u;
         }
@@ -696,7 +695,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                                T >= 1e-6f && T <= 1e6f && nchunks <= p.tmc_chunks;
         bool ovf = !cand_path;
         float tau_low = f_inf();
-        uint32_t tau_key = 0u;  // okey(tau_low)
         auto margin = [](float t) { return t - fmaxf(fabsf(t) * 9.5367431640625e-7f, 1e-30f); };
         // Each warp appends to its own segment of the candidate list (seg entries at cand_v + warp * seg), with
         // a warp-uniform count in a register: no returning atomic.
@@ -802,9 +800,31 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 ovf = true;
             } else {
                 tau_low = margin(t0);
-                tau_key = okey(tau_low);
             }
         }
+        // processed values of the history ids (hcnt and the raw values gathered during pass 1)
+        auto compute_htv = [&]() {
+            if (pen_hist) {
+                for (int u = nchunks; u < HPT; ++u) gather_hist(tid + u * NT);  // short rows
+                cp_async_wait_all();  // this thread's copies
+                for (int j = tid; j < p.W; j += NT) {
+                    const int id = hist_id(j);
+                    if (id < 0) continue;
+                    const uintptr_t ea = row_lo + (uintptr_t)id * ES, wa = ea & ~(uintptr_t)3;
+                    float x;
+                    if (j < HPT * NT && wa >= row_lo && wa + 4 <= row_hi) {
+                        const uint32_t w = __float_as_uint(hraw[j]);
+                        x = ES == 4 ? __uint_as_float(w) : bf16_bits_to_f((uint16_t)(w >> (8 * (unsigned)(ea - wa))));
+                    } else {
+                        x = Elem<E>::gld(R.rowp, id);
+                    }
+                    const int rk = R.rank(id);
+                    htv[rk] = hist_value(id, (int)hcnt[rk], x);  // repeated ids write the same value
+                }
+            }
+            if (censor && tid == 0) htv[R.rank(p.eos)] = f_ninf();  // omni: EOS is -inf
+        };
+        bool htv_done = false;
         if (cand_path && !ovf) {
             // pass 2: each thread re-reads (from L2) its chunks whose maximum clears tau, two at a time so that
             // most threads wait for one round trip
@@ -830,19 +850,29 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                     }
                 }
             };
-            while (__any_sync(0xffffffffu, hits != 0ull)) {
-                const int c1 = hits ? __ffsll((long long)hits) - 1 : -1;
+            // the first round's loads go out, the history values are computed while they are in flight
+            auto next_hit = [&]() {
+                const int c = hits ? __ffsll((long long)hits) - 1 : -1;
                 if (hits) hits &= hits - 1ull;
-                const int c2 = hits ? __ffsll((long long)hits) - 1 : -1;
-                if (hits) hits &= hits - 1ull;
-                uint4 q1[ITS], q2[ITS];
-                load_at(c1, q1);
-                load_at(c2, q2);
+                return c;
+            };
+            int c1 = next_hit(), c2 = next_hit();
+            uint4 q1[ITS], q2[ITS];
+            load_at(c1, q1);
+            load_at(c2, q2);
+            compute_htv();
+            htv_done = true;
+            for (;;) {
                 const uint32_t h1 = c1 >= 0 ? hit_mask(q1, R.e0 + c1 * VPC * EPV) : 0u;
                 const uint32_t h2 = c2 >= 0 ? hit_mask(q2, R.e0 + c2 * VPC * EPV) : 0u;
                 const int pos = seg_reserve(__popc(h1) + __popc(h2));
                 if (h1) place_all(q1, h1, R.e0 + c1 * VPC * EPV, pos);
                 if (h2) place_all(q2, h2, R.e0 + c2 * VPC * EPV, pos + __popc(h1));
+                if (!__any_sync(0xffffffffu, hits != 0ull)) break;
+                c1 = next_hit();
+                c2 = next_hit();
+                load_at(c1, q1);
+                load_at(c2, q2);
             }
             // the ragged head / tail
             if ((tid >> 5) == NWARP - 1) {
@@ -851,27 +881,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 if (eh) place(edge_x, edge_i, pos);
             }
         }
+        if (!htv_done) compute_htv();
         if (lane == 0) ctl->wcnt[tid >> 5] = wn;
-        // processed values of the history ids
-        if (pen_hist) {
-            for (int u = nchunks; u < HPT; ++u) gather_hist(tid + u * NT);  // short rows
-            cp_async_wait_all();  // this thread's copies
-            for (int j = tid; j < p.W; j += NT) {
-                const int id = hist_id(j);
-                if (id < 0) continue;
-                const uintptr_t ea = row_lo + (uintptr_t)id * ES, wa = ea & ~(uintptr_t)3;
-                float x;
-                if (j < HPT * NT && wa >= row_lo && wa + 4 <= row_hi) {
-                    const uint32_t w = __float_as_uint(hraw[j]);
-                    x = ES == 4 ? __uint_as_float(w) : bf16_bits_to_f((uint16_t)(w >> (8 * (unsigned)(ea - wa))));
-                } else {
-                    x = Elem<E>::gld(R.rowp, id);
-                }
-                const int rk = R.rank(id);
-                htv[rk] = hist_value(id, (int)hcnt[rk], x);  // repeated ids write the same value
-            }
-        }
-        if (censor && tid == 0) htv[R.rank(p.eos)] = f_ninf();  // omni: EOS is -inf
+        if (tid == 0) ctl->kn = 0;  // the candidate count of the compaction below
         __syncthreads();
         const bool row_err = ctl->err != 0;
         if (cand_path && !ovf)
@@ -906,12 +918,14 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
 
         // ---------------- candidate list: the items >= the final tau (processed), plus the history ids whose
         // processed value clears f(tau)
+        // (compacted into kv / ki, which then hold the list; cand_v / cand_i become scratch)
         int n = 0;
+        float* cv = kv;
+        int* ci = ki;
+        float* xv = cand_v;
+        int* xi = cand_i;
         if (cand_path && !ovf && !row_err) {
-            const uint32_t tk = max(tau_key, ctl->tau_key);
-            const float tl = okey_to_f(tk);
-            if (tid == 0) ctl->kn = 0;
-            __syncthreads();
+            const float tl = tau_low;
             for (int i = tid; i < p.lcap; i += NT) {
                 if (i % seg < ctl->wcnt[i / seg] && cand_v[i] >= tl) {
                     const int pos = atomicAdd(&ctl->kn, 1);
@@ -935,12 +949,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             }
             __syncthreads();
             n = ctl->kn;
-            if (n <= p.lcap)
-                for (int i = tid; i < n; i += NT) {
-                    cand_v[i] = kv[i];
-                    cand_i[i] = ki[i];
-                }
-            __syncthreads();
             if (n > p.lcap || n < k) ovf = true;
         }
 
@@ -948,7 +956,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             // full-row logsumexp of the penalised values (talker_sampler.py:112); the row maximum is a candidate
             float lm = f_ninf();
             if (cand_path && !ovf) {
-                for (int i = tid; i < n; i += NT) lm = fmaxf(lm, cand_v[i]);
+                for (int i = tid; i < n; i += NT) lm = fmaxf(lm, cv[i]);
             } else {
                 row_visit<E>(R, [&](int i, float x) { lm = fmaxf(lm, R.P(i, x)); });
             }
@@ -963,42 +971,47 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         if (cand_path && !ovf && !row_err) {
             if (n > 256) {
                 // narrow to the items >= the k-th largest processed value (ties kept)
-                const uint32_t kk = kth_key_bucket(n, k, [&](int i) { return okey(cand_v[i]); }, hist, ctl);
+                const uint32_t kk = kth_key_bucket(n, k, [&](int i) { return okey(cv[i]); }, hist, ctl);
                 if (tid == 0) ctl->kn = 0;
                 __syncthreads();
                 for (int i = tid; i < n; i += NT)
-                    if (okey(cand_v[i]) >= kk) {
+                    if (okey(cv[i]) >= kk) {
                         const int pos = atomicAdd(&ctl->kn, 1);
-                        kv[pos] = cand_v[i];
-                        ki[pos] = cand_i[i];
+                        xv[pos] = cv[i];
+                        xi[pos] = ci[i];
                     }
                 __syncthreads();
                 n = ctl->kn;
-                for (int i = tid; i < n; i += NT) { cand_v[i] = kv[i]; cand_i[i] = ki[i]; }
-                __syncthreads();
+                // the narrowed list is the list now; the old one is scratch
+                float* tv = cv;
+                int* ti = ci;
+                cv = xv;
+                ci = xi;
+                xv = tv;
+                xi = ti;
             }
             exact = false;
             if (p.cout_n) {
                 // vocabulary shard: every candidate >= this shard's k-th value
-                list_topk_values(cand_v, n, k, vals, sc);
+                list_topk_values(cv, n, k, vals, sc);
                 const float kth = vals[k - 1];
                 if (tid == 0) ctl->kn = 0;
                 __syncthreads();
                 for (int i = tid; i < n; i += NT) {
-                    if (cand_v[i] >= kth) {
+                    if (cv[i] >= kth) {
                         const int pos = atomicAdd(&ctl->kn, 1);
                         if (pos < p.ccap) {
-                            p.cout_v[(int64_t)r * p.ccap + pos] = cand_v[i];
-                            p.cout_i[(int64_t)r * p.ccap + pos] = (int32_t)(cand_i[i] + p.id_off);
+                            p.cout_v[(int64_t)r * p.ccap + pos] = cv[i];
+                            p.cout_i[(int64_t)r * p.ccap + pos] = (int32_t)(ci[i] + p.id_off);
                         }
                     }
                 }
                 __syncthreads();
                 if (tid == 0) p.cout_n[r] = ctl->kn;
             } else {
-                thr = list_threshold(cand_v, n, k, hf, lse, top_p, p.min_keep, topk_only, vals, sc);
+                thr = list_threshold(cv, n, k, hf, lse, top_p, p.min_keep, topk_only, vals, sc);
                 if (wants_draw)
-                    token = list_draw(cand_v, cand_i, n, thr, (hf && masked_eos) ? p.eos : -1, ctl->u, V, kv, ki, sv,
+                    token = list_draw(cv, ci, n, thr, (hf && masked_eos) ? p.eos : -1, ctl->u, V, xv, xi, sv,
                                       si, sc);
             }
         }
