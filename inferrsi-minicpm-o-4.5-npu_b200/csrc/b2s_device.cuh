@@ -16,13 +16,13 @@ constexpr int NWARP = NT / 32;
 // exp(x) in fp32: n = rint(x*log2 e), r = x - n*ln2 by a two-constant Cody-Waite reduction, exp(r) by its
 // Taylor series to degree 7 in FMA Horner form, then scaled by exact powers of two.  Every operation is
 // an explicitly rounded fp32 op, so the CPU oracle (same sequence, -ffp-contract=off) gives the same bits.
+// Written without branches (the special cases are selected at the end, the reduction runs on x clamped to
+// [-104, 89], where it is the same sequence as for every in-range x) so that independent calls interleave.
 __device__ __forceinline__ float b2s_expf(float x) {
-    if (x != x) return x;
-    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
-    if (x < -103.97208404541015625f) return 0.0f;
-    float t = __fmul_rn(x, 1.44269502162933349609375f);
-    float n = rintf(t);
-    float r = __fmaf_rn(n, -0.693145751953125f, x);
+    const float xc = fminf(fmaxf(x, -104.0f), 89.0f);
+    const float t = __fmul_rn(xc, 1.44269502162933349609375f);
+    const float n = rintf(t);
+    float r = __fmaf_rn(n, -0.693145751953125f, xc);
     r = __fmaf_rn(n, -1.428606765330187045037746429443359375e-6f, r);
     float p = 1.98412701138295233249664306640625e-4f;
     p = __fmaf_rn(p, r, 1.3888889225199818611145019531250e-3f);
@@ -32,10 +32,15 @@ __device__ __forceinline__ float b2s_expf(float x) {
     p = __fmaf_rn(p, r, 0.5f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    int ni = (int)n;
-    if (ni > 127) { p = __fmul_rn(p, 2.0f); ni -= 1; }
-    if (ni < -126) { p = __fmul_rn(p, 5.42101086242752217003726400434970855712890625e-20f); ni += 64; }
-    return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+    int ni = (int)n;  // [-150, 128] for x in range
+    const bool hi = ni > 127, lo = ni < -126;
+    p = hi ? __fmul_rn(p, 2.0f) : p;
+    p = lo ? __fmul_rn(p, 5.42101086242752217003726400434970855712890625e-20f) : p;
+    ni = hi ? ni - 1 : (lo ? ni + 64 : ni);
+    float res = __fmul_rn(p, __uint_as_float((uint32_t)(ni + 127) << 23));
+    res = x < -103.97208404541015625f ? 0.0f : res;
+    res = x > 88.72283935546875f ? __int_as_float(0x7f800000) : res;
+    return x != x ? x : res;
 }
 
 __device__ __forceinline__ float f_inf() { return __int_as_float(0x7f800000); }

@@ -29,10 +29,22 @@ struct Scr {
 __device__ __forceinline__ void list_topk_values(const float* cv, int n, int k, float* vals, const Scr& sc) {
     const int tid = threadIdx.x;
     if (n <= 2 * NT) {
+        // cv is 16-byte aligned: four items per shared load, several loads in flight
+        const float4* c4 = reinterpret_cast<const float4*>(cv);
+        const int n4 = n >> 2;
         for (int i = tid; i < n; i += NT) {
             const float vi = cv[i];
             int rank = 0;
-            for (int j = 0; j < n; ++j) {
+#pragma unroll 4
+            for (int j4 = 0; j4 < n4; ++j4) {
+                const float4 v = c4[j4];
+                const int j = 4 * j4;
+                rank += (v.x > vi) | ((v.x == vi) & (j < i));
+                rank += (v.y > vi) | ((v.y == vi) & (j + 1 < i));
+                rank += (v.z > vi) | ((v.z == vi) & (j + 2 < i));
+                rank += (v.w > vi) | ((v.w == vi) & (j + 3 < i));
+            }
+            for (int j = 4 * n4; j < n; ++j) {
                 const float vj = cv[j];
                 rank += (vj > vi) | ((vj == vi) & (j < i));
             }
@@ -218,6 +230,63 @@ __device__ __forceinline__ int64_t list_draw(const float* cv, const int* ci, int
     int best = 0x7fffffff;
     for (int w = 0; w < NWARP; ++w) best = min(best, sc.red_i[w]);
     return best == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)si[best];
+}
+
+// The whole list stage: top-k values, top-p threshold (returned in thr_out) and, when `draw`, the token.
+// Warp 0 takes the threshold and, when at most KLIST items are kept, the draw as well -- compaction by
+// ballot, vocabulary order by ranking the (distinct) kept ids, the same inverse-CDF draw as list_draw --
+// with no block barrier in between; more kept items (heavy ties at the threshold) go to list_draw.
+// cv must be 16-byte aligned.  Result in every thread.
+__device__ __forceinline__ int64_t list_sample(const float* cv, const int* ci, int n, int k, bool hf, float lse,
+                                               float top_p, int min_keep, bool topk_only, bool draw, int drop_id,
+                                               float u, int V, float* vals, float* kv, int* ki, float* sv, int* si,
+                                               const Scr& sc, float& thr_out) {
+    constexpr int FALLBACK = -2;
+    list_topk_values(cv, n, k, vals, sc);
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const float t = warp_topp_threshold(vals, k, hf, lse, top_p, min_keep, topk_only);
+        int res = 0x7fffffff;
+        if (draw) {
+            int kn = 0;
+            for (int i0 = 0; i0 < n; i0 += 32) {
+                const int i = i0 + lane;
+                const bool keep = i < n && cv[i] >= t && ci[i] != drop_id;
+                const unsigned m = __ballot_sync(0xffffffffu, keep);
+                const int pos = kn + __popc(m & ((1u << lane) - 1u));
+                if (keep && pos < KLIST) {
+                    kv[pos] = cv[i];
+                    ki[pos] = ci[i];
+                }
+                kn += __popc(m);
+            }
+            if (kn <= KLIST) {
+                __syncwarp();
+                for (int a = lane; a < kn; a += 32) {
+                    const int id = ki[a];
+                    int rank = 0;
+#pragma unroll 4
+                    for (int j = 0; j < kn; ++j) rank += ki[j] < id;
+                    sv[rank] = kv[a];
+                    si[rank] = id;
+                }
+                __syncwarp();
+                res = warp_draw_sorted(sv, kn, u);
+            } else {
+                res = FALLBACK;
+            }
+        }
+        if (lane == 0) {
+            *sc.thr = t;
+            *sc.kn = res;
+        }
+    }
+    __syncthreads();
+    thr_out = *sc.thr;
+    const int res = *sc.kn;
+    if (res != FALLBACK) return (!draw || res == 0x7fffffff) ? (int64_t)(V - 1) : (int64_t)si[res];
+    __syncthreads();  // every thread has read sc.kn before list_draw reuses it
+    return list_draw(cv, ci, n, thr_out, drop_id, u, V, kv, ki, sv, si, sc);
 }
 
 }  // namespace b2s

@@ -228,7 +228,7 @@ struct Row {
     const uint4* gvec;          // interior vector 0 in global memory
     int V, nh, nvec, e0;        // head elements [0, nh); interior vectors; first interior element e0 == nh
     const uint32_t* bits;       // history bitmap (nullptr: no history ids)
-    const uint16_t* pref;       // per bitmap word: the history ids below the word (exclusive popcount prefix)
+    const uint16_t* pref;       // per 4-word group of the bitmap: the history ids below it (exclusive prefix)
     const float* htv;           // processed value of each distinct history id, by rank
     float T;
     bool identity;
@@ -247,7 +247,14 @@ struct Row {
     __device__ __forceinline__ float raw(int i) const { return Elem<E>::gld(rowp, i); }
     // rank of a history id i among the row's distinct history ids (ascending id order)
     __device__ __forceinline__ int rank(int i) const {
-        return (int)pref[i >> 5] + __popc(bits[i >> 5] & ((1u << (i & 31)) - 1u));
+        const int w = i >> 5, sub = w & 3;
+        const uint4 q = reinterpret_cast<const uint4*>(bits)[w >> 2];
+        int r = (int)pref[w >> 2];
+        r += sub > 0 ? __popc(q.x) : 0;
+        r += sub > 1 ? __popc(q.y) : 0;
+        r += sub > 2 ? __popc(q.z) : 0;
+        const uint32_t wv = sub == 0 ? q.x : sub == 1 ? q.y : sub == 2 ? q.z : q.w;
+        return r + __popc(wv & ((1u << (i & 31)) - 1u));
     }
     // processed value of element i (history ids and the censored EOS carry their own value)
     __device__ __forceinline__ float P(int i, float x) const {
@@ -577,7 +584,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         // ---------------- prologue: once the staged history has landed, mark its ids in a bitmap and in
         // per-thread slice masks; rank the distinct ids and count them
         if (use_ht) {
-            for (uint32_t w = tid; w < p.bitwords; w += NT) bits[w] = 0;
+            for (uint32_t g = tid; g < p.bitwords / 4; g += NT) reinterpret_cast<uint4*>(bits)[g] = make_uint4(0u, 0u, 0u, 0u);
             for (int d = tid; d < p.hcap; d += NT) hcnt[d] = 0u;
         }
         smask[tid] = 0ull;
@@ -632,15 +639,22 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 mark_slice(p.eos);
             }
             __syncthreads();
-            // rank of an id = the distinct ids below it: exclusive prefix of the bitmap words' popcounts
-            const int wpt = ((int)p.bitwords + NT - 1) / NT;
-            const int w0 = min((int)p.bitwords, tid * wpt), w1 = min((int)p.bitwords, w0 + wpt);
+            // rank of an id = the distinct ids below it: exclusive prefix of the popcounts of the bitmap's
+            // 4-word groups (contiguous groups per thread, 16-byte shared loads)
+            const int G = (int)p.bitwords >> 2;
+            const int gpt = (G + NT - 1) / NT;
+            const int g0 = min(G, tid * gpt), g1 = min(G, g0 + gpt);
+            const uint4* b4 = reinterpret_cast<const uint4*>(bits);
             int cnt = 0;
-            for (int w = w0; w < w1; ++w) cnt += __popc(bits[w]);
+            for (int g = g0; g < g1; ++g) {
+                const uint4 q = b4[g];
+                cnt += __popc(q.x) + __popc(q.y) + __popc(q.z) + __popc(q.w);
+            }
             int base = block_excl_scan_i(cnt, ctl->red_i, &hd);
-            for (int w = w0; w < w1; ++w) {
-                pref[w] = (uint16_t)base;
-                base += __popc(bits[w]);
+            for (int g = g0; g < g1; ++g) {
+                pref[g] = (uint16_t)base;
+                const uint4 q = b4[g];
+                base += __popc(q.x) + __popc(q.y) + __popc(q.z) + __popc(q.w);
             }
             __syncthreads();
             if (pen_hist)
@@ -741,19 +755,21 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         float tmax_nh = f_ninf();
         if (cand_path) {
             const unsigned long long hmask = smask[tid];
-            auto pass1_chunk = [&](const uint4* q, int c) {
+            // the bookkeeping of chunk c, once its maximum is known (its registers are refilled first)
+            auto pass1_account = [&](int c, float vm) {
                 if (c < HPT) gather_hist(tid + c * NT);
-                const float vm = Elem<E>::template vmaxn<ITS>(q);
                 tmaxc[c * NT + tid] = vm;
                 if (!((hmask >> c) & 1ull)) tmax_nh = fmaxf(tmax_nh, vm);
             };
-            // chunk c in nq (even) or nq2 (odd); each buffer is refilled right after its chunk is processed
+            // chunk c in nq (even) or nq2 (odd); each buffer is refilled as soon as its chunk's maximum is taken
             for (int c = 0; c < nchunks; c += 2) {
-                pass1_chunk(nq, c);
+                const float vm0 = Elem<E>::template vmaxn<ITS>(nq);
                 if (c + 2 < nchunks) load_chunk(c + 2, nq);
+                pass1_account(c, vm0);
                 if (c + 1 < nchunks) {
-                    pass1_chunk(nq2, c + 1);
+                    const float vm1 = Elem<E>::template vmaxn<ITS>(nq2);
                     if (c + 3 < nchunks) load_chunk(c + 3, nq2);
+                    pass1_account(c + 1, vm1);
                 }
             }
             // the ragged head / tail (one element in each of the last warp's lanes 16..31)
@@ -1009,10 +1025,10 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 __syncthreads();
                 if (tid == 0) p.cout_n[r] = ctl->kn;
             } else {
-                thr = list_threshold(cv, n, k, hf, lse, top_p, p.min_keep, topk_only, vals, sc);
-                if (wants_draw)
-                    token = list_draw(cv, ci, n, thr, (hf && masked_eos) ? p.eos : -1, ctl->u, V, xv, xi, sv,
-                                      si, sc);
+                const int64_t t = list_sample(cv, ci, n, k, hf, lse, top_p, p.min_keep, topk_only, wants_draw,
+                                              (hf && masked_eos) ? p.eos : -1, ctl->u, V, vals, xv, xi, sv, si, sc,
+                                              thr);
+                if (wants_draw) token = t;
             }
         }
 
@@ -1450,14 +1466,14 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     const bool hashed = !identity && (a->window > 0 || (a->eos >= 0 && a->eos < a->vocab));
     const int hist_ids = (a->window < a->vocab ? a->window : a->vocab) + 1;  // distinct ids: window + EOS
     p.hcap = hashed ? hist_ids : 0;
-    p.bitwords = hashed ? (uint32_t)((a->vocab + 31) / 32) : 0u;
+    p.bitwords = hashed ? (uint32_t)(((a->vocab + 31) / 32 + 3) / 4 * 4) : 0u;  // whole 4-word groups
     uint32_t off = 0;
     p.off_ctl = off;
     off = align_up(off + (uint32_t)sizeof(Ctl), 128);
     p.off_bits = off;
     off = align_up(off + p.bitwords * 4, 16);
-    p.off_pref = off;  // 16-bit ranks: hcap <= 2^13 + 1
-    off = align_up(off + p.bitwords * 2, 16);
+    p.off_pref = off;  // one 16-bit rank per 4-word group: hcap <= 2^13 + 1
+    off = align_up(off + p.bitwords / 4 * 2, 16);
     p.off_hcnt = off;
     off = align_up(off + (uint32_t)p.hcap * 4, 16);
     p.off_hid = off;

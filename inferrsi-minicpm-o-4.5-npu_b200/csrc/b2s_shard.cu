@@ -88,13 +88,13 @@ __global__ void __launch_bounds__(NT, 1) shard_merge_kernel(const MergeParams p)
     __syncthreads();
     const Scr sc{hist, ctl->rctl, &ctl->gather_n, &ctl->kn, &ctl->thr, ctl->red_d, ctl->red_f, ctl->red_i};
     const float top_p = p.rP ? p.rP[r] : p.top_p;
-    const float thr = list_threshold(cv, n, k, false, 0.0f, top_p, p.min_keep, (p.flags & B2S_FLAG_TOPK_ONLY) != 0,
-                                     vals, sc);
     const int64_t step = p.steps ? p.steps[r] : 0;
     const float u = p.rng == B2S_RNG_UNIFORM ? p.uvals[r]
                     : p.rng == B2S_RNG_PHILOX ? uniform_philox(p.seeds[r], step, p.requests ? p.requests[r] : 0)
                                               : uniform_counter(p.seeds[r], step);
-    const int64_t tok = list_draw(cv, ci, n, thr, -1, u, p.V, kv, ki, sv, si, sc);
+    float thr;
+    const int64_t tok = list_sample(cv, ci, n, k, false, 0.0f, top_p, p.min_keep, (p.flags & B2S_FLAG_TOPK_ONLY) != 0,
+                                    true, -1, u, p.V, vals, kv, ki, sv, si, sc, thr);
     if (tid == 0) p.tokens[r] = tok;
 }
 
