@@ -131,6 +131,15 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation may start
+// while the previous kernel of the stream is still running.  It first waits for that kernel's completion
+// (and the visibility of its writes), then lets the next kernel of the stream start early in turn.  Without
+// a programmatic predecessor the wait returns at once.
+__device__ __forceinline__ void pdl_wait_then_release() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- warp / CTA primitives
 
 __device__ __forceinline__ float warp_max(float v) {

@@ -483,6 +483,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     constexpr int ES = Elem<E>::SZ, EPV = Elem<E>::EPV;
     const int V = p.V;
     const Scr sc{hist, ctl->rctl, &ctl->gather_n, &ctl->kn, &ctl->thr, ctl->red_d, ctl->red_f, ctl->red_i};
+    pdl_wait_then_release();  // nothing global is read before the previous kernel of the stream is done
 
     // 16-byte-aligned interior of row r: head elements before it, vectors in it
     auto geometry = [&](int r, int& nh, int& nvec, const uint4*& gvec) {
@@ -1144,6 +1145,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
 template <typename E>
 __global__ void __launch_bounds__(NT, 2) argmax_kernel(const void* logits, int V, int64_t stride, int per,
                                                        int64_t* tokens) {
+    pdl_wait_then_release();
     cg::cluster_group cluster = cg::this_cluster();
     const int C = (int)cluster.num_blocks();
     const int crank = (int)cluster.block_rank();
@@ -1534,8 +1536,12 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     cfg.blockDim = dim3(NT, 1, 1);
     cfg.dynamicSmemBytes = p.smem_total;
     cfg.stream = (cudaStream_t)stream;
-    cfg.attrs = nullptr;
-    cfg.numAttrs = 0;
+    // the launch may overlap the tail of the stream's previous kernel (the kernel waits for it before any read)
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kern, p);
     if (e != cudaSuccess) return cuda_fail(e);
     return B2S_OK;
@@ -1567,7 +1573,8 @@ int b2s_argmax(const void* logits, int32_t dtype, int32_t rows, int32_t vocab, i
     const int es = dtype == B2S_DTYPE_BF16 ? 2 : 4;
     int C = 1;
     const int64_t row_bytes = (int64_t)vocab * es;
-    while (C < 8 && (int64_t)rows * C < 2 * sm_count() && row_bytes / (C * 2) >= 16 * 1024) C <<= 1;
+    // split rows over up to 8 CTAs while the grid stays within one wave (two CTAs per SM)
+    while (C < 8 && (int64_t)rows * C * 2 <= 2 * sm_count() && row_bytes / (C * 2) >= 16 * 1024) C <<= 1;
     int per = ((vocab + C - 1) / C + 15) / 16 * 16;
     while (C > 1 && (int64_t)per * (C - 1) >= vocab) {
         C >>= 1;
@@ -1579,13 +1586,15 @@ int b2s_argmax(const void* logits, int32_t dtype, int32_t rows, int32_t vocab, i
     cfg.blockDim = dim3(NT, 1, 1);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = (cudaStream_t)stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned)C;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see b2s_sample
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = dtype == B2S_DTYPE_BF16
                         ? cudaLaunchKernelEx(&cfg, argmax_kernel<__nv_bfloat16>, logits, (int)vocab, row_stride, per, tokens)
                         : cudaLaunchKernelEx(&cfg, argmax_kernel<float>, logits, (int)vocab, row_stride, per, tokens);
