@@ -25,9 +25,34 @@ struct Scr {
 
 // The k largest values of cv[0..n) (n >= k), descending with multiplicity, into vals[0..k).  Small lists
 // rank every item by counting (value desc, position asc: ranks are a permutation); longer ones find the
-// k-th key by radix select first and rank only the items above it.  vals needs 2*KLIST floats.
+// k-th key by radix select first and rank only the items above it.  vals needs 2*KLIST floats; lists of
+// at most 128 items use sc.hist for their ranks.
 __device__ __forceinline__ void list_topk_values(const float* cv, int n, int k, float* vals, const Scr& sc) {
     const int tid = threadIdx.x;
+    if (n <= 128) {
+        // every (item, segment of the list) pair in its own thread: S segments of L items per item, partial
+        // ranks summed into sc.hist (shared atomics), so no thread walks the whole list
+        uint32_t* rk = sc.hist;
+        const int S = NT / max(n, 1), L = (n + S - 1) / S;
+        for (int i = tid; i < n; i += NT) rk[i] = 0u;
+        __syncthreads();
+        const int i = tid / S, s0 = (tid % S) * L;
+        if (i < n) {
+            const float vi = cv[i];
+            int part = 0;
+            const int s1 = min(n, s0 + L);
+            for (int j = s0; j < s1; ++j) {
+                const float vj = cv[j];
+                part += (vj > vi) | ((vj == vi) & (j < i));
+            }
+            if (part) atomicAdd(&rk[i], (uint32_t)part);
+        }
+        __syncthreads();
+        for (int a = tid; a < n; a += NT)
+            if (rk[a] < (uint32_t)k) vals[rk[a]] = cv[a];
+        __syncthreads();
+        return;
+    }
     if (n <= 2 * NT) {
         // cv is 16-byte aligned: four items per shared load, several loads in flight
         const float4* c4 = reinterpret_cast<const float4*>(cv);
