@@ -91,11 +91,13 @@ struct Params {
     uint32_t off_ctl, off_bits, off_pref, off_hcnt, off_hid, off_htv, off_smask, off_hstage, off_atab, off_cand,
         off_candi, off_lst, off_vals, off_hist, off_hraw, off_tmaxc;
     int tmc_chunks;  // chunks whose per-thread maxima fit (rows with more take the exact path)
+    int csplit;      // 1: two CTAs per row (a cluster): rank 1 builds the history structures, rank 0 the rest
     uint32_t smem_total;
 };
 
 struct Ctl {
     int err, gather_n, kn;
+    int hd_x;  // distinct history ids, from the helper CTA (two-CTA rows)
     int wcnt[NWARP];  // candidates each warp pushed into its segment of the list
     uint32_t rctl[2];
     uint32_t klo, kcnt;
@@ -517,7 +519,14 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     uint4 nq[ITS], nq2[ITS];  // even / odd chunks
     bool next_row_in = false;  // nq already holds chunk 0 of this CTA's next row
 
-    for (int r = blockIdx.x; r < p.rows; r += gridDim.x) {
+    // Two-CTA rows (p.csplit): the cluster's rank 1 stages the history, builds the bitmap, slice masks, ranks
+    // and counts, gathers the history ids' raw values, and copies all of it into rank 0's shared memory,
+    // while rank 0 streams pass 1.  They meet at a cluster barrier; rank 0 does the rest of the row.  A second
+    // cluster barrier ends each row, so the helper never overwrites structures still in use.
+    const bool split = p.csplit != 0;
+    const bool helper = split && cg::this_cluster().block_rank() == 1;
+    const int rstep = split ? (int)gridDim.x / 2 : (int)gridDim.x;
+    for (int r = split ? (int)blockIdx.x / 2 : (int)blockIdx.x; r < p.rows; r += rstep) {
         // ---------------- geometry; the first chunk's loads go out before anything else
         Row<E> R;
         R.rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
@@ -526,15 +535,17 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         R.e0 = R.nh;
         const int nchunks = (R.nvec + VPC - 1) / VPC;
         auto load_chunk = [&](int c, uint4* q) { load_chunk_of(R.gvec, R.nvec, c, q); };
-        if (!next_row_in && nchunks > 0) load_chunk(0, nq);
-        if (nchunks > 1) load_chunk(1, nq2);
+        if (!helper) {
+            if (!next_row_in && nchunks > 0) load_chunk(0, nq);
+            if (nchunks > 1) load_chunk(1, nq2);
+        }
         next_row_in = false;
         if (tid == 0) ctl->err = 0;
         // the history and the penalty table, asynchronously, before the row's parameters are known (a row that
         // turns out not to need them just does not read them)
         const int64_t* hrow = p.hist ? p.hist + (int64_t)r * p.hstride : nullptr;
         const float* alpha = p.alpha ? p.alpha + (int64_t)r * p.alpha_stride : nullptr;
-        if (hrow && p.W > 0) {
+        if (hrow && p.W > 0 && (!split || helper)) {  // two-CTA rows: the helper's copy arrives later
             for (int j = tid; j < p.W; j += NT) cp_async8(&hstage[j], &hrow[j]);
             if (alpha)
                 for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], &alpha[j]);
@@ -584,11 +595,12 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
 
         // ---------------- prologue: once the staged history has landed, mark its ids in a bitmap and in
         // per-thread slice masks; rank the distinct ids and count them
-        if (use_ht) {
+        const bool own_hist = !split || helper;  // this CTA builds the history structures
+        if (use_ht && own_hist) {
             for (uint32_t g = tid; g < p.bitwords / 4; g += NT) reinterpret_cast<uint4*>(bits)[g] = make_uint4(0u, 0u, 0u, 0u);
             for (int d = tid; d < p.hcap; d += NT) hcnt[d] = 0u;
         }
-        smask[tid] = 0ull;
+        if (own_hist) smask[tid] = 0ull;
         // the elements outside the 16-byte interior, one per lane of the last warp's lanes 16..31: the head
         // (at most 7) in lanes 16..23 and the tail (at most 7) in lanes 24..31 -- or, for a row with no
         // interior vector (under 32 bytes, so at most 15 elements), the whole row in lanes 16..31
@@ -615,6 +627,18 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             const int64_t id = hv - p.id_off;
             return (hv >= 0 && id >= 0 && id < V) ? (int)id : -1;
         };
+        // raw value of history position j: the aligned 4-byte word holding it, copied asynchronously into
+        // hraw[j] (positions tid + u * NT, u < HPT, one per chunk so the gathers do not queue up together)
+        const uintptr_t row_lo = reinterpret_cast<uintptr_t>(R.rowp), row_hi = row_lo + (uintptr_t)V * ES;
+        auto gather_hist = [&](int j) {
+            if (!pen_hist || j >= p.W) return;
+            const int id = hist_id(j);
+            if (id < 0) return;
+            const uintptr_t wa = (row_lo + (uintptr_t)id * ES) & ~(uintptr_t)3;
+            if (wa >= row_lo && wa + 4 <= row_hi) cp_async4(&hraw[j], reinterpret_cast<const void*>(wa));
+        };
+        if (helper)  // all of them at once, under the marking and ranking below
+            for (int u = 0; u < HPT; ++u) gather_hist(tid + u * NT);
         // interior element e lies in the pass-1 share of thread v % NT in chunk v / VPC (v: its vector)
         auto mark_slice = [&](int e) {
             const int rel = e - R.e0;
@@ -623,7 +647,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             if (v < R.nvec && v / VPC < 64) atomicOr(&smask[v % NT], 1ull << (v / VPC));
         };
         int hd = 0;  // distinct history ids of the row (the censored EOS included)
-        if (use_ht) {
+        if (use_ht && own_hist) {
             if (pen_hist)
                 for (int j = tid; j < p.W; j += NT) {
                     const int id = hist_id(j);
@@ -671,16 +695,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         } else {
             __syncthreads();
         }
-        // raw value of history position j: the aligned 4-byte word holding it, copied asynchronously into
-        // hraw[j] (positions tid + u * NT, u < HPT, one per chunk so the gathers do not queue up together)
-        const uintptr_t row_lo = reinterpret_cast<uintptr_t>(R.rowp), row_hi = row_lo + (uintptr_t)V * ES;
-        auto gather_hist = [&](int j) {
-            if (!pen_hist || j >= p.W) return;
-            const int id = hist_id(j);
-            if (id < 0) return;
-            const uintptr_t wa = (row_lo + (uintptr_t)id * ES) & ~(uintptr_t)3;
-            if (wa >= row_lo && wa + 4 <= row_hi) cp_async4(&hraw[j], reinterpret_cast<const void*>(wa));
-        };
         // processed value of history id `id`, seen n times, with raw value x
         auto hist_value = [&](int id, int n, float x) {
             if (n >= p.alpha_len && n > 0) {
@@ -697,6 +711,54 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             }
             return __fdiv_rn(v, T);
         };
+        // processed values of the history ids (hcnt and the raw values gathered during pass 1)
+        auto compute_htv = [&]() {
+            if (pen_hist) {
+                if (!split)
+                    for (int u = nchunks; u < HPT; ++u) gather_hist(tid + u * NT);  // short rows
+                cp_async_wait_all();  // this thread's copies
+                for (int j = tid; j < p.W; j += NT) {
+                    const int id = hist_id(j);
+                    if (id < 0) continue;
+                    const uintptr_t ea = row_lo + (uintptr_t)id * ES, wa = ea & ~(uintptr_t)3;
+                    float x;
+                    if (j < HPT * NT && wa >= row_lo && wa + 4 <= row_hi) {
+                        const uint32_t w = __float_as_uint(hraw[j]);
+                        x = ES == 4 ? __uint_as_float(w) : bf16_bits_to_f((uint16_t)(w >> (8 * (unsigned)(ea - wa))));
+                    } else {
+                        x = Elem<E>::gld(R.rowp, id);
+                    }
+                    const int rk = R.rank(id);
+                    htv[rk] = hist_value(id, (int)hcnt[rk], x);  // repeated ids write the same value
+                }
+            }
+            if (censor && tid == 0) htv[R.rank(p.eos)] = f_ninf();  // omni: EOS is -inf
+        };
+        if (helper) {
+            // the history's processed values too; then hand rank 0 what the rest of its row reads -- history
+            // ids, bitmap, processed values and ids by rank, slice masks -- in 16-byte pieces (every region is
+            // 16-byte aligned and padded).  Ranks and counts stay here: rank 0 reads those remotely, and only
+            // on its rare full-row paths.
+            compute_htv();
+            __syncthreads();
+            cg::cluster_group cl = cg::this_cluster();
+            auto copy_region = [&](uint32_t off, uint32_t bytes) {
+                uint4* dst = cl.map_shared_rank(reinterpret_cast<uint4*>(smem + off), 0);
+                const uint4* src = reinterpret_cast<const uint4*>(smem + off);
+                for (uint32_t i = tid; i < (bytes + 15u) / 16u; i += NT) dst[i] = src[i];
+            };
+            if (hrow && p.W > 0) copy_region(p.off_hstage, (uint32_t)p.W * 8u);
+            if (use_ht) {
+                copy_region(p.off_bits, p.bitwords * 4u);
+                copy_region(p.off_htv, (uint32_t)hd * 4u);
+                copy_region(p.off_hid, (uint32_t)hd * 4u);
+            }
+            copy_region(p.off_smask, NT * 8u);
+            if (tid == 0) *cl.map_shared_rank(&ctl->hd_x, 0) = hd;
+            cl.sync();  // the structures are in rank 0's shared memory
+            cl.sync();  // rank 0 is done with this row
+            continue;
+        }
 
         // ---------------- candidate path, in two passes over the row.
         //   pass 1 (HBM, every element once): each thread's largest non-history value, and the largest value
@@ -755,12 +817,12 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         // is left out whole: the value stays a lower bound of a distinct non-history element)
         float tmax_nh = f_ninf();
         if (cand_path) {
-            const unsigned long long hmask = smask[tid];
+            const unsigned long long hmask = split ? 0ull : smask[tid];  // two-CTA rows: applied below
             // the bookkeeping of chunk c, once its maximum is known (its registers are refilled first)
             auto pass1_account = [&](int c, float vm) {
-                if (c < HPT) gather_hist(tid + c * NT);
+                if (!split && c < HPT) gather_hist(tid + c * NT);
                 tmaxc[c * NT + tid] = vm;
-                if (!((hmask >> c) & 1ull)) tmax_nh = fmaxf(tmax_nh, vm);
+                if (!split && !((hmask >> c) & 1ull)) tmax_nh = fmaxf(tmax_nh, vm);
             };
             // chunk c in nq (even) or nq2 (odd); each buffer is refilled as soon as its chunk's maximum is taken
             for (int c = 0; c < nchunks; c += 2) {
@@ -773,6 +835,22 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                     pass1_account(c + 1, vm1);
                 }
             }
+        } else if (!split) {
+            for (int u = 0; u < HPT; ++u) gather_hist(tid + u * NT);
+        }
+        if (split) {
+            // the helper's structures are complete: read them where they are (distributed shared memory)
+            cg::cluster_group cl = cg::this_cluster();
+            cl.sync();
+            R.pref = cl.map_shared_rank(pref, 1);  // the ranks stayed with the helper
+            hd = ctl->hd_x;
+            if (cand_path) {
+                const unsigned long long hm = smask[tid];
+                for (int c = 0; c < nchunks; ++c)
+                    if (!((hm >> c) & 1ull)) tmax_nh = fmaxf(tmax_nh, tmaxc[c * NT + tid]);
+            }
+        }
+        if (cand_path) {
             // the ragged head / tail (one element in each of the last warp's lanes 16..31)
             if (edge_i >= 0 && !R.hbit(edge_i)) tmax_nh = fmaxf(tmax_nh, edge_x);
             // the warp's jw largest per-thread maxima (distinct lanes): take the maximum out jw times
@@ -784,14 +862,12 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 if (who && lane == __ffs(who) - 1) v = f_ninf();
                 if (lane == 0) kv[(tid >> 5) * jw + t] = mj;
             }
-        } else {
-            for (int u = 0; u < HPT; ++u) gather_hist(tid + u * NT);
         }
         // this row's stream is done: start the first chunk of the CTA's next row
-        if (r + (int)gridDim.x < p.rows) {
+        if (r + rstep < p.rows) {
             int nh2, nvec2;
             const uint4* g2;
-            geometry(r + (int)gridDim.x, nh2, nvec2, g2);
+            geometry(r + rstep, nh2, nvec2, g2);
             if (nvec2 > 0) load_chunk_of(g2, nvec2, 0, nq);
             next_row_in = true;
         }
@@ -819,28 +895,6 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 tau_low = margin(t0);
             }
         }
-        // processed values of the history ids (hcnt and the raw values gathered during pass 1)
-        auto compute_htv = [&]() {
-            if (pen_hist) {
-                for (int u = nchunks; u < HPT; ++u) gather_hist(tid + u * NT);  // short rows
-                cp_async_wait_all();  // this thread's copies
-                for (int j = tid; j < p.W; j += NT) {
-                    const int id = hist_id(j);
-                    if (id < 0) continue;
-                    const uintptr_t ea = row_lo + (uintptr_t)id * ES, wa = ea & ~(uintptr_t)3;
-                    float x;
-                    if (j < HPT * NT && wa >= row_lo && wa + 4 <= row_hi) {
-                        const uint32_t w = __float_as_uint(hraw[j]);
-                        x = ES == 4 ? __uint_as_float(w) : bf16_bits_to_f((uint16_t)(w >> (8 * (unsigned)(ea - wa))));
-                    } else {
-                        x = Elem<E>::gld(R.rowp, id);
-                    }
-                    const int rk = R.rank(id);
-                    htv[rk] = hist_value(id, (int)hcnt[rk], x);  // repeated ids write the same value
-                }
-            }
-            if (censor && tid == 0) htv[R.rank(p.eos)] = f_ninf();  // omni: EOS is -inf
-        };
         bool htv_done = false;
         if (cand_path && !ovf) {
             // pass 2: each thread re-reads (from L2) its chunks whose maximum clears tau, two at a time so that
@@ -877,7 +931,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             uint4 q1[ITS], q2[ITS];
             load_at(c1, q1);
             load_at(c2, q2);
-            compute_htv();
+            if (!split) compute_htv();
             htv_done = true;
             for (;;) {
                 const uint32_t h1 = c1 >= 0 ? hit_mask(q1, R.e0 + c1 * VPC * EPV) : 0u;
@@ -898,7 +952,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 if (eh) place(edge_x, edge_i, pos);
             }
         }
-        if (!htv_done) compute_htv();
+        if (!htv_done && !split) compute_htv();
         if (lane == 0) ctl->wcnt[tid >> 5] = wn;
         if (tid == 0) ctl->kn = 0;  // the candidate count of the compaction below
         __syncthreads();
@@ -1134,6 +1188,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         }
         if (p.cout_n && (mode != MODE_FILTER || row_err) && tid == 0) p.cout_n[r] = -1;
         if (!p.cout_n) finish_row((row_err || mode == MODE_SKIP || mode == MODE_FAIL) ? PAD : token);
+        if (split) cg::this_cluster().sync();  // the helper may overwrite the history structures now
         __syncthreads();  // the row's shared state is dead: the next row may reuse it
     }
 }
@@ -1530,18 +1585,30 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
             done[ti] |= bit;
         }
     }
+    // Two CTAs per row when every pair fits on the SMs at once (one 512-thread CTA per SM), the row streams
+    // several chunks and has a penalty history: the history work then runs beside pass 1.
+    {
+        const int64_t row_chunks = ((int64_t)a->vocab * es / 16 + VPC - 1) / VPC;
+        p.csplit = (!so && !a->processed && !identity && p.W > 0 && row_chunks >= 4 && row_chunks <= p.tmc_chunks &&
+                    (int64_t)a->rows * 2 <= sm_count()) ? 1 : 0;
+    }
+    const int64_t grid_rows = a->rows < 65535 * 8 ? a->rows : 65535 * 8;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3((unsigned)(a->rows < 65535 * 16 ? a->rows : 65535 * 16), 1, 1);
+    cfg.gridDim = dim3((unsigned)(p.csplit ? 2 * grid_rows : grid_rows), 1, 1);
     cfg.blockDim = dim3(NT, 1, 1);
     cfg.dynamicSmemBytes = p.smem_total;
     cfg.stream = (cudaStream_t)stream;
     // the launch may overlap the tail of the stream's previous kernel (the kernel waits for it before any read)
-    cudaLaunchAttribute pdl[1];
-    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    pdl[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = pdl;
-    cfg.numAttrs = 1;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    attrs[1].id = cudaLaunchAttributeClusterDimension;
+    attrs[1].val.clusterDim.x = 2;
+    attrs[1].val.clusterDim.y = 1;
+    attrs[1].val.clusterDim.z = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = p.csplit ? 2 : 1;
     e = cudaLaunchKernelEx(&cfg, kern, p);
     if (e != cudaSuccess) return cuda_fail(e);
     return B2S_OK;
