@@ -88,7 +88,7 @@ struct Params {
     int lcap, kbuf, nvals;
     int hcap;  // distinct history ids a row can hold (window + the censored EOS)
     uint32_t bitwords;
-    uint32_t off_ctl, off_bits, off_pref, off_hcnt, off_hid, off_htv, off_smask, off_hstage, off_atab, off_cand,
+    uint32_t off_ctl, off_bits, off_pref, off_hcnt, off_hid, off_hpos, off_htv, off_smask, off_hstage, off_atab, off_cand,
         off_candi, off_lst, off_vals, off_hist, off_hraw, off_tmaxc;
     int tmc_chunks;  // chunks whose per-thread maxima fit (rows with more take the exact path)
     int csplit;      // 1: two CTAs per row (a cluster): rank 1 builds the history structures, rank 0 the rest
@@ -468,6 +468,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     uint16_t* pref = reinterpret_cast<uint16_t*>(smem + p.off_pref);
     uint32_t* hcnt = reinterpret_cast<uint32_t*>(smem + p.off_hcnt);  // occurrences of each distinct id, by rank
     int* hid = reinterpret_cast<int*>(smem + p.off_hid);              // the id of each rank
+    int* hpos = reinterpret_cast<int*>(smem + p.off_hpos);            // a history position of each rank
     float* htv = reinterpret_cast<float*>(smem + p.off_htv);
     unsigned long long* smask = reinterpret_cast<unsigned long long*>(smem + p.off_smask);  // [thread] chunk bits
     int64_t* hstage = reinterpret_cast<int64_t*>(smem + p.off_hstage);
@@ -689,6 +690,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                     const int rk = R.rank(id);
                     atomicAdd(&hcnt[rk], 1u);
                     hid[rk] = id;  // every occurrence writes the same id
+                    hpos[rk] = j;  // and one of them its position
                 }
             if (censor && tid == 0) hid[R.rank(p.eos)] = p.eos;
             // hcnt / hid are read after the next barrier
@@ -712,14 +714,20 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             return __fdiv_rn(v, T);
         };
         // processed values of the history ids (hcnt and the raw values gathered during pass 1)
+        // (once per distinct id, with the raw value gathered at one of its positions)
         auto compute_htv = [&]() {
             if (pen_hist) {
                 if (!split)
                     for (int u = nchunks; u < HPT; ++u) gather_hist(tid + u * NT);  // short rows
-                cp_async_wait_all();  // this thread's copies
-                for (int j = tid; j < p.W; j += NT) {
-                    const int id = hist_id(j);
-                    if (id < 0) continue;
+                cp_async_wait_all();
+                __syncthreads();  // every thread's gathers have landed
+                for (int d = tid; d < hd; d += NT) {
+                    const int id = hid[d];
+                    if (censor && id == p.eos) {  // omni: EOS is -inf (a history id or not)
+                        htv[d] = f_ninf();
+                        continue;
+                    }
+                    const int j = hpos[d];
                     const uintptr_t ea = row_lo + (uintptr_t)id * ES, wa = ea & ~(uintptr_t)3;
                     float x;
                     if (j < HPT * NT && wa >= row_lo && wa + 4 <= row_hi) {
@@ -728,11 +736,11 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                     } else {
                         x = Elem<E>::gld(R.rowp, id);
                     }
-                    const int rk = R.rank(id);
-                    htv[rk] = hist_value(id, (int)hcnt[rk], x);  // repeated ids write the same value
+                    htv[d] = hist_value(id, (int)hcnt[d], x);
                 }
+            } else if (censor && tid == 0) {
+                htv[R.rank(p.eos)] = f_ninf();  // omni: EOS is -inf (no history ids)
             }
-            if (censor && tid == 0) htv[R.rank(p.eos)] = f_ninf();  // omni: EOS is -inf
         };
         if (helper) {
             // the history's processed values too; then hand rank 0 what the rest of its row reads -- history
@@ -1534,6 +1542,8 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     p.off_hcnt = off;
     off = align_up(off + (uint32_t)p.hcap * 4, 16);
     p.off_hid = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_hpos = off;
     off = align_up(off + (uint32_t)p.hcap * 4, 16);
     p.off_htv = off;
     off = align_up(off + (uint32_t)p.hcap * 4, 16);
