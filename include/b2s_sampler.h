@@ -60,7 +60,7 @@ typedef struct b2s_sample_args {
     int32_t logits_dtype;
     int32_t rows;
     int32_t vocab;
-    int32_t cluster; /* reserved (ABI version 1 field): b2s_sample runs one CTA per row and ignores it */
+    int32_t cluster; /* reserved (ABI version 1 field), ignored: the launcher picks one or two CTAs per row */
     int64_t logits_row_stride;
     /* penalty history [rows, window] int64 (most recent last); ids < 0 are empty (PAD) */
     const int64_t* history;
