@@ -645,7 +645,8 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             const int rel = e - R.e0;
             if (rel < 0) return;
             const int v = rel / EPV;
-            if (v < R.nvec && v / VPC < 64) atomicOr(&smask[v % NT], 1ull << (v / VPC));
+            const int c = v / VPC;  // (the low word of smask[t] holds chunks 0..31)
+            if (v < R.nvec && c < 64) atomicOr(reinterpret_cast<uint32_t*>(&smask[v % NT]) + (c >> 5), 1u << (c & 31));
         };
         int hd = 0;  // distinct history ids of the row (the censored EOS included)
         if (use_ht && own_hist) {
