@@ -213,6 +213,32 @@ def test_benchmark_shapes_match_oracle(pkg, kind, B):
     assert np.array_equal(got_c, want_c)
 
 
+@pytest.mark.parametrize("sem", ["omni", "hf"])
+def test_paired_cta_rows_with_eos_rules(pkg, sem):
+    """Thinker-size rows at a batch small enough for two CTAs per row (no processed output asked), with the
+    EOS masked (omni: censored to -inf first; hf: dropped from the draw) and the EOS id inside several
+    histories: the same tokens as the oracle, and as the one-CTA path (the launch with processed output)."""
+    ts = pkg.talker_sampler
+    g = I.rng(211)
+    B, V, W, eos = 12, I.THINKER_V, 96, 151_000
+    logits, hist = I.zipf_rows(g, B, V, W)
+    logits = I.bf16_bits_to_f32(I.to_bf16_bits(logits))
+    logits[::2, eos] = logits[::2].max(axis=1) + 1.0  # EOS would win if it were not masked
+    hist[1::3, :5] = eos
+    hist[2::5, 7] = -1
+    steps = np.full(B, 3, np.int64)
+    cfg = C._cfg(semantics=sem, temperature=0.9, top_k=32, top_p=0.9, repetition_penalty=1.2, window=W,
+                 min_new_tokens=10, max_new_tokens=C.BIG, min_keep=1 if sem == "omni" else 3)
+    case = C._case(f"paired_{sem}", logits, "bf16", hist, steps, eos, cfg, 212)
+    _, want_c, _, _ = H.run_oracle(case, counter=True)
+    _, got_split, st1 = run_gpu(ts, case, counter=True, processed=False)
+    _, got_one, st2 = run_gpu(ts, case, counter=True, processed=True)
+    assert st1 == 0 and st2 == 0
+    assert np.array_equal(got_split, want_c), (got_split, want_c)
+    assert np.array_equal(got_one, want_c)
+    assert not np.any(got_split == eos)
+
+
 def test_step_state_matches_oracle_sequence(pkg):
     """step() over 40 frames (hf, EOS rules, penalties) equals the oracle driven frame by frame."""
     ts = pkg.talker_sampler
