@@ -257,6 +257,42 @@ __device__ __forceinline__ int64_t list_draw(const float* cv, const int* ci, int
     return best == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)si[best];
 }
 
+// Warp 0, k <= 32: warp_topp_threshold with one value per lane (vals[lane]).  The same fp32 values and
+// fp64 accumulation; the fp64 sums only associate differently, which reaches their fp32 rounding only at
+// a boundary.
+__device__ __forceinline__ float warp_topp_threshold32(const float* vals, int k, bool hf, float lse, float top_p,
+                                                       int min_keep, bool topk_only) {
+    const int lane = threadIdx.x & 31;
+    const bool valid = lane < k;
+    const float e = b2s_expf(__fsub_rn(vals[valid ? lane : 0], hf ? lse : vals[0]));
+    float pk = valid ? e : 0.0f;
+    if (!hf) {
+        const float sf = (float)warp_sum((double)pk);
+        pk = __fdiv_rn(pk, sf);  // 0 stays 0 (sf >= 1)
+    }
+    const double incl = warp_incl_scan((double)pk);
+    const bool below = valid && __fsub_rn((float)incl, pk) < top_p;
+    const int cnt = __popc(__ballot_sync(0xffffffffu, below));
+    const int kept = topk_only ? k : max(min(min_keep, k), min(cnt, k));
+    return vals[kept - 1];
+}
+
+// Warp 0, kn <= 32 items, lane i holding the value v of the i-th item in vocabulary order (any value past
+// kn): warp_draw_sorted with one item per lane.  Returns the position drawn in every lane, or 0x7fffffff.
+__device__ __forceinline__ int warp_draw32(float v, int kn, float u) {
+    const int lane = threadIdx.x & 31;
+    const bool valid = lane < kn;
+    const float m = warp_max(valid ? v : __int_as_float(0xff800000));
+    const float e = valid ? b2s_expf(__fsub_rn(v, m)) : 0.0f;
+    const float sf = (float)warp_sum((double)e);
+    const float pr = __fdiv_rn(e, sf);  // 0 stays 0
+    const double incl = warp_incl_scan((double)pr);
+    const double total = __shfl_sync(0xffffffffu, incl, 31);
+    const float target = __fmul_rn(u, (float)total);
+    const unsigned hit = __ballot_sync(0xffffffffu, valid && (float)incl > target);
+    return hit ? __ffs(hit) - 1 : 0x7fffffff;
+}
+
 // The whole list stage: top-k values, top-p threshold (returned in thr_out) and, when `draw`, the token.
 // Warp 0 takes the threshold and, when at most KLIST items are kept, the draw as well -- compaction by
 // ballot, vocabulary order by ranking the (distinct) kept ids, the same inverse-CDF draw as list_draw --
@@ -270,7 +306,8 @@ __device__ __forceinline__ int64_t list_sample(const float* cv, const int* ci, i
     list_topk_values(cv, n, k, vals, sc);
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
-        const float t = warp_topp_threshold(vals, k, hf, lse, top_p, min_keep, topk_only);
+        const float t = k <= 32 ? warp_topp_threshold32(vals, k, hf, lse, top_p, min_keep, topk_only)
+                                : warp_topp_threshold(vals, k, hf, lse, top_p, min_keep, topk_only);
         int res = 0x7fffffff;
         if (draw) {
             int kn = 0;
@@ -285,20 +322,21 @@ __device__ __forceinline__ int64_t list_sample(const float* cv, const int* ci, i
                 }
                 kn += __popc(m);
             }
-            if (kn <= KLIST) {
+            if (kn <= 32) {
+                // one kept item per lane: vocabulary order by counting the smaller ids (they are distinct)
                 __syncwarp();
-                for (int a = lane; a < kn; a += 32) {
-                    const int id = ki[a];
-                    int rank = 0;
-#pragma unroll 4
-                    for (int j = 0; j < kn; ++j) rank += ki[j] < id;
-                    sv[rank] = kv[a];
+                const int id = lane < kn ? ki[lane] : 0x7fffffff;
+                const float x = lane < kn ? kv[lane] : 0.0f;
+                int rank = 0;
+                for (int j = 0; j < kn; ++j) rank += __shfl_sync(0xffffffffu, id, j) < id;
+                if (lane < kn) {
+                    sv[rank] = x;
                     si[rank] = id;
                 }
                 __syncwarp();
-                res = warp_draw_sorted(sv, kn, u);
+                res = warp_draw32(sv[lane < kn ? lane : 0], kn, u);
             } else {
-                res = FALLBACK;
+                res = FALLBACK;  // more than 32 kept items: the block form below is quicker
             }
         }
         if (lane == 0) {
