@@ -459,9 +459,13 @@ __device__ uint32_t kth_key_bucket(int n, int k, KeyFn key, uint32_t* hist, Ctl*
 }
 
 // The whole row program; with a grid smaller than the batch each CTA loops over rows.
-template <typename E>
+// LEAN: a launch with neither processed output nor vocabulary-shard output (the decode step); the code of
+// those outputs is left out of that instantiation.
+template <typename E, bool LEAN>
 __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     extern __shared__ __align__(128) unsigned char smem[];
+    const bool has_proc = !LEAN && p.proc != nullptr;  // processed-logits output
+    int32_t* const cout_n = LEAN ? nullptr : p.cout_n;  // vocabulary-shard output
     const int tid = threadIdx.x, lane = tid & 31;
     Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
     uint32_t* bits = reinterpret_cast<uint32_t*>(smem + p.off_bits);
@@ -564,7 +568,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         const int64_t min_new = p.rminn ? p.rminn[r] : p.min_new, max_new = p.rmaxn ? p.rmaxn[r] : p.max_new;
         const bool masked_eos = eos_ok && step < min_new;
         int mode;
-        if (!p.proc && !p.cout_n && !is_live) mode = MODE_SKIP;
+        if (!has_proc && !cout_n && !is_live) mode = MODE_SKIP;
         else if (identity) mode = MODE_FULL;
         else if (step >= max_new - 1) mode = MODE_FORCED;
         else if (hf && step <= 0) mode = MODE_FULL;
@@ -577,7 +581,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 if (tid == 0) set_status(p, B2S_STATUS_TOPK_LIMIT);
             }
         }
-        if (p.cout_n && mode != MODE_FILTER) mode = MODE_FAIL;
+        if (cout_n && mode != MODE_FILTER) mode = MODE_FAIL;
         const bool topk_only = (p.flags & B2S_FLAG_TOPK_ONLY) != 0;
         if (tid == 32) {  // one thread: the row's uniform (read after the next barrier)
             ctl->u = (p.rng == B2S_RNG_UNIFORM || !p.seeds) ? (p.uvals ? p.uvals[r] : 0.0f)
@@ -655,7 +659,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                     const int id = hist_id(j);
                     if (id < 0) {
                         // a vocabulary shard ignores ids of the other shards; an unsharded row flags ids >= vocab
-                        if (hstage[j] >= 0 && !p.cout_n) set_status(p, B2S_STATUS_HISTORY_RANGE);
+                        if (hstage[j] >= 0 && !cout_n) set_status(p, B2S_STATUS_HISTORY_RANGE);
                         continue;
                     }
                     atomicOr(&bits[id >> 5], 1u << (id & 31));
@@ -1071,7 +1075,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 xi = ti;
             }
             exact = false;
-            if (p.cout_n) {
+            if (cout_n) {
                 // vocabulary shard: every candidate >= this shard's k-th value
                 list_topk_values(cv, n, k, vals, sc);
                 const float kth = vals[k - 1];
@@ -1087,7 +1091,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                     }
                 }
                 __syncthreads();
-                if (tid == 0) p.cout_n[r] = ctl->kn;
+                if (tid == 0) cout_n[r] = ctl->kn;
             } else {
                 const int64_t t = list_sample(cv, ci, n, k, hf, lse, top_p, p.min_keep, topk_only, wants_draw,
                                               (hf && masked_eos) ? p.eos : -1, ctl->u, V, vals, xv, xi, sv, si, sc,
@@ -1099,7 +1103,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         // ---------------- exact path: radix select of the k-th processed key over the row
         if (exact && !row_err && mode == MODE_FILTER) {
             const uint32_t kth = row_kth_key<E>(R, k, hist, ctl);
-            if (p.cout_n) {
+            if (cout_n) {
                 if (tid == 0) ctl->kn = 0;
                 __syncthreads();
                 row_visit<E>(R, [&](int i, float x) {
@@ -1113,7 +1117,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                     }
                 });
                 __syncthreads();
-                if (tid == 0) p.cout_n[r] = ctl->kn;
+                if (tid == 0) cout_n[r] = ctl->kn;
             } else {
                 // values above the k-th (fewer than k), sorted, then k - count copies of the k-th
                 if (tid == 0) ctl->gather_n = 0;
@@ -1182,7 +1186,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         }
 
         // ---------------- processed row
-        if (p.proc && !p.cout_n) {
+        if (has_proc && !cout_n) {
             float* out = p.proc + (int64_t)r * p.pstride;
             const int drop = (hf && masked_eos) ? p.eos : -1;
             if (mode == MODE_FORCED) {
@@ -1195,8 +1199,8 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 });
             }
         }
-        if (p.cout_n && (mode != MODE_FILTER || row_err) && tid == 0) p.cout_n[r] = -1;
-        if (!p.cout_n) finish_row((row_err || mode == MODE_SKIP || mode == MODE_FAIL) ? PAD : token);
+        if (cout_n && (mode != MODE_FILTER || row_err) && tid == 0) cout_n[r] = -1;
+        if (!cout_n) finish_row((row_err || mode == MODE_SKIP || mode == MODE_FAIL) ? PAD : token);
         if (split) cg::this_cluster().sync();  // the helper may overwrite the history structures now
         __syncthreads();  // the row's shared state is dead: the next row may reuse it
     }
@@ -1579,16 +1583,19 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     if (p.smem_total > limit) return B2S_ERR_UNSUPPORTED;
 
     cudaError_t e;
-    void (*kern)(const Params) = a->logits_dtype == B2S_DTYPE_BF16 ? sample_kernel<__nv_bfloat16> : sample_kernel<float>;
+    const bool lean = !so && !a->processed;
+    const bool bf16 = a->logits_dtype == B2S_DTYPE_BF16;
+    void (*kern)(const Params) = bf16 ? (lean ? sample_kernel<__nv_bfloat16, true> : sample_kernel<__nv_bfloat16, false>)
+                                      : (lean ? sample_kernel<float, true> : sample_kernel<float, false>);
     {
-        // the attribute is per device: remember which (device, dtype) pairs have it
+        // the attribute is per device: remember which (device, kernel) pairs have it
         static std::mutex mu;
-        static uint64_t done[2] = {0, 0};
+        static uint64_t done[4] = {0, 0, 0, 0};
         int dev = 0;
         e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return cuda_fail(e);
         std::lock_guard<std::mutex> g(mu);
-        const int ti = a->logits_dtype == B2S_DTYPE_BF16 ? 1 : 0;
+        const int ti = (bf16 ? 1 : 0) + (lean ? 2 : 0);
         const uint64_t bit = 1ull << (dev & 63);
         if (!(done[ti] & bit)) {
             e = set_smem_attr(kern, 227 * 1024);
