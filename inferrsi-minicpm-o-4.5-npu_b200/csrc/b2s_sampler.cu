@@ -460,8 +460,10 @@ __device__ uint32_t kth_key_bucket(int n, int k, KeyFn key, uint32_t* hist, Ctl*
 
 // The whole row program; with a grid smaller than the batch each CTA loops over rows.
 // LEAN: a launch with neither processed output nor vocabulary-shard output (the decode step); the code of
-// those outputs is left out of that instantiation.
-template <typename E, bool LEAN>
+// those outputs is left out of that instantiation.  SEM >= 0: the launch's semantics fixed at compile time, so
+// the other orders' code is left out too (only the omni decode step uses it: an hf-only build measured slower
+// on the batched Talker shape); -1: read from the parameters.
+template <typename E, bool LEAN, int SEM>
 __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const bool has_proc = !LEAN && p.proc != nullptr;  // processed-logits output
@@ -559,8 +561,8 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         // ---------------- row parameters and mode (global loads overlap the stream)
         const int64_t step = p.steps ? p.steps[r] : 0;
         const bool is_live = (p.active ? p.active[r] != 0 : true) && !(p.finished ? p.finished[r] != 0 : false);
-        const bool identity = p.sem == B2S_SEM_IDENTITY;
-        const bool hf = p.sem == B2S_SEM_HF;
+        const bool identity = SEM >= 0 ? false : p.sem == B2S_SEM_IDENTITY;
+        const bool hf = SEM >= 0 ? SEM == B2S_SEM_HF : p.sem == B2S_SEM_HF;
         const float T = p.rT ? p.rT[r] : p.T;
         const float top_p = p.rP ? p.rP[r] : p.top_p;
         const int top_k = p.rK ? p.rK[r] : p.top_k;
@@ -1585,17 +1587,23 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     cudaError_t e;
     const bool lean = !so && !a->processed;
     const bool bf16 = a->logits_dtype == B2S_DTYPE_BF16;
-    void (*kern)(const Params) = bf16 ? (lean ? sample_kernel<__nv_bfloat16, true> : sample_kernel<__nv_bfloat16, false>)
-                                      : (lean ? sample_kernel<float, true> : sample_kernel<float, false>);
+    // variant: 0 general, 1 lean, 2 lean with the omni order fixed at compile time
+    const int var = !lean ? 0 : a->semantics == B2S_SEM_OMNI ? 2 : 1;
+    using K = void (*)(const Params);
+    static const K kernels[2][3] = {
+        {sample_kernel<float, false, -1>, sample_kernel<float, true, -1>, sample_kernel<float, true, B2S_SEM_OMNI>},
+        {sample_kernel<__nv_bfloat16, false, -1>, sample_kernel<__nv_bfloat16, true, -1>,
+         sample_kernel<__nv_bfloat16, true, B2S_SEM_OMNI>}};
+    K kern = kernels[bf16 ? 1 : 0][var];
     {
         // the attribute is per device: remember which (device, kernel) pairs have it
         static std::mutex mu;
-        static uint64_t done[4] = {0, 0, 0, 0};
+        static uint64_t done[6] = {0, 0, 0, 0, 0, 0};
         int dev = 0;
         e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return cuda_fail(e);
         std::lock_guard<std::mutex> g(mu);
-        const int ti = (bf16 ? 1 : 0) + (lean ? 2 : 0);
+        const int ti = (bf16 ? 3 : 0) + var;
         const uint64_t bit = 1ull << (dev & 63);
         if (!(done[ti] & bit)) {
             e = set_smem_attr(kern, 227 * 1024);
