@@ -813,12 +813,12 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             }
         };
         // bit it * EPV + j: element j of vector it is >= tau_low and not a history id
-        auto hit_mask = [&](const uint4* q, int cbase) {
+        auto hit_mask = [&](const uint4* q, int cbase, int t) {
             uint32_t hm = 0u;
 #pragma unroll
             for (int it = 0; it < ITS; ++it) {
                 if (Elem<E>::vmax(q[it]) >= tau_low) {
-                    const uint32_t hb = R.hbits(cbase + (it * NT + tid) * EPV, EPV);
+                    const uint32_t hb = R.hbits(cbase + (it * NT + t) * EPV, EPV);
 #pragma unroll
                     for (int j = 0; j < EPV; ++j)
                         if (Elem<E>::at(q[it], j) >= tau_low && !((hb >> j) & 1u)) hm |= 1u << (it * EPV + j);
@@ -912,54 +912,79 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         }
         bool htv_done = false;
         if (cand_path && !ovf) {
-            // pass 2: each thread re-reads (from L2) its chunks whose maximum clears tau, two at a time so that
-            // most threads wait for one round trip
+            // pass 2: the (chunk, thread) shares whose maximum clears tau are re-read from L2.  Each warp first
+            // lists its hit shares and deals them out over its lanes, two per lane per round, so a warp needs a
+            // single round trip unless it holds more than 64 hits, however they fall among its threads.
             uint64_t hits = 0ull;
             for (int c = 0; c < nchunks; ++c) hits |= (uint64_t)(tmaxc[c * NT + tid] >= tau_low) << c;
-            auto load_at = [&](int c, uint4* q) {
+            const int wcap = p.lcap / 2;  // kv, ki, sv, si (16 * lcap bytes, free until compaction) per warp
+            uint16_t* const wl = reinterpret_cast<uint16_t*>(kv) + (tid >> 5) * wcap;
+            const int cnt = __popcll((long long)hits);
+            int incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += t;
+            }
+            const int tot = __shfl_sync(0xffffffffu, incl, 31);
+            const int nh = tot <= wcap ? tot : 0;  // more (flat rows): the warp's segment is flagged as overflowed
+            if (tot <= wcap) {
+                int pos = incl - cnt;
+                for (uint64_t h = hits; h; h &= h - 1ull)
+                    wl[pos++] = (uint16_t)(((__ffsll((long long)h) - 1) << 9) | tid);
+            }
+            __syncwarp();
+            static_assert(NT == 512, "list entries pack (chunk << 9) | thread");
+            // list entry i: its share's global position and owner thread; its vectors into q
+            auto load_share = [&](int i, uint4* q, int& cbase, int& t) {
+                int c = -1;
+                t = 0;
+                if (i < nh) {
+                    const int e = wl[i];
+                    c = e >> 9;
+                    t = e & (NT - 1);
+                }
+                cbase = c >= 0 ? R.e0 + c * VPC * EPV : -1;
                 const int vn = c >= 0 ? min(VPC, R.nvec - c * VPC) : 0;
 #pragma unroll
                 for (int it = 0; it < ITS; ++it) {
-                    const int vl = it * NT + tid;
+                    const int vl = it * NT + t;
                     q[it] = vl < vn ? __ldg(R.gvec + (size_t)c * VPC + vl)
                                     : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
                 }
             };
-            auto place_all = [&](const uint4* q, uint32_t hm, int cbase, int pos) {
+            auto place_all = [&](const uint4* q, uint32_t hm, int cbase, int t, int pos) {
 #pragma unroll
                 for (int it = 0; it < ITS; ++it) {
                     uint32_t m = (hm >> (it * EPV)) & ((1u << EPV) - 1u);
                     while (m) {
                         const int j = __ffs(m) - 1;
                         m &= m - 1u;
-                        place(Elem<E>::at(q[it], j), cbase + (it * NT + tid) * EPV + j, pos++);
+                        place(Elem<E>::at(q[it], j), cbase + (it * NT + t) * EPV + j, pos++);
                     }
                 }
             };
-            // the first round's loads go out, the history values are computed while they are in flight
-            auto next_hit = [&]() {
-                const int c = hits ? __ffsll((long long)hits) - 1 : -1;
-                if (hits) hits &= hits - 1ull;
-                return c;
-            };
-            int c1 = next_hit(), c2 = next_hit();
+            int i1 = lane, i2 = lane + 32;
+            int cb1, cb2, t1, t2;
             uint4 q1[ITS], q2[ITS];
-            load_at(c1, q1);
-            load_at(c2, q2);
+            load_share(i1, q1, cb1, t1);
+            load_share(i2, q2, cb2, t2);
+            // the history values are computed while the first round's loads are in flight
             if (!split) compute_htv();
             htv_done = true;
             for (;;) {
-                const uint32_t h1 = c1 >= 0 ? hit_mask(q1, R.e0 + c1 * VPC * EPV) : 0u;
-                const uint32_t h2 = c2 >= 0 ? hit_mask(q2, R.e0 + c2 * VPC * EPV) : 0u;
+                const uint32_t h1 = cb1 >= 0 ? hit_mask(q1, cb1, t1) : 0u;
+                const uint32_t h2 = cb2 >= 0 ? hit_mask(q2, cb2, t2) : 0u;
                 const int pos = seg_reserve(__popc(h1) + __popc(h2));
-                if (h1) place_all(q1, h1, R.e0 + c1 * VPC * EPV, pos);
-                if (h2) place_all(q2, h2, R.e0 + c2 * VPC * EPV, pos + __popc(h1));
-                if (!__any_sync(0xffffffffu, hits != 0ull)) break;
-                c1 = next_hit();
-                c2 = next_hit();
-                load_at(c1, q1);
-                load_at(c2, q2);
+                if (h1) place_all(q1, h1, cb1, t1, pos);
+                if (h2) place_all(q2, h2, cb2, t2, pos + __popc(h1));
+                i1 += 64;
+                i2 += 64;
+                if (i1 - lane >= nh) break;  // the round's first entry: the same in every lane
+                load_share(i1, q1, cb1, t1);
+                load_share(i2, q2, cb2, t2);
             }
+            if (tot > wcap) wn = seg + 1;
             // the ragged head / tail
             if ((tid >> 5) == NWARP - 1) {
                 const bool eh = edge_i >= 0 && edge_x >= tau_low && !R.hbit(edge_i);
