@@ -442,3 +442,29 @@ def test_shard_candidates_merge_equal_unsharded(pkg):
         got = vs.merge_candidates([c[0] for c in cand], [c[1] for c in cand], [c[2] for c in cand], I.THINKER_V,
                                   steps, seeds, cfg, uniform_values=u).cpu().numpy()
         assert np.array_equal(got, want), kind
+
+
+@pytest.mark.parametrize("sem", ["omni", "hf"])
+def test_flat_and_tied_thinker_rows(pkg, sem):
+    """Thinker-size rows where most (chunk, thread) shares clear the first threshold: a flat row, a row whose
+    upper half ties at its maximum, and a plain row beside them.  A warp then holds more hit shares than its
+    pass-2 list has room for, and the row must finish on the full-row path with the oracle's bits, with and
+    without the processed-logits output."""
+    ts = pkg.talker_sampler
+    g = I.rng(123)
+    V, B = 151_936, 4
+    logits = np.zeros((B, V), np.float32)
+    logits[1] = np.where(g.random(V) < 0.5, 1.0, np.round(g.standard_normal(V) * 16) / 16 - 2.0)
+    logits[2] = np.round(g.standard_normal(V) * 4) / 4
+    logits[3] = g.standard_normal(V) * 2
+    hist = g.integers(0, V, size=(B, 64))
+    cfg = C._cfg(semantics=sem, top_k=20, top_p=0.8, window=64, min_new_tokens=0, min_keep=1)
+    case = C._case(f"flat_{sem}", logits, "bf16", hist, np.full(B, 5), -1, cfg, 321)
+    want_p, want_t, _, _ = H.run_oracle(case)
+    got_p, got_t, status = run_gpu(ts, case)
+    assert status == 0
+    assert len(H.compare_processed(want_p, got_p)) == 0
+    assert np.array_equal(got_t, want_t), (got_t, want_t)
+    _, got_lean, status = run_gpu(ts, case, processed=False)
+    assert status == 0
+    assert np.array_equal(got_lean, want_t), (got_lean, want_t)
