@@ -8,8 +8,11 @@ repetition penalty 1.05 over a 512-token history, omni order, Philox4x32-10 unif
 top-k, top-p, draw, and the in-place history / step update.  Synthetic data, generated on the host.
 
 ``--gpus N`` (under torchrun): every rank runs its own B rows (row sharding, no collective on the data
-path; ``scaling`` = weak); timing is the max over ranks.  ``--impl reference`` times the CPU oracle (the
-reference algorithm restated in C, all host threads) on the same workload instead.
+path; ``scaling`` = weak); timing is the max over ranks, and ``value`` is the whole job's rows/s
+(``value_per_gpu`` beside it).  ``--impl reference`` times the reference's own sampler
+(``engine/talker_sampler.py``: ``processed_logits`` + ``draw`` under CPU torch on every host core, loaded
+from the bytecode that ``oracle/ref_build.py`` compiles into ``oracle/_ref``) on the same workload; the C
+restatement of the oracle is timed beside it as a second CPU figure.
 """
 
 from __future__ import annotations
@@ -210,14 +213,76 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
                       f"(oracle/sampler_oracle.c, OpenMP)"}
 
 
+def reference_cpu(w, *, steps: int = 0, warmup: int = 1, seconds: float = 10.0, threads: int = 0) -> dict:
+    """The reference's own sampler on the host cores: ``engine/talker_sampler.py`` imported unchanged from
+    its bytecode in ``oracle/_ref`` (``oracle/ref_build.py``), ``processed_logits`` + ``draw`` (counter RNG)
+    under CPU torch with every host thread; the greedy workload times the reference's
+    ``logits.float().argmax(-1)`` tail (``engine/runtime/thinker_decode.py:107``).  Each step is one batch
+    of at most 64 rows of the workload; ``steps`` > 0 times exactly that many steps, else as many as fit
+    in ``seconds``.  Rows whose configs differ (the batched Talker) run as one call per distinct config,
+    as a reference caller would."""
+    import torch
+
+    from oracle import ref_build
+
+    ref = ref_build.load()
+    threads = threads or len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    rows = min(w["rows"], 64)
+    logits, hist = make_inputs(w, rows, 1234)
+    x = torch.from_numpy(logits)
+    if w["dtype"] == "bf16":
+        x = x.to(torch.bfloat16)
+    h = torch.from_numpy(hist)
+    seeds = torch.arange(rows, dtype=torch.int64)
+    eos = w.get("eos", -1)
+    groups = [(list(range(rows)), w["temperature"], w["top_k"], w["top_p"])]
+    if "row_temperature" in w:
+        groups = [([r for r in range(rows) if r % 3 == j], w["row_temperature"][j], w["row_top_k"][j],
+                   w["row_top_p"][j]) for j in range(3)]
+    cfgs = [(torch.tensor(idx), ref.TalkerSampling(temperature=T, top_p=p, top_k=k, repetition_penalty=w["penalty"],
+                                                   window=w["window"], min_new_tokens=w.get("min_new", 0),
+                                                   max_new_tokens=1 << 40, min_keep=w.get("min_keep", 1),
+                                                   semantics=w.get("order", "omni"), rng="counter"))
+            for idx, T, k, p in groups if idx]
+
+    def one(step: int):
+        st = torch.full((rows,), step + 1, dtype=torch.int64)
+        if w.get("op") == "argmax":
+            return x.float().argmax(-1)
+        out = []
+        for idx, cfg in cfgs:
+            xs, hs, ss = (x, h, st) if len(cfgs) == 1 else (x[idx], h[idx], st[idx])
+            proc = ref.processed_logits(xs, hs, ss, eos, cfg)
+            out.append(ref.draw(proc, seeds[idx], ss))
+        return out
+
+    for i in range(max(1, warmup)):
+        one(i)
+    done, n, t0 = 0, 0, time.perf_counter()
+    while True:
+        one(n)
+        n += 1
+        done += rows
+        el = time.perf_counter() - t0
+        if (steps > 0 and n >= steps) or (steps <= 0 and el >= seconds):
+            break
+    what = "logits.float().argmax(-1)" if w.get("op") == "argmax" else "processed_logits + draw"
+    return {"value": done / el, "unit": "rows/s", "cores": threads, "kind": "reference",
+            "sample": f"{n} steps x {rows} rows of the {w['vocab']}-vocab workload in {el:.1f} s "
+                      f"(reference engine/talker_sampler.py {what}, CPU torch {torch.__version__}, "
+                      f"{threads} threads)"}
+
+
 def metric_of(w) -> str:
     if w.get("op") == "vocab_shard":
         return (f"sampled rows/s at B={w['rows']} x V={w['vocab']} over the job's vocabulary shards "
                 "(per-shard candidates + NCCL all-gather + merged draw)")
     if w.get("op") == "argmax":
-        return f"greedy rows/s at B={w['rows']} x V={w['vocab']} per GPU (argmax, first index on ties)"
-    return (f"sampled rows/s at B={w['rows']} x V={w['vocab']} per GPU "
-            "(fused penalty+temperature+top-k+top-p+draw)")
+        return (f"greedy rows/s, whole job (n_gpus x B={w['rows']} rows per GPU) at V={w['vocab']}; per GPU = "
+                "value_per_gpu (argmax, first index on ties)")
+    return (f"sampled rows/s, whole job (n_gpus x B={w['rows']} rows per GPU) at V={w['vocab']}; per GPU = "
+            "value_per_gpu (fused penalty+temperature+top-k+top-p+draw)")
 
 
 def dtype_of(w) -> str:
@@ -357,14 +422,23 @@ def run_vocab_shard(args, w, rank: int, world: int, local: int):
 
 
 def run_reference(args, w, rank: int):
-    """The reference algorithm on the host cores (the C restatement, all threads); rank 0 only."""
+    """The reference's own sampler on the host cores (``reference_cpu``: K timed steps after W warm-up
+    steps, each a batch of at most 64 rows); rank 0 only.  The oracle's C restatement is timed beside it
+    (``cpu_baseline_port``).  Without the reference bytecode the port is the baseline, and says so."""
     if rank != 0:
         return
-    cb = cpu_baseline(w, seconds=args.cpu_seconds)
+    from oracle import ref_build
+
+    port = cpu_baseline(w, seconds=min(args.cpu_seconds, 5.0))
+    if ref_build.available():
+        cb = reference_cpu(w, steps=args.steps, warmup=args.warmup)
+    else:
+        cb = dict(port, sample=port["sample"] + "; reference bytecode absent (oracle/ref_build.py not run)")
     line = {"impl": "reference", "metric": metric_of(w), "value": cb["value"], "unit": "rows/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": dtype_of(w), "data": "synthetic",
-            "config": config_of(args, w, args.gpus), "cpu_baseline": cb,
+            "value_per_gpu": cb["value"], "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_of(w),
+            "data": "synthetic", "config": config_of(args, w, args.gpus), "cpu_baseline": cb,
+            "cpu_baseline_port": port,
             "e2e": {"value": cb["value"], "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
@@ -463,6 +537,10 @@ def main():
             for i in range(n):
                 one_step(i)
         graphs.append((gr, n))
+    # one untimed replay of each graph: its upload and the first replay's cold start stay out of the timed region
+    with torch.cuda.stream(stream):
+        for gr, _ in graphs:
+            gr.replay()
     torch.cuda.synchronize()
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clocks = ClockSampler(vis.split(",")[local].strip() if vis else local)
@@ -530,9 +608,12 @@ def main():
         dist.all_reduce(et, op=dist.ReduceOp.MAX)
     e2e_value = B * world * e2e_steps / (float(et.item()) / 1e3)
 
-    cb = None
+    cb = cb_port = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_baseline(w, seconds=args.cpu_seconds)
+        from oracle import ref_build
+
+        cb_port = cpu_baseline(w, seconds=min(args.cpu_seconds, 5.0))
+        cb = reference_cpu(w, seconds=args.cpu_seconds) if ref_build.available() else cb_port
     for gr, _ in graphs:
         del gr
     graphs.clear()
@@ -544,8 +625,8 @@ def main():
     traffic = profiled_traffic(args.workload, w)
     line = {
         "metric": metric_of(w),
-        "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "value": value, "unit": "rows/s", "value_per_gpu": value / world, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": dtype_of(w), "data": "synthetic",
         "config": config_of(args, w, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -555,6 +636,7 @@ def main():
         "gpu_launches": args.steps,
         "clocks": ck,
         "cpu_baseline": cb,
+        "cpu_baseline_port": cb_port,
     }
     print(json.dumps(line))
 

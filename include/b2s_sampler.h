@@ -4,9 +4,12 @@
  * Every entry point takes plain device pointers and sizes plus a CUDA stream handle
  * (cudaStream_t passed as void*), enqueues its kernels on that stream, never synchronises,
  * never allocates, and returns B2S_OK or a B2S_ERR_* code for invalid arguments or launch
- * failures.  Errors that can only be seen on the device (history ids >= vocab, a per-row
- * top_k above the declared bound, a timed-out wait) are OR-ed into an optional device status
- * word and the affected row yields token PAD (-1); there are no device traps.
+ * failures.  Conditions that can only be seen on the device are OR-ed into an optional device
+ * status word (B2S_STATUS_*); there are no device traps.  A history id >= vocab is ignored (the
+ * row is sampled as if that position were PAD; the reference's scatter_add would raise), a
+ * repetition count beyond the penalty table is clamped to its last entry; a per-row top_k above
+ * the declared bound, an incomplete vocabulary shard or a bounded wait that gave up make the
+ * affected row yield token PAD (-1) with its state unchanged.
  *
  * The interface replaces the reference module engine/talker_sampler.py (pure torch in the
  * reference; the reference has no native library) and the greedy argmax of the Thinker call
@@ -44,10 +47,10 @@ extern "C" {
 #define B2S_RNG_PHILOX 2  /* Philox4x32-10: key = seed, counter = (step, request) */
 
 /* bits of the device status word */
-#define B2S_STATUS_HISTORY_RANGE 1u /* a history id >= vocab was ignored */
+#define B2S_STATUS_HISTORY_RANGE 1u /* a history id >= vocab was ignored (the row is still sampled) */
 #define B2S_STATUS_TOPK_LIMIT 2u    /* a row's top_k exceeded max_top_k; the row returned PAD */
-#define B2S_STATUS_WAIT_TIMEOUT 4u  /* reserved: a bounded device wait gave up (the current kernels have none) */
-#define B2S_STATUS_COUNT_LIMIT 8u   /* a token repeated more times than alpha_len-1 in the history */
+#define B2S_STATUS_WAIT_TIMEOUT 4u  /* a bounded device wait gave up; the row returned PAD */
+#define B2S_STATUS_COUNT_LIMIT 8u   /* a token repeated more than alpha_len-1 times; its count was clamped */
 #define B2S_STATUS_SHARD_INCOMPLETE 16u /* a shard's candidate list overflowed `cap` or failed; the row returned PAD */
 
 /* flags */

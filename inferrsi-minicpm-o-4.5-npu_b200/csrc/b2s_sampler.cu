@@ -1362,43 +1362,47 @@ __global__ void __launch_bounds__(NT, 2) argmax_kernel(const void* logits, int V
 
 // ---------------------------------------------------------------- standalone repetition penalty
 
-// grid (chunks, rows): copy the chunk to fp32, then overwrite the history ids of the chunk with their
-// penalised value (the same CTA, after a barrier, so the overwrite wins).
+// grid (chunks, row groups): copy the chunk to fp32, then overwrite the history ids of the chunk with their
+// penalised value (the same CTA, after a barrier, so the overwrite wins).  A CTA takes the rows
+// blockIdx.y, blockIdx.y + gridDim.y, ... so that any row count fits the grid's y limit.
 template <typename E>
-__global__ void __launch_bounds__(NT) penalty_kernel(const void* x, int V, int64_t xstride, const int64_t* hist, int W,
-                                                     int64_t hstride, const float* alpha, int alpha_len,
-                                                     int alpha_stride, float* out, int64_t ostride, int chunk,
-                                                     uint32_t slots, uint32_t* status) {
+__global__ void __launch_bounds__(NT) penalty_kernel(const void* x, int rows, int V, int64_t xstride,
+                                                     const int64_t* hist, int W, int64_t hstride, const float* alpha,
+                                                     int alpha_len, int alpha_stride, float* out, int64_t ostride,
+                                                     int chunk, uint32_t slots, uint32_t* status) {
     extern __shared__ __align__(16) uint32_t ht[];
-    const int r = blockIdx.y, tid = threadIdx.x;
+    const int tid = threadIdx.x;
     const int lo = blockIdx.x * chunk, hi = min(V, lo + chunk);
-    const unsigned char* rowp = reinterpret_cast<const unsigned char*>(x) + (int64_t)r * xstride * Elem<E>::SZ;
-    float* orow = out + (int64_t)r * ostride;
-    for (int i = lo + tid; i < hi; i += NT) orow[i] = Elem<E>::gld(rowp, i);
-    for (uint32_t s = tid; s < slots; s += NT) ht[s] = HT_EMPTY;
-    __syncthreads();
-    const int64_t* h = hist + (int64_t)r * hstride;
-    for (int j = tid; j < W; j += NT) {
-        const int64_t id = h[j];
-        if (id < 0) continue;
-        if (id >= V) {
-            if (blockIdx.x == 0 && status) atomicOr(status, B2S_STATUS_HISTORY_RANGE);
-            continue;
+    for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+        const unsigned char* rowp = reinterpret_cast<const unsigned char*>(x) + (int64_t)r * xstride * Elem<E>::SZ;
+        float* orow = out + (int64_t)r * ostride;
+        for (int i = lo + tid; i < hi; i += NT) orow[i] = Elem<E>::gld(rowp, i);
+        for (uint32_t s = tid; s < slots; s += NT) ht[s] = HT_EMPTY;
+        __syncthreads();
+        const int64_t* h = hist + (int64_t)r * hstride;
+        for (int j = tid; j < W; j += NT) {
+            const int64_t id = h[j];
+            if (id < 0) continue;
+            if (id >= V) {
+                if (blockIdx.x == 0 && status) atomicOr(status, B2S_STATUS_HISTORY_RANGE);
+                continue;
+            }
+            if (id >= lo && id < hi) ht_insert(ht, slots, (uint32_t)(id - lo), 1u);
         }
-        if (id >= lo && id < hi) ht_insert(ht, slots, (uint32_t)(id - lo), 1u);
-    }
-    __syncthreads();
-    const float* al = alpha + (int64_t)r * alpha_stride;
-    for (uint32_t s = tid; s < slots; s += NT) {
-        const uint32_t w = ht[s];
-        if (w == HT_EMPTY) continue;
-        const int i = lo + (int)(w >> HT_CNT_BITS);
-        int n = (int)(w & ((1u << HT_CNT_BITS) - 1));
-        if (n >= alpha_len) {
-            if (status) atomicOr(status, B2S_STATUS_COUNT_LIMIT);
-            n = alpha_len - 1;
+        __syncthreads();
+        const float* al = alpha + (int64_t)r * alpha_stride;
+        for (uint32_t s = tid; s < slots; s += NT) {
+            const uint32_t w = ht[s];
+            if (w == HT_EMPTY) continue;
+            const int i = lo + (int)(w >> HT_CNT_BITS);
+            int n = (int)(w & ((1u << HT_CNT_BITS) - 1));
+            if (n >= alpha_len) {
+                if (status) atomicOr(status, B2S_STATUS_COUNT_LIMIT);
+                n = alpha_len - 1;
+            }
+            orow[i] = pen(Elem<E>::gld(rowp, i), n, al);
         }
-        orow[i] = pen(Elem<E>::gld(rowp, i), n, al);
+        __syncthreads();  // the table is reset for the next row
     }
 }
 
@@ -1414,13 +1418,20 @@ __global__ void uniform_kernel(const int64_t* seeds, const int64_t* steps, const
 // ================================================================ host side (C-ABI)
 
 namespace {
-
 thread_local char g_cuda_err[256] = "";
+}  // namespace
 
+namespace b2s {
+// Records a failed CUDA runtime call for b2s_last_cuda_error() (every launcher of the library reports
+// through it) and returns B2S_ERR_CUDA.
 int cuda_fail(cudaError_t e) {
     snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
     return B2S_ERR_CUDA;
 }
+}  // namespace b2s
+
+namespace {
+using b2s::cuda_fail;
 
 uint32_t align_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 int next_pow2(int x) {
@@ -1734,15 +1745,15 @@ int b2s_repetition_penalty(const void* x, int32_t x_dtype, int32_t rows, int32_t
     const int chunk = 16384;
     const int ids = window < chunk ? window : chunk;
     const uint32_t slots = (uint32_t)next_pow2(2 * ids > 32 ? 2 * ids : 32);
-    dim3 grid((unsigned)((vocab + chunk - 1) / chunk), (unsigned)rows);
+    dim3 grid((unsigned)((vocab + chunk - 1) / chunk), (unsigned)(rows < 65535 ? rows : 65535));
     const size_t smem = slots * 4;
     cudaStream_t st = (cudaStream_t)stream;
     if (x_dtype == B2S_DTYPE_BF16)
-        penalty_kernel<__nv_bfloat16><<<grid, NT, smem, st>>>(x, vocab, x_row_stride, history, window,
+        penalty_kernel<__nv_bfloat16><<<grid, NT, smem, st>>>(x, rows, vocab, x_row_stride, history, window,
                                                               history_row_stride, alpha, alpha_len, alpha_row_stride,
                                                               out, out_row_stride, chunk, slots, status);
     else
-        penalty_kernel<float><<<grid, NT, smem, st>>>(x, vocab, x_row_stride, history, window, history_row_stride,
+        penalty_kernel<float><<<grid, NT, smem, st>>>(x, rows, vocab, x_row_stride, history, window, history_row_stride,
                                                       alpha, alpha_len, alpha_row_stride, out, out_row_stride, chunk,
                                                       slots, status);
     cudaError_t e = cudaGetLastError();

@@ -12,6 +12,8 @@
 
 namespace b2s {
 
+int cuda_fail(cudaError_t e);  // b2s_sampler.cu
+
 struct MergeParams {
     const float* cv;
     const int32_t* ci;
@@ -107,6 +109,7 @@ extern "C" int b2s_shard_merge(const float* cand_values, const int32_t* cand_ids
     if (!cand_values || !cand_ids || !cand_count || !a || !a->tokens) return B2S_ERR_INVALID;
     if (shards < 1 || shards > 64 || rows < 0 || cap < 1 || vocab < 1) return B2S_ERR_INVALID;
     if (a->rng == B2S_RNG_UNIFORM ? !a->uniform_values : !a->seeds) return B2S_ERR_INVALID;
+    if (a->rng != B2S_RNG_UNIFORM && !a->steps) return B2S_ERR_INVALID;  // the counter / Philox draw is keyed by the step
     if (rows == 0) return B2S_OK;
     MergeParams p;
     memset(&p, 0, sizeof(p));
@@ -134,9 +137,9 @@ extern "C" int b2s_shard_merge(const float* cand_values, const int32_t* cand_ids
     const size_t smem = (sizeof(MergeCtl) + 15) / 16 * 16 + 256 * 4 + 2 * KLIST * 4 + (size_t)p.nmax * 4 * 6;
     if (smem > 227 * 1024) return B2S_ERR_UNSUPPORTED;
     cudaError_t e = cudaFuncSetAttribute(shard_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return B2S_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_fail(e);
     shard_merge_kernel<<<(unsigned)rows, NT, smem, (cudaStream_t)stream>>>(p);
     e = cudaGetLastError();
-    if (e != cudaSuccess) return B2S_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_fail(e);
     return B2S_OK;
 }

@@ -69,7 +69,7 @@ class RowParams:
     top_p: Optional[torch.Tensor] = None        # float32
     top_k: Optional[torch.Tensor] = None        # int32
     repetition_penalty: Optional[Sequence[float]] = None
-    max_top_k: int = 0                          # host bound on top_k (0: derived from the cfg / top_k list)
+    max_top_k: int = 0                          # host bound on every row's top_k; required with ``top_k``
     min_new_tokens: Optional[torch.Tensor] = None  # int64: EOS masked while steps < min_new_tokens
     max_new_tokens: Optional[torch.Tensor] = None  # int64: EOS forced once steps >= max_new_tokens - 1
 
@@ -119,7 +119,12 @@ def alpha_table(penalty, length: int, device) -> torch.Tensor:
 
 
 def _k_bound(cfg_top_k: int, min_keep: int, rp: Optional[RowParams]) -> int:
+    """The launch's bound on k = max(top_k, min_keep) over its rows (it sizes the kernel's on-chip lists).
+    A per-row ``top_k`` tensor needs ``RowParams.max_top_k``: reading the bound off the tensor would
+    synchronise with the device, and a row above the bound would only come back as PAD."""
     kb = max(int(cfg_top_k), int(min_keep), 1)
+    if rp is not None and rp.top_k is not None and not rp.max_top_k:
+        raise ValueError("RowParams.top_k needs RowParams.max_top_k, a host bound on every row's top_k")
     if rp is not None and rp.max_top_k:
         kb = max(kb, int(rp.max_top_k), int(min_keep))
     return kb
@@ -288,7 +293,9 @@ class DecodeState:
     generators: Optional[list] = None
 
     @classmethod
-    def new(cls, seeds: list, cfg: TalkerSampling = TalkerSampling(), device="cuda") -> "DecodeState":
+    def new(cls, seeds: list, cfg: TalkerSampling = TalkerSampling(), device="cpu") -> "DecodeState":
+        """The reference's constructor and default device (``talker_sampler.py:226-231``); the sampling
+        entry points of this engine need the state on a CUDA device, so callers pass ``device``."""
         b = len(seeds)
         return cls(seeds=torch.tensor(seeds, dtype=torch.int64, device=device),
                    steps=torch.zeros(b, dtype=torch.int64, device=device),
@@ -346,8 +353,9 @@ def sample(logits: torch.Tensor, history: Optional[torch.Tensor], steps: torch.T
         uniform_values = uniform_values.to(torch.float32).contiguous()
     else:
         r = {"counter": RNG_COUNTER, "philox": RNG_PHILOX}[rng]
-    return _run(logits, history=history, steps=steps, seeds=seeds, requests=requests, uniform_values=uniform_values,
-                active=active, finished=finished, status=status, eos=eos, rng=r, cluster=cluster, **kw)[0]
+    return _run(logits, history=history, steps=_i64(steps), seeds=_i64(seeds), requests=_i64(requests),
+                uniform_values=uniform_values, active=active, finished=finished, status=status, eos=eos, rng=r,
+                cluster=cluster, **kw)[0]
 
 
 def step_(state: DecodeState, logits: torch.Tensor, eos: int, cfg: TalkerSampling = TalkerSampling(), *,

@@ -47,6 +47,7 @@ def sample(logits: torch.Tensor, history: Optional[torch.Tensor], seeds: torch.T
            cluster: int = 0) -> torch.Tensor:
     """One sampled Thinker token per row ([B] int64)."""
     ts._need_cuda(logits, history, seeds, steps, uniform_values, requests)
+    seeds, steps, requests = ts._i64(seeds), ts._i64(steps), ts._i64(requests)
     W = 0 if history is None else history.shape[-1]
     no_pen = cfg.repetition_penalty == 1.0 and cfg.presence_penalty == 0.0 and cfg.frequency_penalty == 0.0
     if cfg.temperature == 0.0 and (no_pen or W == 0):

@@ -1,10 +1,9 @@
 """Generate the golden outputs by running the REFERENCE sampler (``engine/talker_sampler.py``) on the
 cases of ``cases.py``.
 
-Run in a checkout that has the reference source (default ``/root/reference``; override with
-``REFERENCE_ROOT``):
+Run it with ``REFERENCE_ROOT`` naming a checkout of the reference source:
 
-    python -m tests.golden.make_golden
+    REFERENCE_ROOT=<reference checkout> python -m tests.golden.make_golden
 
 It writes ``tests/golden/{talker,thinker,edge,seq,rng}.npz``.  Each case stores the sha256 of its
 regenerated inputs, the reference's ``processed_logits`` output, its ``draw`` tokens with the
@@ -25,7 +24,9 @@ HERE = Path(__file__).resolve().parent
 
 
 def reference_module():
-    root = os.environ.get("REFERENCE_ROOT", "/root/reference")
+    root = os.environ.get("REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("set REFERENCE_ROOT to a checkout of the reference source")
     if root not in sys.path:
         sys.path.insert(0, root)
     from engine import talker_sampler as ts  # noqa: E402  (reference module, imported unchanged)
@@ -65,8 +66,36 @@ def run_sequence(ts, name) -> dict:
             "finished": state.finished.numpy(), "digest": np.array(C.I.digest(x))}
 
 
+def multinomial_scenario(mod):
+    """The native-RNG block of the reference (``draw_multinomial`` then
+    ``restore_multinomial_states_after_block``, ``talker_sampler.py:175-212``) on seeded CPU generators:
+    K = 4 draws per row, PAD patterns that end a row's block at every position, then one more draw from
+    the restored generators.  ``mod`` is the reference module or the engine's drop-in module."""
+    g = torch.Generator().manual_seed(3)
+    K, B, V = 4, 6, 6562
+    xs = torch.randn(K + 1, B, V, generator=g) * 2.0
+    gens = [torch.Generator().manual_seed(100 + r) for r in range(B)]
+    toks, states = [], []
+    for s in range(K):
+        toks.append(mod.draw_multinomial(xs[s], gens))
+        states.append([gen.get_state() for gen in gens])
+    host = torch.stack(toks).clone()
+    # the first PAD of each row's column: none, 0, 1, 3, 2, 1 (then 3)
+    for row, cols in ((1, [0, 1, 2, 3]), (2, [1, 2, 3]), (3, [3]), (4, [2, 3]), (5, [1, 3])):
+        host[cols, row] = mod.PAD
+    mod.restore_multinomial_states_after_block(gens, states, host)
+    after = mod.draw_multinomial(xs[K], gens)
+    return {"block_tokens": torch.stack(toks).numpy(), "host_tokens": host.numpy(), "after_restore": after.numpy()}
+
+
 def main() -> None:
     from tests.golden import cases as C
+
+    if sys.argv[1:] == ["multinomial"]:  # only the native-RNG fixture
+        ts = reference_module()
+        np.savez_compressed(HERE / "multinomial.npz", **multinomial_scenario(ts))
+        print("multinomial done")
+        return
 
     ts = reference_module()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
