@@ -56,6 +56,7 @@ extern "C" {
 /* flags */
 #define B2S_FLAG_FORCE_GENERAL 1 /* take the exact radix-select path even when the candidate path applies */
 #define B2S_FLAG_TOPK_ONLY 2     /* no top-p cut: keep every value >= the k-th largest (top_k_filter) */
+#define B2S_FLAG_STREAM 4        /* use the streaming kernel even where the row-resident one applies */
 
 typedef struct b2s_sample_args {
     /* logits [rows, vocab], row-major with logits_row_stride elements between rows */
@@ -63,7 +64,11 @@ typedef struct b2s_sample_args {
     int32_t logits_dtype;
     int32_t rows;
     int32_t vocab;
-    int32_t cluster; /* reserved (ABI version 1 field), ignored: the launcher picks one or two CTAs per row */
+    /* CTAs per row of the row-resident kernel (1, 2, 4 or 8), or 0 for the launcher's choice.  The
+     * row-resident kernel serves decode steps (tokens and/or state out, no processed or shard output, hf or
+     * omni order, k = max(top_k, min_keep) <= 128); hf takes one CTA per row.  A nonzero value for a launch
+     * it cannot serve, or whose row slice does not fit a CTA's shared memory, is B2S_ERR_UNSUPPORTED. */
+    int32_t cluster;
     int64_t logits_row_stride;
     /* penalty history [rows, window] int64 (most recent last); ids < 0 are empty (PAD) */
     const int64_t* history;

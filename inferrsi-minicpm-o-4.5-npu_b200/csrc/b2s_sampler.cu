@@ -19,8 +19,7 @@
 // Selection runs on raw values: for ids outside the history the processed value is fl(x / T), monotone in
 // x, so the order and the k-th element carry over; history ids are processed exactly.  No block in this
 // file waits on another block.
-#include "b2s_device.cuh"
-#include "b2s_list.cuh"
+#include "b2s_row.cuh"
 
 #include <cooperative_groups.h>
 #include <stdio.h>
@@ -33,430 +32,6 @@
 namespace cg = cooperative_groups;
 
 namespace b2s {
-
-constexpr int KFAST = KLIST;     // largest top_k served by the candidate path
-#ifndef B2S_CHUNK_BYTES
-#define B2S_CHUNK_BYTES 32768
-#endif
-constexpr int CHUNK = B2S_CHUNK_BYTES;  // bytes of the row a CTA takes per stream iteration
-constexpr int VPC = CHUNK / 16;         // 16-byte vectors per stream iteration
-constexpr int NBUCKET = 1024;    // buckets per threshold round
-constexpr int HPT = 4;           // history positions per thread gathered during the stream
-constexpr int MODE_FILTER = 0, MODE_FULL = 1, MODE_FORCED = 2, MODE_SKIP = 3, MODE_FAIL = 4;
-constexpr int64_t PAD = -1;
-constexpr uint32_t HT_EMPTY = 0xFFFFFFFFu;
-constexpr int HT_CNT_BITS = 14;
-
-struct Params {
-    const void* logits;
-    int64_t lstride;
-    int rows, V, W, eos;
-    const int64_t* hist;
-    int64_t hstride;
-    const int64_t* steps;
-    const int64_t* seeds;
-    const int64_t* requests;
-    const float* uvals;
-    const uint8_t* active;
-    const uint8_t* finished;
-    float T, top_p, presence, frequency;
-    int top_k, min_keep;
-    int64_t min_new, max_new;
-    const int64_t* rminn;  // per-row min_new / max_new, or nullptr
-    const int64_t* rmaxn;
-    const float* rT;
-    const float* rP;
-    const int32_t* rK;
-    const float* alpha;
-    int alpha_len, alpha_stride;
-    int sem, rng, flags;
-    int64_t* tokens;
-    float* proc;
-    int64_t pstride;
-    int64_t* hist_out;
-    int64_t hostride;
-    int64_t* steps_out;
-    uint8_t* fin_out;
-    uint32_t* status;
-    // vocabulary-shard candidate output (b2s_shard_candidates); cout_n == nullptr otherwise
-    float* cout_v;
-    int32_t* cout_i;
-    int32_t* cout_n;
-    int ccap;
-    int64_t id_off;  // global id of column 0 of these rows (history ids are global)
-    // geometry and shared-memory layout (bytes)
-    int lcap, kbuf, nvals;
-    int hcap;  // distinct history ids a row can hold (window + the censored EOS)
-    uint32_t bitwords;
-    uint32_t off_ctl, off_bits, off_pref, off_hcnt, off_hid, off_hpos, off_htv, off_smask, off_hstage, off_atab, off_cand,
-        off_candi, off_lst, off_vals, off_hist, off_hraw, off_tmaxc;
-    int tmc_chunks;  // chunks whose per-thread maxima fit (rows with more take the exact path)
-    int csplit;      // 1: two CTAs per row (a cluster): rank 1 builds the history structures, rank 0 the rest
-    uint32_t smem_total;
-};
-
-struct Ctl {
-    int err, gather_n, kn;
-    int hd_x;  // distinct history ids, from the helper CTA (two-CTA rows)
-    int wcnt[NWARP];  // candidates each warp pushed into its segment of the list
-    uint32_t rctl[2];
-    uint32_t klo, kcnt;
-    float thr;
-    float u;
-    double red_d[NWARP + 1];
-    float red_f[NWARP + 1];
-    int red_i[NWARP + 1];
-    uint32_t red_u[2 * NWARP + 2];
-};
-
-template <typename E>
-struct Elem;
-template <>
-struct Elem<float> {
-    static constexpr int SZ = 4, EPV = 4;
-    static __device__ __forceinline__ float gld(const void* base, int64_t i) {
-        return __ldg(reinterpret_cast<const float*>(base) + i);
-    }
-    static __device__ __forceinline__ float sld(const unsigned char* s) { return *reinterpret_cast<const float*>(s); }
-    static __device__ __forceinline__ float vmax(uint4 q) {
-        return fmaxf(fmaxf(__uint_as_float(q.x), __uint_as_float(q.y)), fmaxf(__uint_as_float(q.z), __uint_as_float(q.w)));
-    }
-    static __device__ __forceinline__ float at(uint4 q, int j) {
-        const uint32_t w = j == 0 ? q.x : j == 1 ? q.y : j == 2 ? q.z : q.w;
-        return __uint_as_float(w);
-    }
-    // maximum of the 4 elements, NaN if any is NaN
-    static __device__ __forceinline__ float vmax_nan(uint4 q) {
-        return fmax_nan(fmax_nan(__uint_as_float(q.x), __uint_as_float(q.y)),
-                        fmax_nan(__uint_as_float(q.z), __uint_as_float(q.w)));
-    }
-    static constexpr uint32_t NEG = 0xff800000u;  // -inf in every element of a word
-    static __device__ __forceinline__ void st_ninf(unsigned char* s) { *reinterpret_cast<uint32_t*>(s) = NEG; }
-    template <int N>
-    static __device__ __forceinline__ float vmaxn(const uint4* q) {
-        float m = vmax(q[0]);
-#pragma unroll
-        for (int t = 1; t < N; ++t) m = fmaxf(m, vmax(q[t]));
-        return m;
-    }
-};
-template <>
-struct Elem<__nv_bfloat16> {
-    static constexpr int SZ = 2, EPV = 8;
-    static __device__ __forceinline__ float gld(const void* base, int64_t i) {
-        return bf16_bits_to_f(__ldg(reinterpret_cast<const unsigned short*>(base) + i));
-    }
-    static __device__ __forceinline__ float sld(const unsigned char* s) {
-        return bf16_bits_to_f(*reinterpret_cast<const uint16_t*>(s));
-    }
-    static __device__ __forceinline__ float vmax(uint4 q) {
-        const __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&q.x), b = *reinterpret_cast<__nv_bfloat162*>(&q.y);
-        const __nv_bfloat162 c = *reinterpret_cast<__nv_bfloat162*>(&q.z), d = *reinterpret_cast<__nv_bfloat162*>(&q.w);
-        const __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
-        return fmaxf(__low2float(m), __high2float(m));
-    }
-    static __device__ __forceinline__ float at(uint4 q, int j) {
-        const uint32_t w = (j >> 1) == 0 ? q.x : (j >> 1) == 1 ? q.y : (j >> 1) == 2 ? q.z : q.w;
-        return __uint_as_float((j & 1) ? (w & 0xffff0000u) : (w << 16));
-    }
-    // maximum of the 8 elements, NaN if any is NaN (bf16 max is exact)
-    static __device__ __forceinline__ float vmax_nan(uint4 q) {
-        const __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&q.x), b = *reinterpret_cast<__nv_bfloat162*>(&q.y);
-        const __nv_bfloat162 c = *reinterpret_cast<__nv_bfloat162*>(&q.z), d = *reinterpret_cast<__nv_bfloat162*>(&q.w);
-        const __nv_bfloat162 m = __hmax2_nan(__hmax2_nan(a, b), __hmax2_nan(c, d));
-        return fmax_nan(__low2float(m), __high2float(m));
-    }
-    static constexpr uint32_t NEG = 0xff80ff80u;
-    static __device__ __forceinline__ void st_ninf(unsigned char* s) { *reinterpret_cast<uint16_t*>(s) = (uint16_t)0xff80u; }
-    // max of N x 8 bf16 values in packed bf16x2 arithmetic
-    template <int N>
-    static __device__ __forceinline__ float vmaxn(const uint4* q) {
-        __nv_bfloat162 r;
-#pragma unroll
-        for (int t = 0; t < N; ++t) {
-            const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&q[t].x);
-            const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&q[t].y);
-            const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&q[t].z);
-            const __nv_bfloat162 d = *reinterpret_cast<const __nv_bfloat162*>(&q[t].w);
-            const __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
-            r = t == 0 ? m : __hmax2(r, m);
-        }
-        return fmaxf(__low2float(r), __high2float(r));
-    }
-};
-
-__device__ __forceinline__ void set_status(const Params& p, uint32_t bits) {
-    if (p.status) atomicOr(p.status, bits);
-}
-
-// Open-addressing hash of id -> occurrence count, packed as id << 14 | count in one word (ids < 2^18).
-__device__ __forceinline__ uint32_t ht_slot(uint32_t id, uint32_t slots) { return (id * 2654435761u) & (slots - 1); }
-__device__ __forceinline__ void ht_insert(uint32_t* ht, uint32_t slots, uint32_t id, uint32_t add) {
-    uint32_t hs = ht_slot(id, slots);
-    for (uint32_t probe = 0; probe < slots; ++probe) {
-        uint32_t cur = ht[hs];
-        if (cur == HT_EMPTY) {
-            cur = atomicCAS(&ht[hs], HT_EMPTY, (id << HT_CNT_BITS) | add);
-            if (cur == HT_EMPTY) return;
-        }
-        if ((cur >> HT_CNT_BITS) == id) {
-            if (add) atomicAdd(&ht[hs], add);
-            return;
-        }
-        hs = (hs + 1) & (slots - 1);
-    }
-}
-__device__ __forceinline__ int ht_find(const uint32_t* ht, uint32_t slots, uint32_t id) {
-    uint32_t h = ht_slot(id, slots);
-    for (uint32_t probe = 0; probe < slots; ++probe) {
-        const uint32_t w = ht[h];
-        if (w == HT_EMPTY) return -1;
-        if ((w >> HT_CNT_BITS) == id) return (int)h;
-        h = (h + 1) & (slots - 1);
-    }
-    return -1;
-}
-
-__device__ __forceinline__ float pen_a(float v, int n, float a) {
-    if (n <= 0) return v;  // penalty**0 == 1: v * 1 == v / 1 == v
-    return v < 0.0f ? __fmul_rn(v, a) : __fdiv_rn(v, a);
-}
-__device__ __forceinline__ float pen(float v, int n, const float* alpha) { return n <= 0 ? v : pen_a(v, n, alpha[n]); }
-
-// Per-row context: where the row's elements live and how an element's processed value is obtained.
-template <typename E>
-struct Row {
-    const unsigned char* rowp;  // element 0 in global memory
-    const uint4* gvec;          // interior vector 0 in global memory
-    int V, nh, nvec, e0;        // head elements [0, nh); interior vectors; first interior element e0 == nh
-    const uint32_t* bits;       // history bitmap (nullptr: no history ids)
-    const uint16_t* pref;       // per 4-word group of the bitmap: the history ids below it (exclusive prefix)
-    const float* htv;           // processed value of each distinct history id, by rank
-    float T;
-    bool identity;
-    int censor;                 // element whose processed value is -inf regardless (omni censored EOS) or -1
-
-    __device__ __forceinline__ float f(float x) const { return identity ? x : __fdiv_rn(x, T); }
-    __device__ __forceinline__ bool hbit(int i) const { return bits && ((bits[i >> 5] >> (i & 31)) & 1u); }
-    // bits [i, i + n) of the history bitmap (n <= 8), packed from bit 0
-    __device__ __forceinline__ uint32_t hbits(int i, int n) const {
-        if (!bits) return 0;
-        const int w = i >> 5, o = i & 31;
-        uint32_t b = bits[w] >> o;
-        if (o + n > 32) b |= bits[w + 1] << (32 - o);
-        return b & ((1u << n) - 1u);
-    }
-    __device__ __forceinline__ float raw(int i) const { return Elem<E>::gld(rowp, i); }
-    // rank of a history id i among the row's distinct history ids (ascending id order)
-    __device__ __forceinline__ int rank(int i) const {
-        const int w = i >> 5, sub = w & 3;
-        const uint4 q = reinterpret_cast<const uint4*>(bits)[w >> 2];
-        int r = (int)pref[w >> 2];
-        r += sub > 0 ? __popc(q.x) : 0;
-        r += sub > 1 ? __popc(q.y) : 0;
-        r += sub > 2 ? __popc(q.z) : 0;
-        const uint32_t wv = sub == 0 ? q.x : sub == 1 ? q.y : sub == 2 ? q.z : q.w;
-        return r + __popc(wv & ((1u << (i & 31)) - 1u));
-    }
-    // processed value of element i (history ids and the censored EOS carry their own value)
-    __device__ __forceinline__ float P(int i, float x) const {
-        if (hbit(i)) return htv[rank(i)];
-        return f(x);
-    }
-    __device__ __forceinline__ uint4 vec(int v) const { return __ldg(gvec + v); }
-};
-
-// Visit every element of the row as (index, raw value): interior vectors round-robin over the threads,
-// head elements by thread 0, tail elements by thread 1.
-template <typename E, typename Fn>
-__device__ __forceinline__ void row_visit(const Row<E>& R, Fn fn) {
-    const int tid = threadIdx.x;
-    constexpr int EPV = Elem<E>::EPV;
-    for (int v = tid; v < R.nvec; v += NT) {
-        const uint4 q = R.vec(v);
-        const int b = R.e0 + v * EPV;
-#pragma unroll
-        for (int j = 0; j < EPV; ++j) fn(b + j, Elem<E>::at(q, j));
-    }
-    if (tid == 0)
-        for (int i = 0; i < R.nh; ++i) fn(i, Elem<E>::gld(R.rowp, i));
-    if (tid == 1)
-        for (int i = R.e0 + R.nvec * EPV; i < R.V; ++i) fn(i, Elem<E>::gld(R.rowp, i));
-}
-
-// Ordered scan of the kept mass: every element i with keep(i, P_i) contributes p_i = fl(expf(P_i - m) / s);
-// returns the first index whose fp64 prefix of p, rounded to fp32, exceeds u * total (talker_sampler.py:
-// 168-172), or V - 1.  m = max kept P, s = fl(sum expf(P - m)).  Contiguous element ranges per thread keep
-// the prefix in index order.
-template <typename E, typename Keep>
-__device__ int64_t ordered_draw(const Row<E>& R, Keep keep, float u, Ctl* ctl) {
-    const int tid = threadIdx.x;
-    const int V = R.V;
-    const int L = (V + NT - 1) / NT;
-    const int i0 = min(V, tid * L), i1 = min(V, i0 + L);
-    float lm = f_ninf();
-    for (int i = i0; i < i1; ++i) {
-        const float P = R.P(i, R.raw(i));
-        if (keep(i, P)) lm = fmaxf(lm, P);
-    }
-    const float m = block_max(lm, ctl->red_f);
-    auto e_of = [&](int i) {
-        const float P = R.P(i, R.raw(i));
-        return keep(i, P) ? b2s_expf(__fsub_rn(P, m)) : 0.0f;
-    };
-    double es = 0.0;
-    for (int i = i0; i < i1; ++i) es += (double)e_of(i);
-    const float sf = (float)block_sum(es, ctl->red_d);
-    double ps = 0.0;
-    for (int i = i0; i < i1; ++i) ps += (double)__fdiv_rn(e_of(i), sf);
-    double total;
-    double acc = block_excl_scan(ps, ctl->red_d, &total);
-    const float target = __fmul_rn(u, (float)total);
-    int first = 0x7fffffff;
-    for (int i = i0; i < i1; ++i) {
-        const float pi = __fdiv_rn(e_of(i), sf);
-        if (pi == 0.0f) continue;
-        acc += (double)pi;
-        if ((float)acc > target) { first = i; break; }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
-    __syncthreads();
-    if ((tid & 31) == 0) ctl->red_i[tid >> 5] = first;
-    __syncthreads();
-    int best = 0x7fffffff;
-    for (int w = 0; w < NWARP; ++w) best = min(best, ctl->red_i[w]);
-    __syncthreads();
-    return best == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)best;
-}
-
-// Radix select over the row: the key of the k-th largest processed value (1 <= k <= V).
-template <typename E>
-__device__ uint32_t row_kth_key(const Row<E>& R, int k, uint32_t* hist, Ctl* ctl) {
-    const int tid = threadIdx.x;
-    uint32_t prefix = 0, mask = 0;
-    int krem = k;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int i = tid; i < 256; i += NT) hist[i] = 0;
-        __syncthreads();
-        row_visit<E>(R, [&](int i, float x) {
-            const uint32_t kk = okey(R.P(i, x));
-            if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255u], 1u);
-        });
-        __syncthreads();
-        if (tid < 32) {
-            uint32_t c[8], s = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) { c[j] = hist[255 - 8 * tid - j]; s += c[j]; }  // 8-word stride
-            uint32_t incl = s;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-                if (tid >= o) incl += t;
-            }
-            const uint32_t excl = incl - s;
-            if (excl < (uint32_t)krem && (uint32_t)krem <= incl) {
-                uint32_t cum = excl;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    if (cum + c[j] >= (uint32_t)krem) {
-                        ctl->rctl[0] = (uint32_t)(255 - 8 * tid - j);
-                        ctl->rctl[1] = (uint32_t)krem - cum;
-                        break;
-                    }
-                    cum += c[j];
-                }
-            }
-        }
-        __syncthreads();
-        prefix |= ctl->rctl[0] << shift;
-        mask |= 0xFFu << shift;
-        krem = (int)ctl->rctl[1];
-        __syncthreads();
-    }
-    return prefix;
-}
-
-// T such that at least k of the n keys produced by key(i) are >= T, found with two rounds of a 1024-bucket
-// histogram over [min key, max key]: T is the lower edge of the bucket holding the k-th largest key (the
-// key itself when the second round resolves it).  Returns 0 when n < k.  Every thread calls it.
-template <typename KeyFn>
-__device__ uint32_t kth_key_bucket(int n, int k, KeyFn key, uint32_t* hist, Ctl* ctl) {
-    const int tid = threadIdx.x, lane = tid & 31;
-    uint32_t kmn = 0xFFFFFFFFu, kmx = 0;
-    for (int i = tid; i < n; i += NT) {
-        const uint32_t kk = key(i);
-        kmn = min(kmn, kk);
-        kmx = max(kmx, kk);
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        kmn = min(kmn, __shfl_xor_sync(0xffffffffu, kmn, o));
-        kmx = max(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
-    }
-    __syncthreads();
-    if (lane == 0) {
-        ctl->red_u[2 * (tid >> 5)] = kmn;
-        ctl->red_u[2 * (tid >> 5) + 1] = kmx;
-    }
-    __syncthreads();
-    uint32_t klo = 0xFFFFFFFFu, khi = 0;
-    for (int w = 0; w < NWARP; ++w) {
-        klo = min(klo, ctl->red_u[2 * w]);
-        khi = max(khi, ctl->red_u[2 * w + 1]);
-    }
-    if (n < k) return 0u;
-    int krem = k;
-    for (int round = 0; round < 2 && khi > klo; ++round) {
-        const uint32_t range = khi - klo;
-        const int nbits = 32 - __clz(range);
-        const int sh = nbits > 10 ? nbits - 10 : 0;
-        for (int b = tid; b < NBUCKET; b += NT) hist[b] = 0;
-        __syncthreads();
-        for (int i = tid; i < n; i += NT) {
-            const uint32_t kk = key(i);
-            if (kk >= klo && kk <= khi) atomicAdd(&hist[(kk - klo) >> sh], 1u);
-        }
-        __syncthreads();
-        if (tid < 32) {
-            // lane l owns buckets 1023-32l .. 992-32l (descending); find the lane, then the bucket inside it
-            uint32_t sum = 0;
-#pragma unroll 8
-            for (int j = 0; j < 32; ++j) sum += hist[NBUCKET - 1 - 32 * tid - ((j + tid) & 31)];  // rotated: no bank conflicts
-            uint32_t incl = sum;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-                if (tid >= o) incl += t;
-            }
-            const uint32_t excl = incl - sum;
-            const unsigned who = __ballot_sync(0xffffffffu, excl < (uint32_t)krem && (uint32_t)krem <= incl);
-            const int L = __ffs(who) - 1;  // who != 0: krem <= the total count
-            const uint32_t base = __shfl_sync(0xffffffffu, excl, L);
-            const int b = NBUCKET - 1 - 32 * L - tid;
-            const uint32_t cb = hist[b];
-            uint32_t inc2 = cb;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t t = __shfl_up_sync(0xffffffffu, inc2, o);
-                if (tid >= o) inc2 += t;
-            }
-            const unsigned who2 = __ballot_sync(0xffffffffu, base + inc2 >= (uint32_t)krem);
-            if (tid == __ffs(who2) - 1) {
-                ctl->klo = klo + ((uint32_t)b << sh);
-                ctl->kcnt = (uint32_t)krem - (base + inc2 - cb);
-            }
-        }
-        __syncthreads();
-        const uint32_t nlo = ctl->klo;
-        const uint32_t span = (1u << sh) - 1u;
-        khi = min(khi, nlo + span);
-        klo = nlo;
-        krem = (int)ctl->kcnt;
-        __syncthreads();
-    }
-    return klo;
-}
 
 // The whole row program; with a grid smaller than the batch each CTA loops over rows.
 // LEAN: a launch with neither processed output nor vocabulary-shard output (the decode step); the code of
@@ -1146,61 +721,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
                 __syncthreads();
                 if (tid == 0) cout_n[r] = ctl->kn;
             } else {
-                // values above the k-th (fewer than k), sorted, then k - count copies of the k-th
-                if (tid == 0) ctl->gather_n = 0;
-                __syncthreads();
-                row_visit<E>(R, [&](int i, float x) {
-                    const float P = R.P(i, x);
-                    if (okey(P) > kth) vals[atomicAdd(&ctl->gather_n, 1)] = P;
-                });
-                __syncthreads();
-                const int ng = ctl->gather_n;
-                int n2 = 1;
-                while (n2 < ng) n2 <<= 1;
-                for (int i = ng + tid; i < n2; i += NT) vals[i] = f_ninf();
-                __syncthreads();
-                for (int size = 2; size <= n2; size <<= 1) {
-                    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-                        for (int i = tid; i < n2; i += NT) {
-                            const int j = i ^ stride;
-                            if (j > i) {
-                                const bool desc = (i & size) == 0;
-                                const float a = vals[i], b = vals[j];
-                                if (desc ? (a < b) : (a > b)) { vals[i] = b; vals[j] = a; }
-                            }
-                        }
-                        __syncthreads();
-                    }
-                }
-                for (int i = ng + tid; i < k; i += NT) vals[i] = okey_to_f(kth);
-                __syncthreads();
-                // top-p over the k values, prefix in order (contiguous chunk per thread)
-                const int per_t = (k + NT - 1) / NT;
-                const int a0 = min(k, tid * per_t), a1 = min(k, a0 + per_t);
-                const float m = vals[0];
-                float sf = 1.0f;
-                if (!hf) {
-                    double es = 0.0;
-                    for (int i = a0; i < a1; ++i) es += (double)b2s_expf(__fsub_rn(vals[i], m));
-                    sf = (float)block_sum(es, ctl->red_d);
-                }
-                auto pk = [&](int i) {
-                    return hf ? b2s_expf(__fsub_rn(vals[i], lse)) : __fdiv_rn(b2s_expf(__fsub_rn(vals[i], m)), sf);
-                };
-                double ls = 0.0;
-                for (int i = a0; i < a1; ++i) ls += (double)pk(i);
-                double total;
-                double acc = block_excl_scan(ls, ctl->red_d, &total);
-                int cnt = 0;
-                for (int i = a0; i < a1; ++i) {
-                    const float pi = pk(i);
-                    acc += (double)pi;
-                    cnt += __fsub_rn((float)acc, pi) < top_p;
-                }
-                cnt = block_sum_i(cnt, ctl->red_i);
-                const int kept = topk_only ? k : max(min(p.min_keep, k), min(cnt, k));
-                thr = vals[kept - 1];
-                __syncthreads();
+                thr = exact_threshold<E>(R, kth, k, hf, lse, top_p, p.min_keep, topk_only, vals, ctl);
                 full = true;  // draw by the ordered scan over the elements >= thr
             }
         }
@@ -1482,6 +1003,62 @@ struct ShardOut {
     int64_t offset;
 };
 
+// Shared-memory layout of the row-resident kernel with CL CTAs per row (b2s_resident.cu); false when the row
+// slice and the structures beside it do not fit one CTA.  Fills p's resident fields and list sizes.
+static bool resident_layout(b2s::Params& p, const b2s_sample_args* a, int CL, int es, int kmax) {
+    using namespace b2s;
+    const int64_t nvec_max = (int64_t)a->vocab * es / 16;  // the widest 16-byte interior of a row
+    const int64_t sv = (nvec_max + CL - 1) / CL;
+    if (sv > (int64_t)RMAXP * RPV) return false;
+    const int kfast = kmax < KFAST ? kmax : KFAST;
+    int lcap = next_pow2(4 * kfast + 128);
+    lcap = lcap < 256 ? 256 : (lcap > 2048 ? 2048 : lcap);
+    p.cl = CL;
+    p.slice_vecs = (int)sv;
+    p.lcap = lcap;
+    // the merged list: an equal share per CTA (a CTA with more candidates than its share sends the row to the
+    // full-row path)
+    p.ltot = CL * lcap < 1024 ? CL * lcap : (lcap > 1024 ? lcap : 1024);
+    p.csplit = 0;
+    uint32_t off = 0;
+    p.off_ctl = off;
+    off = align_up(off + (uint32_t)sizeof(Ctl), 128);
+    p.off_bar = off;
+    off = align_up(off + RMAXP * 8, 128);
+    p.off_slice = off;
+    off = align_up(off + (uint32_t)sv * 16, 128);
+    p.off_bits = off;
+    off = align_up(off + p.bitwords * 4, 16);
+    p.off_pref = off;
+    off = align_up(off + p.bitwords / 4 * 2, 16);
+    p.off_hcnt = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_hid = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_hpos = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_htv = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_hraw = off;
+    off = align_up(off + (uint32_t)(a->window < HPT * NT ? a->window : HPT * NT) * 4, 16);
+    p.off_hstage = off;
+    off = align_up(off + (uint32_t)a->window * 8, 16);
+    p.off_atab = off;
+    off = align_up(off + (uint32_t)(a->window <= 0 ? 0 : a->alpha_len) * 4, 16);
+    p.off_cand = off;
+    off = align_up(off + (uint32_t)p.ltot * 4, 16);
+    p.off_candi = off;
+    off = align_up(off + (uint32_t)p.ltot * 4, 16);
+    p.off_lst = off;
+    off = align_up(off + (uint32_t)p.ltot * 16, 16);
+    p.off_vals = off;
+    off = align_up(off + (uint32_t)p.nvals * 4, 16);
+    p.off_hist = off;
+    off = align_up(off + NBUCKET * 4, 16);
+    p.smem_total = off;
+    return off <= 227 * 1024;
+}
+
 static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut* so) {
     using namespace b2s;
     if (!a || !a->logits || a->rows < 0 || a->vocab <= 0) return B2S_ERR_INVALID;
@@ -1622,6 +1199,68 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
 
     cudaError_t e;
     const bool lean = !so && !a->processed;
+    // Row-resident kernel: decode steps (no processed / shard output) of up to 128 candidates, one wave of
+    // clusters, and one CTA per row for hf (its full-row normaliser is taken from the resident row).
+    // `cluster` > 0 asks for it with that many CTAs per row; 0 lets the launcher pick the smallest that fits.
+    {
+        const bool streamed = (a->flags & B2S_FLAG_STREAM) != 0;
+        if (a->cluster != 0 && (streamed || !(a->cluster == 1 || a->cluster == 2 || a->cluster == 4 || a->cluster == 8)))
+            return B2S_ERR_INVALID;
+        const bool res_ok = lean && draws && !identity && !streamed && kmax <= KLIST;
+        int CL = 0;
+        Params rp = p;
+        if (a->cluster != 0) {
+            if (!res_ok || (a->semantics == B2S_SEM_HF && a->cluster > 1) || !resident_layout(rp, a, a->cluster, es, kmax))
+                return B2S_ERR_UNSUPPORTED;
+            CL = a->cluster;
+        } else if (res_ok) {
+            for (int c = 1; c <= 8; c <<= 1) {
+                if (a->semantics == B2S_SEM_HF && c > 1) break;
+                if ((int64_t)a->rows * c > sm_count()) break;
+                if (resident_layout(rp, a, c, es, kmax)) {
+                    CL = c;
+                    break;
+                }
+            }
+        }
+        if (CL > 0) {
+            const bool omni = a->semantics == B2S_SEM_OMNI;
+            ResKernel kern = resident_kernel_for(a->logits_dtype == B2S_DTYPE_BF16, omni);
+            {
+                static std::mutex mu;
+                static uint64_t done[4] = {0, 0, 0, 0};
+                int dev = 0;
+                e = cudaGetDevice(&dev);
+                if (e != cudaSuccess) return cuda_fail(e);
+                std::lock_guard<std::mutex> g(mu);
+                const int ti = (a->logits_dtype == B2S_DTYPE_BF16 ? 2 : 0) + (omni ? 1 : 0);
+                const uint64_t bit = 1ull << (dev & 63);
+                if (!(done[ti] & bit)) {
+                    e = set_smem_attr(kern, 227 * 1024);
+                    if (e != cudaSuccess) return cuda_fail(e);
+                    done[ti] |= bit;
+                }
+            }
+            cudaLaunchConfig_t cfg;
+            memset(&cfg, 0, sizeof(cfg));
+            cfg.gridDim = dim3((unsigned)((int64_t)a->rows * CL), 1, 1);
+            cfg.blockDim = dim3(NT, 1, 1);
+            cfg.dynamicSmemBytes = rp.smem_total;
+            cfg.stream = (cudaStream_t)stream;
+            cudaLaunchAttribute attrs[2];
+            attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attrs[0].val.programmaticStreamSerializationAllowed = 1;
+            attrs[1].id = cudaLaunchAttributeClusterDimension;
+            attrs[1].val.clusterDim.x = (unsigned)CL;
+            attrs[1].val.clusterDim.y = 1;
+            attrs[1].val.clusterDim.z = 1;
+            cfg.attrs = attrs;
+            cfg.numAttrs = CL > 1 ? 2 : 1;
+            e = cudaLaunchKernelEx(&cfg, kern, rp);
+            if (e != cudaSuccess) return cuda_fail(e);
+            return B2S_OK;
+        }
+    }
     const bool bf16 = a->logits_dtype == B2S_DTYPE_BF16;
     // variant: 0 general, 1 lean, 2 lean with the omni order fixed at compile time
     const int var = !lean ? 0 : a->semantics == B2S_SEM_OMNI ? 2 : 1;

@@ -32,6 +32,7 @@ M32 = 0xFFFFFFFF
 SEM_HF, SEM_OMNI, SEM_IDENTITY = 0, 1, 2
 RNG_UNIFORM, RNG_COUNTER, RNG_PHILOX = 0, 1, 2
 FLAG_FORCE_EXACT = 1
+FLAG_STREAM = 4  # the streaming kernel even where the row-resident one applies (include/b2s_sampler.h)
 NEVER = 1 << 62  # max_new_tokens that never forces EOS
 
 

@@ -3,7 +3,8 @@ INFRASTRUCTURE ONLY.
 
 The reference's sampling path is one pure-torch module, ``engine/talker_sampler.py``.  This recipe
 compiles that file, where it lies in the reference checkout, with ``py_compile`` into
-``oracle/_ref/talker_sampler.pyc``: a build output (git-ignored, like the oracle's ``.so``), not a copy
+``oracle/_ref/talker_sampler.refbc`` (CPython bytecode; the suffix keeps tools that skip ``*.pyc`` caches
+from dropping it): a build output (git-ignored, like the oracle's ``.so``), not a copy
 of the source.  The GPU box has no reference checkout; the bytecode travels with the built files and
 ``load()`` imports it unchanged, so ``bench.py --impl reference`` times the reference's own torch code
 on the host cores.  Nothing in the product package imports this module.
@@ -22,7 +23,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
-PYC = OUT_DIR / "talker_sampler.pyc"
+PYC = OUT_DIR / "talker_sampler.refbc"
 MODULE = Path("engine") / "talker_sampler.py"
 
 
@@ -33,7 +34,7 @@ def build(reference_root: str | os.PathLike) -> Path | None:
         return None
     OUT_DIR.mkdir(exist_ok=True)
     if not PYC.exists() or PYC.stat().st_mtime < src.stat().st_mtime:
-        tmp = PYC.with_suffix(".pyc.tmp")
+        tmp = PYC.with_suffix(".refbc.tmp")
         py_compile.compile(str(src), cfile=str(tmp), dfile=str(MODULE), doraise=True,
                            invalidation_mode=py_compile.PycInvalidationMode.UNCHECKED_HASH)
         os.replace(tmp, PYC)

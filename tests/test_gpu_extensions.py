@@ -91,7 +91,7 @@ def test_thinker_sample_entry_all_modes(pkg, kind):
     W = hist.shape[1]
     xin = I.to_bf16_bits(logits) if kind == "thinker" else logits
     steps = np.arange(B, dtype=np.int64) + 1
-    seeds = (np.arange(B, dtype=np.int64) * 0x9E3779B97F4A7C15) & ((1 << 63) - 1)
+    seeds = ((np.arange(B, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15)) & np.uint64((1 << 63) - 1)).astype(np.int64)
     u = I.rng(3).random(B, dtype=np.float32)
     hd, sd, td = (torch.from_numpy(a).to(DEV) for a in (hist, seeds, steps))
     ocfg = orc.Cfg(temperature=0.9, top_p=0.9, top_k=32, repetition_penalty=1.05, window=W, min_new_tokens=0,
