@@ -307,7 +307,8 @@ def config_of(args, w, world: int) -> dict:
             "parallelism": f"rows x{world}",
             "l2": f"{nbuf} rotating logits buffers ({nbuf * B * V * (2 if w['dtype'] == 'bf16' else 4) / 2**20:.0f}"
                   " MiB > L2)",
-            "cuda_graph_steps": 0 if args.eager else min(args.steps, 1000)}
+            "cuda_graph_steps": 0 if args.eager else min(args.steps, 1000), "kernel_path": args.path,
+            "cluster": args.cluster}
 
 
 def run_vocab_shard(args, w, rank: int, world: int, local: int):
@@ -454,6 +455,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--eager", action="store_true", help="time plain launches instead of CUDA graphs (profiling)")
+    ap.add_argument("--path", default="auto", choices=["auto", "stream", "resident"],
+                    help="sampling kernel: the launcher's choice, the streaming kernel, or the row-resident kernel")
+    ap.add_argument("--cluster", type=int, default=0, help="CTAs per row of the row-resident kernel (0: auto)")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     rank = int(os.environ.get("RANK", "0"))
@@ -519,7 +523,8 @@ def main():
                                  state.active, kw["alpha"], None, None if rp is None else rp.temperature,
                                  None if rp is None else rp.top_p, None if rp is None else rp.top_k,
                                  kw["temperature"], cfg.top_p, cfg.top_k, kw["min_keep"], cfg.min_new_tokens,
-                                 cfg.max_new_tokens, eos, kw["semantics"], ts.RNG_PHILOX, kw["max_top_k"], 0)
+                                 cfg.max_new_tokens, eos, kw["semantics"], ts.RNG_PHILOX, kw["max_top_k"],
+                                 args.cluster, ts.FLAG_STREAM if args.path == "stream" else 0)
 
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.synchronize()

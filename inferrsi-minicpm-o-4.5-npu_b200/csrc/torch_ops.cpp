@@ -176,7 +176,7 @@ Tensor sample_state_cuda(const Tensor& logits, Tensor& history, Tensor& steps, T
                          const optional<Tensor>& row_temperature, const optional<Tensor>& row_top_p,
                          const optional<Tensor>& row_top_k, double temperature, double top_p, int64_t top_k,
                          int64_t min_keep, int64_t min_new, int64_t max_new, int64_t eos, int64_t semantics, int64_t rng,
-                         int64_t max_top_k, int64_t cluster) {
+                         int64_t max_top_k, int64_t cluster, int64_t flags) {
     c10::cuda::CUDAGuard guard(logits.device());
     TORCH_CHECK(steps.is_contiguous() && finished.is_contiguous() && history.is_contiguous(),
                 "state tensors must be contiguous");
@@ -184,7 +184,7 @@ Tensor sample_state_cuda(const Tensor& logits, Tensor& history, Tensor& steps, T
     b2s_sample_args a;
     fill_args(a, logits, history, steps, seeds, c10::nullopt, uniform_values, active, finished, row_temperature,
               row_top_p, row_top_k, alpha, status, temperature, top_p, top_k, min_keep, min_new, max_new, 0.0,
-              0.0, eos, semantics, rng, max_top_k, 0, cluster);
+              0.0, eos, semantics, rng, max_top_k, flags, cluster);
     Tensor tokens = at::empty({logits.size(0)}, logits.options().dtype(at::kLong));
     a.tokens = tokens.data_ptr<int64_t>();
     a.history_out = history.numel() ? history.data_ptr<int64_t>() : nullptr;
@@ -199,7 +199,7 @@ Tensor sample_state_meta(const Tensor& logits, Tensor&, Tensor&, Tensor&, const 
                          const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
                          const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
                          const optional<Tensor>&, double, double, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
-                         int64_t, int64_t, int64_t) {
+                         int64_t, int64_t, int64_t, int64_t) {
     return at::empty({logits.size(0)}, logits.options().dtype(at::kLong));
 }
 
@@ -353,8 +353,8 @@ TORCH_LIBRARY(minicpmo_sampler, m) {
         "sample_state_(Tensor logits, Tensor(a!) history, Tensor(b!) steps, Tensor(c!) finished, Tensor? seeds, "
         "Tensor? uniform_values, Tensor? active, Tensor? alpha, Tensor? status, Tensor? row_temperature, "
         "Tensor? row_top_p, Tensor? row_top_k, float temperature, float top_p, int top_k, int min_keep, "
-        "int min_new_tokens, int max_new_tokens, int eos, int semantics, int rng, int max_top_k, int cluster) "
-        "-> Tensor tokens");
+        "int min_new_tokens, int max_new_tokens, int eos, int semantics, int rng, int max_top_k, int cluster, "
+        "int flags=0) -> Tensor tokens");
     m.def("argmax(Tensor logits) -> Tensor");
     m.def("uniform(Tensor seeds, Tensor steps, Tensor? requests, int rng) -> Tensor");
     m.def("repetition_penalty(Tensor x, Tensor history, Tensor alpha) -> Tensor");
