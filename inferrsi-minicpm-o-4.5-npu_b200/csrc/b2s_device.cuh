@@ -180,6 +180,9 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 __device__ __forceinline__ void cluster_arrive_relaxed() {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
 // Programmatic dependent launch: a kernel launched with programmatic stream serialisation may start

@@ -23,13 +23,20 @@ struct Scr {
     int* red_i;
 };
 
+// list_topk_values for lists of more than 128 items (kept out of line: decode steps rarely take it).
+static __device__ __noinline__ void list_topk_values_large(const float* cv, int n, int k, float* vals, Scr sc);
+
 // The k largest values of cv[0..n) (n >= k), descending with multiplicity, into vals[0..k).  Small lists
 // rank every item by counting (value desc, position asc: ranks are a permutation); longer ones find the
 // k-th key by radix select first and rank only the items above it.  vals needs 2*KLIST floats; lists of
 // at most 128 items use sc.hist for their ranks.
 __device__ __forceinline__ void list_topk_values(const float* cv, int n, int k, float* vals, const Scr& sc) {
     const int tid = threadIdx.x;
-    if (n <= 128) {
+    if (n > 128) {
+        list_topk_values_large(cv, n, k, vals, sc);
+        return;
+    }
+    {
         // every (item, segment of the list) pair in its own thread: S segments of L items per item, partial
         // ranks summed into sc.hist (shared atomics), so no thread walks the whole list
         uint32_t* rk = sc.hist;
@@ -51,8 +58,11 @@ __device__ __forceinline__ void list_topk_values(const float* cv, int n, int k, 
         for (int a = tid; a < n; a += NT)
             if (rk[a] < (uint32_t)k) vals[rk[a]] = cv[a];
         __syncthreads();
-        return;
     }
+}
+
+static __device__ __noinline__ void list_topk_values_large(const float* cv, int n, int k, float* vals, Scr sc) {
+    const int tid = threadIdx.x;
     if (n <= 2 * NT) {
         // cv is 16-byte aligned: four items per shared load, several loads in flight
         const float4* c4 = reinterpret_cast<const float4*>(cv);
@@ -101,7 +111,7 @@ __device__ __forceinline__ void list_topk_values(const float* cv, int n, int k, 
 // Warp 0: the value threshold of the top-p cut over vals[0..k) (hf: probabilities exp(v - lse) of the full
 // row; omni: softmax over the k values), kept count clamped to [min(min_keep, k), k]
 // (talker_sampler.py:110-115, :127-132).  Returns the threshold in lane 0..31 of warp 0.
-__device__ __forceinline__ float warp_topp_threshold(const float* vals, int k, bool hf, float lse, float top_p,
+static __device__ __noinline__ float warp_topp_threshold(const float* vals, int k, bool hf, float lse, float top_p,
                                                      int min_keep, bool topk_only) {
     const int lane = threadIdx.x & 31;
     float pk[4];
@@ -198,8 +208,8 @@ __device__ __forceinline__ int warp_draw_sorted(const float* sv, int kn, float u
 // Draw over the items >= thr (minus `drop_id` when >= 0): softmax over them, cumulative mass in vocabulary
 // order (fp64, rounded per prefix), first id whose mass exceeds u * total, else V - 1
 // (talker_sampler.py:168-172).  kv/ki and sv/si: scratch of >= n items each.  Result in every thread.
-__device__ __forceinline__ int64_t list_draw(const float* cv, const int* ci, int n, float thr, int drop_id, float u,
-                                             int V, float* kv, int* ki, float* sv, int* si, const Scr& sc) {
+static __device__ __noinline__ int64_t list_draw(const float* cv, const int* ci, int n, float thr, int drop_id, float u,
+                                          int V, float* kv, int* ki, float* sv, int* si, Scr sc) {
     const int tid = threadIdx.x;
     if (tid == 0) *sc.kn = 0;
     __syncthreads();
@@ -291,6 +301,86 @@ __device__ __forceinline__ int warp_draw32(float v, int kn, float u) {
     const float target = __fmul_rn(u, (float)total);
     const unsigned hit = __ballot_sync(0xffffffffu, valid && (float)incl > target);
     return hit ? __ffs(hit) - 1 : 0x7fffffff;
+}
+
+// One warp (no block barrier): the whole list stage for n <= 128 items and k <= 32 (n >= k).  Lane l takes
+// items l, l + 32, l + 64, l + 96: its rank among the n values (value descending, position ascending -- a
+// permutation, as list_topk_values) from 16-byte loads of cv (16-byte aligned) gives the sorted top-k values;
+// then warp_topp_threshold32, the kept items (value >= threshold, id != drop_id) compacted by ballot, their
+// vocabulary order by counting smaller ids, and warp_draw32.  vals: >= 32 floats; sv: >= 32 floats; si: >= 64
+// ints (16-byte aligned), all private to the warp.  Returns the token in every lane (V - 1 when no prefix
+// exceeds u * total), or -2 when more than 32 items are kept (the caller then runs list_sample).
+__device__ __forceinline__ int64_t warp_list_small(const float* cv, const int* ci, int n, int k, bool hf, float lse,
+                                                   float top_p, int min_keep, bool topk_only, int drop_id, float u,
+                                                   int V, float* vals, float* sv, int* si, float& thr_out) {
+    const int lane = threadIdx.x & 31;
+    float x[4];
+    int id[4], rk[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int i = lane + 32 * t;
+        x[t] = i < n ? cv[i] : __int_as_float(0xff800000);
+        id[t] = i < n ? ci[i] : -1;
+        rk[t] = 0;
+    }
+    const int nt = (n + 31) >> 5;
+    const float4* c4 = reinterpret_cast<const float4*>(cv);
+    for (int j4 = 0; j4 < ((n + 3) >> 2); ++j4) {
+        const float4 v = c4[j4];
+        const int j = 4 * j4;
+        const float w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            if (t < nt) {
+                const int i = lane + 32 * t;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    rk[t] += (j + c < n) & ((w[c] > x[t]) | ((w[c] == x[t]) & (j + c < i)));
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+        if (lane + 32 * t < n && rk[t] < k) vals[rk[t]] = x[t];
+    __syncwarp();
+    const float thr = warp_topp_threshold32(vals, k, hf, lse, top_p, min_keep, topk_only);
+    thr_out = thr;
+    // the kept items, compacted by ballot
+    int kn = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const bool keep = lane + 32 * t < n && x[t] >= thr && id[t] != drop_id;
+        const unsigned m = __ballot_sync(0xffffffffu, keep);
+        const int pos = kn + __popc(m & ((1u << lane) - 1u));
+        if (keep && pos < 32) {
+            sv[pos] = x[t];
+            si[pos] = id[t];
+        }
+        kn += __popc(m);
+    }
+    if (kn > 32) return -2;
+    __syncwarp();
+    // vocabulary order: the rank of each kept id among the kept ids (distinct)
+    const int myid = lane < kn ? si[lane] : 0x7fffffff;
+    const float myv = lane < kn ? sv[lane] : 0.0f;
+    int r = 0;
+    const int4* s4 = reinterpret_cast<const int4*>(si);
+    for (int j4 = 0; j4 < ((kn + 3) >> 2); ++j4) {
+        const int4 q = s4[j4];
+        const int j = 4 * j4;
+        r += (j < kn) & (q.x < myid);
+        r += (j + 1 < kn) & (q.y < myid);
+        r += (j + 2 < kn) & (q.z < myid);
+        r += (j + 3 < kn) & (q.w < myid);
+    }
+    __syncwarp();
+    if (lane < kn) {
+        vals[r] = myv;
+        si[32 + r] = myid;
+    }
+    __syncwarp();
+    const int pos = warp_draw32(vals[lane < kn ? lane : 0], kn, u);
+    return pos == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)si[32 + pos];
 }
 
 // The whole list stage: top-k values, top-p threshold (returned in thr_out) and, when `draw`, the token.

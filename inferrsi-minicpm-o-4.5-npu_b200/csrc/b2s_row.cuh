@@ -22,8 +22,9 @@ constexpr int NBUCKET = 1024;    // buckets per threshold round
 constexpr int HPT = 4;           // history positions per thread gathered during the stream
 constexpr int MODE_FILTER = 0, MODE_FULL = 1, MODE_FORCED = 2, MODE_SKIP = 3, MODE_FAIL = 4;
 constexpr int64_t PAD = -1;
-constexpr int RPV = 1024;  // row-resident kernel: 16-byte vectors per piece (16 KB), one bulk copy + mbarrier each
-constexpr int RMAXP = 16;  // row-resident kernel: pieces of one CTA's slice at most
+constexpr int RPV = 2048;  // row-resident kernel: 16-byte vectors per piece (32 KB), one bulk copy + mbarrier each
+constexpr int RMAXP = 8;   // row-resident kernel: pieces of one CTA's slice at most (256 KB)
+constexpr int RSH = RPV / NT;  // row-resident kernel: vectors of a thread's share of a piece
 constexpr uint32_t HT_EMPTY = 0xFFFFFFFFu;
 constexpr int HT_CNT_BITS = 14;
 
@@ -92,6 +93,8 @@ struct Ctl {
     int red_i[NWARP + 1];
     uint32_t red_u[2 * NWARP + 2];
     int rx_n[8];  // row-resident kernel: candidates each other CTA of the cluster handed over (-1: incomplete)
+    int lovf;     // row-resident kernel: a CTA's candidates are incomplete or did not fit rank 0's list
+    float rx_tau[8];  // row-resident kernel: each CTA's tau (every one bounds the row's k-th value from below)
 };
 
 template <typename E>

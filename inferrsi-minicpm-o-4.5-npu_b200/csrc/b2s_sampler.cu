@@ -1039,8 +1039,9 @@ static bool resident_layout(b2s::Params& p, const b2s_sample_args* a, int CL, in
     off = align_up(off + (uint32_t)p.hcap * 4, 16);
     p.off_htv = off;
     off = align_up(off + (uint32_t)p.hcap * 4, 16);
-    p.off_hraw = off;
-    off = align_up(off + (uint32_t)(a->window < HPT * NT ? a->window : HPT * NT) * 4, 16);
+    p.off_smask = off;
+    off = align_up(off + NT * 4, 16);
+    p.off_hraw = off;  // unused: the history ids' raw values are read from the resident slice
     p.off_hstage = off;
     off = align_up(off + (uint32_t)a->window * 8, 16);
     p.off_atab = off;
