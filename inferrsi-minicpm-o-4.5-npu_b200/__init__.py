@@ -8,7 +8,7 @@ The directory name is not a Python identifier; ``__graft_entry__.load_package()`
 ``b200_sampler``.
 """
 
-from . import _native, talker_sampler, thinker_sampler, vocab_shard  # noqa: F401
+from . import _native, seeds, talker_sampler, thinker_sampler, vocab_shard  # noqa: F401
 from .talker_sampler import (  # noqa: F401
     PAD,
     DecodeState,

@@ -91,6 +91,23 @@ def multinomial_scenario(mod):
 def main() -> None:
     from tests.golden import cases as C
 
+    if sys.argv[1:] == ["request_seed"]:  # only the request-seed fixture (engine/runtime/backend.py:51-54)
+        root = os.environ.get("REFERENCE_ROOT")
+        if not root:
+            raise SystemExit("set REFERENCE_ROOT to a checkout of the reference source")
+        sys.path.insert(0, root)
+        from types import SimpleNamespace
+
+        from engine.runtime.backend import request_seed  # noqa: E402  (reference function, imported unchanged)
+
+        ids = ["req-0", "abc", "x" * 40, "", "ümlaut-request", "7f3a9c"] + [f"chat-{i}" for i in range(10)]
+        explicit = [0, 1, 12345, -5, (1 << 63) - 1, 1 << 63, (1 << 64) + 7, -(1 << 70)]
+        np.savez_compressed(HERE / "request_seed.npz", ids=np.array(ids), by_id=np.array(
+            [request_seed(SimpleNamespace(request_id=i, seed=None)) for i in ids], np.int64),
+            explicit=np.array([str(e) for e in explicit]), by_seed=np.array(
+            [request_seed(SimpleNamespace(request_id="r", seed=e)) for e in explicit], np.int64))
+        print("request_seed done")
+        return
     if sys.argv[1:] == ["multinomial"]:  # only the native-RNG fixture
         ts = reference_module()
         np.savez_compressed(HERE / "multinomial.npz", **multinomial_scenario(ts))

@@ -61,3 +61,18 @@ def test_restore_rewinds_to_last_draw_before_pad(pkg):
         ts.restore_multinomial_states_after_block(gens[:3], states, host)
     with pytest.raises(ValueError):
         ts.draw_multinomial(torch.zeros(3, 10), gens)
+
+
+def test_request_seed_matches_reference(pkg):
+    """Request seeds (explicit seed to 63 bits, else SHA-256 of the request id) == the reference's
+    ``request_seed`` on the same requests (fixture made by running it, ``make_golden.py request_seed``)."""
+    from types import SimpleNamespace
+
+    fx = np.load(make_golden.HERE / "request_seed.npz")
+    sd = pkg.seeds
+    got = [sd.request_seed(SimpleNamespace(request_id=str(i), seed=None)) for i in fx["ids"]]
+    assert got == [int(x) for x in fx["by_id"]]
+    got = [sd.seed_of("r", int(e)) for e in fx["explicit"]]
+    assert got == [int(x) for x in fx["by_seed"]]
+    t = sd.request_seeds([SimpleNamespace(request_id="a", seed=None), SimpleNamespace(request_id="b", seed=9)])
+    assert t.dtype == torch.int64 and t.tolist() == [sd.seed_of("a"), 9]
