@@ -340,18 +340,23 @@ def run_vocab_shard(args, w, rank: int, world: int, local: int):
     del base
     cfg = ths.ThinkerSampling(temperature=w["temperature"], top_k=w["top_k"], top_p=w["top_p"], repetition_penalty=1.0,
                               window=0, rng="philox")
-    cap = 1024  # per-shard list capacity: heavy ties at the shard's 64th value
+    cap = vs.default_cap(cfg)  # per-shard list: every element above the shard's 64th value, ties up to 64
     steps = torch.ones(B, dtype=torch.int64, device=dev)
     seeds = torch.arange(B, dtype=torch.int64, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def one_step(x):
+        # stage 1 -> all-gather of [B, 2*cap+1] int32 -> stage 2 -> stage 3 -> max-all-reduce of [B] int64
         v, i, n = vs.shard_candidates(x, lo, None, steps, cfg, cap=cap, status=status)
         if world > 1:
             vv, ii, nn = vs.exchange(v, i, n)
         else:
             vv, ii, nn = v[None], i[None], n[None]
-        return vs.merge_candidates(vv, ii, nn, V, steps, seeds, cfg, rng="philox", status=status)
+        tok, pend = vs.merge(vv, ii, nn, V, steps, seeds, cfg, rng="philox", status=status)
+        out = vs.resolve(x, lo, rank, None, steps, cfg, tok, pend, status=status)
+        if world > 1:
+            dist.all_reduce(out, op=dist.ReduceOp.MAX)
+        return out
 
     for i in range(args.warmup):
         one_step(bufs[i % nbuf])
@@ -411,13 +416,14 @@ def run_vocab_shard(args, w, rank: int, world: int, local: int):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": dtype_of(w), "data": "synthetic",
         "config": {**config_of(args, w, world), "parallelism": f"vocab x{world}", "shard_columns": hi - lo,
-                   "shard_list_cap": cap, "cuda_graph_steps": 0},
+                   "shard_list_cap": cap, "cuda_graph_steps": 0, "value_per_gpu": None},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None, "bytes_per_gpu_step": per_gpu_bytes, "peak_source": peak_kind},
         "e2e": {"value": B * e2e_steps / (float(et.item()) / 1e3), "unit": "rows/s",
                 "h2d_bytes_per_step": host.numel() * host.element_size(), "d2h_bytes_per_step": B * 8,
                 "steps": e2e_steps},
-        "gpu_launches": args.steps * 2, "clocks": ck, "status_flags": bad, "cpu_baseline": None,
+        "gpu_launches": args.steps * 3, "clocks": ck, "status_flags": bad, "cpu_baseline": None,
+        "exchange_bytes_per_rank_step": B * (2 * cap + 1) * 4,
     }
     print(json.dumps(line))
 

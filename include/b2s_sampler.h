@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define B2S_ABI_VERSION 2
+#define B2S_ABI_VERSION 3
 
 /* return codes */
 #define B2S_OK 0
@@ -146,24 +146,48 @@ int b2s_uniform(const int64_t* seeds, const int64_t* steps, const int64_t* reque
  * Vocabulary-sharded head, stage 1 (no counterpart in the reference, which has no multi-device code).
  * `args` describes this rank's shard: logits [rows, shard_vocab] are the columns
  * [vocab_offset, vocab_offset + shard_vocab) of the full head; history ids and eos are global ids.
- * Omni order only.  Per row it writes every processed element >= the shard's k-th largest value
- * (k = max(top_k, min_keep)) as (value fp32, global id int32) pairs, unordered, into
- * cand_values / cand_ids [rows][cap], and the true number of such elements into cand_count[rows]
- * (> cap means the list was cut; -1 means the row failed on the device).
+ * Omni order only.  Per row it writes, as (value fp32, global id int32) pairs into cand_values /
+ * cand_ids [rows][cap], every processed element above the shard's k-th largest value
+ * (k = max(top_k, min_keep); there are fewer than k, and cap >= k is required), then elements equal to
+ * it while room is left; cand_count[rows] is the number of elements >= the k-th value (above cap: the
+ * unsent ones are ties at the k-th value, the smallest value sent; -1: the row failed on the device).
  */
 int b2s_shard_candidates(const b2s_sample_args* args, int64_t vocab_offset, int32_t cap, float* cand_values,
                          int32_t* cand_ids, int32_t* cand_count, void* stream);
 
+/* A row whose draw falls among ties that its shard did not send (stage 2 -> stage 3). */
+typedef struct b2s_shard_pending {
+    double base;   /* cumulative mass of the kept elements before the shard, in vocabulary order */
+    float thr;     /* the row's value threshold: kept elements are >= thr */
+    float vmax;    /* the largest kept value */
+    float sf;      /* softmax normaliser of the kept set */
+    float target;  /* u * total mass: the token is the first element whose cumulative mass exceeds it */
+    int32_t shard; /* the shard holding the token, or -1 when stage 2 resolved the row */
+    int32_t pad_;
+} b2s_shard_pending;
+
 /*
  * Vocabulary-sharded head, stage 2: from the all-gathered stage-1 outputs of `shards` shards
- * (layout [shards][rows][cap], counts [shards][rows]) draw each row's token over the full vocabulary
- * `vocab`: top-k values, top-p cut, value threshold, inverse-CDF draw in global id order.  The token
- * equals b2s_sample's on the unsharded row.  Rows whose lists are incomplete get PAD and set
- * B2S_STATUS_SHARD_INCOMPLETE.  Uses args->top_k / top_p / min_keep / row_* / rng / seeds / steps /
- * requests / uniform_values / tokens / status / flags; k must be <= 128.
+ * (layout [shards][rows][cap], counts [shards][rows]) each row's top-k values (the sent values and the
+ * unsent ties), top-p cut and value threshold over the full vocabulary `vocab`, and the shard whose
+ * range holds the draw.  args->tokens[row] receives the token when every kept element of that shard
+ * was sent, else -2 with the row's pending[row] record naming the shard (pending may be NULL: such rows
+ * then get PAD and B2S_STATUS_SHARD_INCOMPLETE).  Uses args->top_k / top_p / min_keep / row_* / rng /
+ * seeds / steps / requests / uniform_values / tokens / status / flags; k must be <= 128.
  */
 int b2s_shard_merge(const float* cand_values, const int32_t* cand_ids, const int32_t* cand_count, int32_t shards,
-                    int32_t rows, int32_t cap, int32_t vocab, const b2s_sample_args* args, void* stream);
+                    int32_t rows, int32_t cap, int32_t vocab, const b2s_sample_args* args,
+                    b2s_shard_pending* pending, void* stream);
+
+/*
+ * Vocabulary-sharded head, stage 3, on the rank of shard `shard` (args and vocab_offset as in stage 1):
+ * tokens_out[row] = merged[row] for rows stage 2 resolved, the global id of the row's token for rows
+ * pending on this shard (a scan of the shard row's processed elements in vocabulary order from the
+ * record's mass), -1 for rows pending on other shards.  A max-all-reduce of tokens_out over the shards'
+ * ranks gives every rank the tokens of b2s_sample on the unsharded row.
+ */
+int b2s_shard_resolve(const b2s_sample_args* args, int64_t vocab_offset, int32_t shard,
+                      const b2s_shard_pending* pending, const int64_t* merged, int64_t* tokens_out, void* stream);
 
 /*
  * Count-based repetition penalty on its own: out = x * penalty**n where x < 0, x / penalty**n otherwise,

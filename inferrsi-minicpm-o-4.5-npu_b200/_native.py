@@ -53,7 +53,9 @@ CAPI_SIGNATURES = {
                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "b2s_shard_merge": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(SampleArgs),
-                                       ctypes.c_void_p]),
+                                       ctypes.c_void_p, ctypes.c_void_p]),
+    "b2s_shard_resolve": (ctypes.c_int, [ctypes.POINTER(SampleArgs), ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "b2s_repetition_penalty": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_int64, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                               ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,

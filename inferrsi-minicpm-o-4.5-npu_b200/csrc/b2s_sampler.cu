@@ -678,21 +678,24 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             }
             exact = false;
             if (cout_n) {
-                // vocabulary shard: every candidate >= this shard's k-th value
+                // vocabulary shard: every candidate above this shard's k-th value (fewer than k <= cap), then the ones
+                // equal to it while room is left; the count is of every element >= the k-th value
                 list_topk_values(cv, n, k, vals, sc);
                 const float kth = vals[k - 1];
                 if (tid == 0) ctl->kn = 0;
                 __syncthreads();
-                for (int i = tid; i < n; i += NT) {
-                    if (cv[i] >= kth) {
-                        const int pos = atomicAdd(&ctl->kn, 1);
-                        if (pos < p.ccap) {
-                            p.cout_v[(int64_t)r * p.ccap + pos] = cv[i];
-                            p.cout_i[(int64_t)r * p.ccap + pos] = (int32_t)(ci[i] + p.id_off);
+                for (int pass = 0; pass < 2; ++pass) {
+                    for (int i = tid; i < n; i += NT) {
+                        if (pass == 0 ? cv[i] > kth : cv[i] == kth) {
+                            const int pos = atomicAdd(&ctl->kn, 1);
+                            if (pos < p.ccap) {
+                                p.cout_v[(int64_t)r * p.ccap + pos] = cv[i];
+                                p.cout_i[(int64_t)r * p.ccap + pos] = (int32_t)(ci[i] + p.id_off);
+                            }
                         }
                     }
+                    __syncthreads();
                 }
-                __syncthreads();
                 if (tid == 0) cout_n[r] = ctl->kn;
             } else {
                 const int64_t t = list_sample(cv, ci, n, k, hf, lse, top_p, p.min_keep, topk_only, wants_draw,
@@ -706,19 +709,22 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         if (exact && !row_err && mode == MODE_FILTER) {
             const uint32_t kth = row_kth_key<E>(R, k, hist, ctl);
             if (cout_n) {
+                // as above: the elements above the k-th key first, then the ones equal to it
                 if (tid == 0) ctl->kn = 0;
                 __syncthreads();
-                row_visit<E>(R, [&](int i, float x) {
-                    const float P = R.P(i, x);
-                    if (okey(P) >= kth) {
-                        const int pos = atomicAdd(&ctl->kn, 1);
-                        if (pos < p.ccap) {
-                            p.cout_v[(int64_t)r * p.ccap + pos] = P;
-                            p.cout_i[(int64_t)r * p.ccap + pos] = (int32_t)(i + p.id_off);
+                for (int pass = 0; pass < 2; ++pass) {
+                    row_visit<E>(R, [&](int i, float x) {
+                        const float P = R.P(i, x);
+                        if (pass == 0 ? okey(P) > kth : okey(P) == kth) {
+                            const int pos = atomicAdd(&ctl->kn, 1);
+                            if (pos < p.ccap) {
+                                p.cout_v[(int64_t)r * p.ccap + pos] = P;
+                                p.cout_i[(int64_t)r * p.ccap + pos] = (int32_t)(i + p.id_off);
+                            }
                         }
-                    }
-                });
-                __syncthreads();
+                    });
+                    __syncthreads();
+                }
                 if (tid == 0) cout_n[r] = ctl->kn;
             } else {
                 thr = exact_threshold<E>(R, kth, k, hf, lse, top_p, p.min_keep, topk_only, vals, ctl);
@@ -1321,6 +1327,10 @@ int b2s_sample(const b2s_sample_args* a, void* stream) { return launch_sample(a,
 int b2s_shard_candidates(const b2s_sample_args* a, int64_t vocab_offset, int32_t cap, float* cand_values,
                          int32_t* cand_ids, int32_t* cand_count, void* stream) {
     if (!a || !cand_values || !cand_ids || !cand_count || cap < 1 || vocab_offset < 0) return B2S_ERR_INVALID;
+    {
+        const int kb = a->max_top_k > 0 ? a->max_top_k : a->top_k;
+        if (cap < (kb > a->min_keep ? kb : a->min_keep)) return B2S_ERR_INVALID;  // every element above the k-th fits
+    }
     if (a->semantics != B2S_SEM_OMNI) return B2S_ERR_UNSUPPORTED;  // hf needs the full-row normaliser
     if (a->processed || a->history_out || a->steps_out || a->finished_out) return B2S_ERR_INVALID;
     if (vocab_offset + a->vocab > (int64_t)INT32_MAX) return B2S_ERR_UNSUPPORTED;

@@ -250,7 +250,7 @@ std::tuple<Tensor, Tensor, Tensor> shard_candidates_meta(
 }
 
 // values / ids: [shards, rows, cap]; counts: [shards, rows]
-Tensor shard_merge_cuda(const Tensor& values, const Tensor& ids, const Tensor& counts, int64_t vocab,
+std::tuple<Tensor, Tensor> shard_merge_cuda(const Tensor& values, const Tensor& ids, const Tensor& counts, int64_t vocab,
                         const optional<Tensor>& steps, const optional<Tensor>& seeds, const optional<Tensor>& requests,
                         const optional<Tensor>& uniform_values, const optional<Tensor>& row_top_p,
                         const optional<Tensor>& row_top_k, const optional<Tensor>& status, double top_p,
@@ -280,18 +280,57 @@ Tensor shard_merge_cuda(const Tensor& values, const Tensor& ids, const Tensor& c
     a.rng = (int32_t)rng;
     a.flags = (int32_t)flags;
     Tensor tokens = at::empty({B}, values.options().dtype(at::kLong));
+    // one b2s_shard_pending record per row (32 bytes), kept opaque on the Python side
+    static_assert(sizeof(b2s_shard_pending) == 32, "b2s_shard_pending is 32 bytes");
+    Tensor pending = at::empty({B, 4}, values.options().dtype(at::kLong));
     a.tokens = tokens.data_ptr<int64_t>();
     check_rc(b2s_shard_merge(values.data_ptr<float>(), ids.data_ptr<int32_t>(), counts.data_ptr<int32_t>(), (int32_t)S,
-                             (int32_t)B, (int32_t)cap, (int32_t)vocab, &a, at::cuda::getCurrentCUDAStream().stream()),
+                             (int32_t)B, (int32_t)cap, (int32_t)vocab, &a,
+                             reinterpret_cast<b2s_shard_pending*>(pending.data_ptr<int64_t>()),
+                             at::cuda::getCurrentCUDAStream().stream()),
              "b2s_shard_merge");
-    return tokens;
+    return {tokens, pending};
 }
 
-Tensor shard_merge_meta(const Tensor& values, const Tensor&, const Tensor&, int64_t, const optional<Tensor>&,
-                        const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
-                        const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&, double, int64_t,
-                        int64_t, int64_t, int64_t) {
-    return at::empty({values.size(1)}, values.options().dtype(at::kLong));
+std::tuple<Tensor, Tensor> shard_merge_meta(const Tensor& values, const Tensor&, const Tensor&, int64_t,
+                                            const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
+                                            const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
+                                            const optional<Tensor>&, double, int64_t, int64_t, int64_t, int64_t) {
+    return {at::empty({values.size(1)}, values.options().dtype(at::kLong)),
+            at::empty({values.size(1), 4}, values.options().dtype(at::kLong))};
+}
+
+// Stage 3 on this rank's shard: tokens for the rows pending on `shard`, the merged ones elsewhere, -1 for the rest.
+Tensor shard_resolve_cuda(const Tensor& logits, const optional<Tensor>& history, const optional<Tensor>& steps,
+                          const optional<Tensor>& alpha, const optional<Tensor>& row_temperature,
+                          const optional<Tensor>& status, const Tensor& pending, const Tensor& merged,
+                          double temperature, double presence, double frequency, int64_t eos, int64_t min_new,
+                          int64_t offset, int64_t shard) {
+    c10::cuda::CUDAGuard guard(logits.device());
+    const int64_t B = logits.size(0);
+    TORCH_CHECK(pending.is_cuda() && pending.dim() == 2 && pending.size(0) == B && pending.size(1) == 4 &&
+                    pending.scalar_type() == at::kLong && pending.is_contiguous(),
+                "pending must be the [rows, 4] int64 CUDA records of shard_merge");
+    TORCH_CHECK(merged.is_cuda() && merged.numel() == B && merged.scalar_type() == at::kLong && merged.is_contiguous(),
+                "merged must be the [rows] int64 CUDA tokens of shard_merge");
+    b2s_sample_args a;
+    fill_args(a, logits, history, steps, c10::nullopt, c10::nullopt, c10::nullopt, c10::nullopt, c10::nullopt,
+              row_temperature, c10::nullopt, c10::nullopt, alpha, status, temperature, 1.0, 1, 1, min_new,
+              (int64_t)1 << 62, presence, frequency, -1, B2S_SEM_OMNI, B2S_RNG_UNIFORM, 1, 0, 0);
+    a.eos = (int32_t)std::max<int64_t>(std::min<int64_t>(eos, INT32_MAX), -1);
+    Tensor out = at::empty({B}, logits.options().dtype(at::kLong));
+    check_rc(b2s_shard_resolve(&a, offset, (int32_t)shard,
+                               reinterpret_cast<const b2s_shard_pending*>(pending.data_ptr<int64_t>()),
+                               merged.data_ptr<int64_t>(), out.data_ptr<int64_t>(),
+                               at::cuda::getCurrentCUDAStream().stream()),
+             "b2s_shard_resolve");
+    return out;
+}
+
+Tensor shard_resolve_meta(const Tensor& logits, const optional<Tensor>&, const optional<Tensor>&,
+                          const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&, const Tensor&,
+                          const Tensor&, double, double, double, int64_t, int64_t, int64_t, int64_t) {
+    return at::empty({logits.size(0)}, logits.options().dtype(at::kLong));
 }
 
 Tensor penalty_cuda(const Tensor& x, const Tensor& history, const Tensor& alpha) {
@@ -366,7 +405,11 @@ TORCH_LIBRARY(minicpmo_sampler, m) {
     m.def(
         "shard_merge(Tensor values, Tensor ids, Tensor counts, int vocab, Tensor? steps, Tensor? seeds, "
         "Tensor? requests, Tensor? uniform_values, Tensor? row_top_p, Tensor? row_top_k, Tensor? status, "
-        "float top_p, int top_k, int min_keep, int rng, int flags) -> Tensor");
+        "float top_p, int top_k, int min_keep, int rng, int flags) -> (Tensor tokens, Tensor pending)");
+    m.def(
+        "shard_resolve(Tensor logits, Tensor? history, Tensor? steps, Tensor? alpha, Tensor? row_temperature, "
+        "Tensor? status, Tensor pending, Tensor merged, float temperature, float presence_penalty, "
+        "float frequency_penalty, int eos, int min_new_tokens, int offset, int shard) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(minicpmo_sampler, CUDA, m) {
@@ -377,6 +420,7 @@ TORCH_LIBRARY_IMPL(minicpmo_sampler, CUDA, m) {
     m.impl("repetition_penalty", &penalty_cuda);
     m.impl("shard_candidates", &shard_candidates_cuda);
     m.impl("shard_merge", &shard_merge_cuda);
+    m.impl("shard_resolve", &shard_resolve_cuda);
 }
 
 TORCH_LIBRARY_IMPL(minicpmo_sampler, Meta, m) {
@@ -387,4 +431,5 @@ TORCH_LIBRARY_IMPL(minicpmo_sampler, Meta, m) {
     m.impl("repetition_penalty", &penalty_meta);
     m.impl("shard_candidates", &shard_candidates_meta);
     m.impl("shard_merge", &shard_merge_meta);
+    m.impl("shard_resolve", &shard_resolve_meta);
 }

@@ -1,18 +1,19 @@
-"""Vocabulary-sharded Thinker sampling across the GPUs of one node (no counterpart in the reference, which
-runs on a single device).
+"""Vocabulary-sharded Thinker sampling across the GPUs of one node (no counterpart in the reference, which runs on a
+single device).
 
 Rank s holds logits for the contiguous columns [offset_s, offset_s + V_s) of the LM head.  One step:
 
-1. ``shard_candidates`` (kernel): the shard's processed values (omni order: penalty -> /T) and every
-   element >= the shard's k-th largest value, as (value, global id) pairs, plus their count;
-2. one ``all_gather_into_tensor`` over NCCL of the packed [rows, 2*cap+1] int32 buffer (values as bits,
-   ids, count) -- the only exchange;
-3. ``merge_candidates`` (kernel, on every rank): global top-k values, top-p cut, threshold, and the draw in
-   global id order.  Every rank computes the same token, so nothing else is exchanged.
+1. ``shard_candidates`` (kernel): the shard's processed values (omni order: penalty -> /T) -- every element above
+   the shard's k-th largest value, then elements equal to it up to ``cap`` >= k, as (value, global id) pairs, and the
+   count of every element >= the shard's k-th value.  With ``cap = k`` a row costs 8k + 4 bytes.
+2. one ``all_gather_into_tensor`` over NCCL of the packed [rows, 2*cap+1] int32 buffer (values as bits, ids, count).
+3. ``merge`` (kernel, on every rank): the row's top-k values (the sent ones and, by value and count, the ties a shard
+   did not send), the top-p cut, the value threshold, and the shard whose range holds the draw; the token when that
+   shard sent all its kept elements, else a pending record naming it.
+4. ``resolve`` (kernel, on every rank): the pending shard's rank scans its row in vocabulary order for the token;
+   one max-all-reduce of [rows] int64 gives every rank the same tokens.
 
-A shard list that overflows ``cap`` (more ties at its k-th value than fit) makes that row's token PAD and
-sets a status bit; it is never silently wrong.  The result equals the unsharded kernel's token on the
-concatenated row.
+The tokens equal the unsharded kernel's on the concatenated row, however many elements tie at the threshold.
 """
 
 from __future__ import annotations
@@ -30,32 +31,36 @@ def _k(cfg) -> int:
 
 
 def default_cap(cfg) -> int:
-    k = _k(cfg)
-    c = 1
-    while c < 2 * k:
-        c <<= 1
-    return max(c, 32)
+    """The list capacity per shard and row: k (every element above the shard's k-th value fits)."""
+    return _k(cfg)
+
+
+def _alpha(cfg, history, device):
+    W = 0 if history is None else history.shape[-1]
+    return ts.alpha_table(cfg.repetition_penalty, W + 1, device) if W > 0 else None
 
 
 def shard_candidates(logits: torch.Tensor, offset: int, history: Optional[torch.Tensor], steps: torch.Tensor, cfg, *,
                      cap: Optional[int] = None, eos: int = -1, status: Optional[torch.Tensor] = None,
                      cluster: int = 0):
-    """Stage 1 on this rank's shard ``logits`` [B, V_s] (columns start at global id ``offset``; history ids
-    are global).  Returns (values [B, cap] fp32, ids [B, cap] int32 global, count [B] int32)."""
+    """Stage 1 on this rank's shard ``logits`` [B, V_s] (columns start at global id ``offset``; history ids are
+    global).  Returns (values [B, cap] fp32, ids [B, cap] int32 global, count [B] int32)."""
     ts._need_cuda(logits, history, steps)
     cap = cap or default_cap(cfg)
-    W = 0 if history is None else history.shape[-1]
-    alpha = ts.alpha_table(cfg.repetition_penalty, W + 1, logits.device) if W > 0 else None
+    if cap < _k(cfg):
+        raise ValueError(f"cap ({cap}) must be >= top_k ({_k(cfg)})")
     return _native.ops().shard_candidates(
-        logits, history, steps.to(torch.int64), alpha, None, None, None, status, ts._temperature(cfg.temperature),
-        float(cfg.top_p), int(cfg.top_k), 1, float(getattr(cfg, "presence_penalty", 0.0)),
-        float(getattr(cfg, "frequency_penalty", 0.0)), int(eos), _k(cfg), int(offset), int(cap), int(cluster))
+        logits, history, steps.to(torch.int64), _alpha(cfg, history, logits.device), None, None, None, status,
+        ts._temperature(cfg.temperature), float(cfg.top_p), int(cfg.top_k), 1,
+        float(getattr(cfg, "presence_penalty", 0.0)), float(getattr(cfg, "frequency_penalty", 0.0)), int(eos), _k(cfg),
+        int(offset), int(cap), int(cluster))
 
 
-def merge_candidates(values, ids, counts, vocab: int, steps: torch.Tensor, seeds: Optional[torch.Tensor], cfg, *,
-                     uniform_values: Optional[torch.Tensor] = None, requests: Optional[torch.Tensor] = None,
-                     rng: str = "philox", status: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Stage 2 over all shards' candidates (lists of per-shard tensors, or stacked [S, B, cap] / [S, B])."""
+def merge(values, ids, counts, vocab: int, steps: torch.Tensor, seeds: Optional[torch.Tensor], cfg, *,
+          uniform_values: Optional[torch.Tensor] = None, requests: Optional[torch.Tensor] = None,
+          rng: str = "philox", status: Optional[torch.Tensor] = None):
+    """Stage 2 over all shards' candidates (lists of per-shard tensors, or stacked [S, B, cap] / [S, B]).
+    Returns (tokens [B] int64 -- -2 where the row is pending --, pending [B, 4] int64 records)."""
     if isinstance(values, (list, tuple)):
         values, ids, counts = torch.stack(list(values)), torch.stack(list(ids)), torch.stack(list(counts))
     ts._need_cuda(values, ids, counts, steps, seeds, uniform_values, requests)
@@ -67,8 +72,33 @@ def merge_candidates(values, ids, counts, vocab: int, steps: torch.Tensor, seeds
     else:
         r = {"philox": ts.RNG_PHILOX, "counter": ts.RNG_COUNTER}[rng]
     return _native.ops().shard_merge(values.contiguous(), ids.contiguous(), counts.contiguous(), int(vocab),
-                                     steps.to(torch.int64), seeds, requests, uniform_values, None, None, status,
-                                     float(cfg.top_p), int(cfg.top_k), 1, r, 0)
+                                     steps.to(torch.int64), ts._i64(seeds), ts._i64(requests), uniform_values, None,
+                                     None, status, float(cfg.top_p), int(cfg.top_k), 1, r, 0)
+
+
+def resolve(logits: torch.Tensor, offset: int, shard: int, history: Optional[torch.Tensor], steps: torch.Tensor, cfg,
+            tokens: torch.Tensor, pending: torch.Tensor, *, eos: int = -1,
+            status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Stage 3 on shard ``shard``: [B] int64 -- the tokens of the rows pending on this shard, the merged tokens of
+    resolved rows, -1 for rows pending on other shards (the max over all shards is the result)."""
+    ts._need_cuda(logits, history, steps, tokens, pending)
+    return _native.ops().shard_resolve(
+        logits, history, steps.to(torch.int64), _alpha(cfg, history, logits.device), None, status, pending, tokens,
+        ts._temperature(cfg.temperature), float(getattr(cfg, "presence_penalty", 0.0)),
+        float(getattr(cfg, "frequency_penalty", 0.0)), int(eos), 0, int(offset), int(shard))
+
+
+def merge_candidates(values, ids, counts, vocab: int, steps, seeds, cfg, *, shard_logits: Sequence[torch.Tensor],
+                     offsets: Sequence[int], history=None, uniform_values=None, requests=None, rng: str = "philox",
+                     status=None) -> torch.Tensor:
+    """Stages 2 and 3 with every shard's logits on this device (one process holding all shards): the tokens."""
+    tok, pend = merge(values, ids, counts, vocab, steps, seeds, cfg, uniform_values=uniform_values,
+                      requests=requests, rng=rng, status=status)
+    out = None
+    for s, (x, off) in enumerate(zip(shard_logits, offsets)):
+        t = resolve(x, off, s, history, steps, cfg, tok, pend, status=status)
+        out = t if out is None else torch.maximum(out, t)
+    return out
 
 
 def pack(values: torch.Tensor, ids: torch.Tensor, counts: torch.Tensor) -> torch.Tensor:
@@ -82,21 +112,6 @@ def unpack(buf: torch.Tensor, shards: int, rows: int, cap: int):
             b[:, :, 2 * cap].contiguous())
 
 
-def sample_sharded(logits: torch.Tensor, offset: int, vocab: int, history: Optional[torch.Tensor],
-                   steps: torch.Tensor, seeds: Optional[torch.Tensor], cfg, *, group=None, cap: Optional[int] = None,
-                   uniform_values: Optional[torch.Tensor] = None, requests: Optional[torch.Tensor] = None,
-                   rng: str = "philox", status: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """One sampled token per row of the full vocabulary, from this rank's shard; every rank returns the same
-    tokens.  ``group``: the torch.distributed process group of the shards (rank order = shard order)."""
-    import torch.distributed as dist
-
-    cap = cap or default_cap(cfg)
-    v, i, n = shard_candidates(logits, offset, history, steps, cfg, cap=cap, status=status)
-    vv, ii, nn = exchange(v, i, n, group=group)
-    return merge_candidates(vv, ii, nn, vocab, steps, seeds, cfg, uniform_values=uniform_values, requests=requests,
-                            rng=rng, status=status)
-
-
 def exchange(values: torch.Tensor, ids: torch.Tensor, counts: torch.Tensor, *, group=None):
     """Every shard's candidate lists on every rank: one ``all_gather_into_tensor`` of the packed buffer.
     Returns (values [S, B, cap], ids [S, B, cap], counts [S, B]) in rank order.  Works on any backend that
@@ -108,6 +123,25 @@ def exchange(values: torch.Tensor, ids: torch.Tensor, counts: torch.Tensor, *, g
     allb = torch.empty((world * mine.shape[0], mine.shape[1]), dtype=torch.int32, device=mine.device)
     dist.all_gather_into_tensor(allb, mine, group=group)
     return unpack(allb, world, mine.shape[0], values.shape[1])
+
+
+def sample_sharded(logits: torch.Tensor, offset: int, vocab: int, history: Optional[torch.Tensor],
+                   steps: torch.Tensor, seeds: Optional[torch.Tensor], cfg, *, group=None, cap: Optional[int] = None,
+                   uniform_values: Optional[torch.Tensor] = None, requests: Optional[torch.Tensor] = None,
+                   rng: str = "philox", status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One sampled token per row of the full vocabulary, from this rank's shard; every rank returns the same
+    tokens.  ``group``: the torch.distributed process group of the shards (rank order = shard order).  Two
+    collectives: the all-gather of the candidate lists and a max-all-reduce of [B] int64 tokens."""
+    import torch.distributed as dist
+
+    cap = cap or default_cap(cfg)
+    v, i, n = shard_candidates(logits, offset, history, steps, cfg, cap=cap, status=status)
+    vv, ii, nn = exchange(v, i, n, group=group)
+    tok, pend = merge(vv, ii, nn, vocab, steps, seeds, cfg, uniform_values=uniform_values, requests=requests, rng=rng,
+                      status=status)
+    out = resolve(logits, offset, dist.get_rank(group), history, steps, cfg, tok, pend, status=status)
+    dist.all_reduce(out, op=dist.ReduceOp.MAX, group=group)
+    return out
 
 
 def shard_bounds(vocab: int, shards: int) -> Sequence[int]:

@@ -74,7 +74,7 @@ def test_torch_op_library_registers_ops(pkg):
 
     pkg._native.ops()
     for op in ("sample", "sample_state_", "argmax", "uniform", "repetition_penalty", "shard_candidates",
-               "shard_merge"):
+               "shard_merge", "shard_resolve"):
         assert hasattr(torch.ops.minicpmo_sampler, op), op
 
 
@@ -84,3 +84,17 @@ def test_product_path_refuses_cpu_tensors(pkg):
     x = torch.zeros(2, 16)
     with pytest.raises(ValueError):
         pkg.thinker_sampler.argmax(x)
+
+
+def test_shard_pending_record_layout(tmp_path):
+    """b2s_shard_pending is 32 bytes with the double first: the torch layer keeps it as [rows, 4] int64."""
+    src = tmp_path / "pend.c"
+    src.write_text("\n".join([
+        "#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void) {",
+        '  printf("%zu %zu %zu %zu\\n", sizeof(b2s_shard_pending), offsetof(b2s_shard_pending, base),',
+        "         offsetof(b2s_shard_pending, thr), offsetof(b2s_shard_pending, shard));",
+        "  return 0;", "}"]) + "\n")
+    exe = tmp_path / "pend"
+    subprocess.run(["gcc", "-std=c11", "-x", "c", str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
+    assert out == ["32", "0", "8", "24"]

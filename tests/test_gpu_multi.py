@@ -53,7 +53,7 @@ def _worker(rank: int, world: int, port: int, out_q):
         seeds = torch.arange(B, dtype=torch.int64, device=dev)
         cfg = ts.ThinkerSampling(temperature=T, top_k=K, top_p=TOP_P, repetition_penalty=1.1, rng="counter")
         status = torch.zeros(1, dtype=torch.int32, device=dev)
-        tok = vs.sample_sharded(xs, lo, V, h, steps, seeds, cfg, rng="counter", status=status, cap=1024)
+        tok = vs.sample_sharded(xs, lo, V, h, steps, seeds, cfg, rng="counter", status=status)
         # the unsharded kernel on the whole row, on this rank's GPU
         full = torch.from_numpy(x).to(dev).to(torch.bfloat16)
         want = ts.sample(full, h, seeds, steps, cfg)

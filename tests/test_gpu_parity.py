@@ -439,11 +439,15 @@ def test_status_flags_and_pad_rows(pkg):
                             ts.TalkerSampling(temperature=0.0))
 
 
-def test_shard_candidates_merge_equal_unsharded(pkg):
-    """Vocabulary-sharded sampling on one GPU (8 shards run one after the other) == the unsharded kernel."""
+@pytest.mark.parametrize("rng", ["uniform", "philox"])
+def test_shard_candidates_merge_equal_unsharded(pkg, rng):
+    """Vocabulary-sharded sampling on one GPU (8 shards run one after the other: stage 1 per shard, the merge, the
+    resolve per shard, the max over shards) == the unsharded kernel, with lists capped at k: the tie-heavy rows
+    leave ties unsent, and rows whose draw falls among them are finished by their shard (stage 3)."""
     vs = pkg.vocab_shard
     ts = pkg.talker_sampler
-    for kind, B in (("cfg5", 32), ("cfg3", 16)):
+    pending_seen = 0
+    for kind, B in (("cfg5", 64), ("cfg3", 16), ("cfg4", 8)):
         case = _full_size(ts, kind, B, 7 + B)
         x = gpu_logits(case)
         hist = torch.from_numpy(case.history).to(DEV)
@@ -451,16 +455,26 @@ def test_shard_candidates_merge_equal_unsharded(pkg):
         seeds = torch.from_numpy(case.seeds).to(DEV)
         u = torch.from_numpy(case.uniforms).to(DEV)
         cfg = cfg_of(ts, case)
-        want = ts.sample(x, hist, steps, seeds, -1, cfg, uniform_values=u).cpu().numpy()
-        _, want_o, _, _ = H.run_oracle(case)
-        assert np.array_equal(want, want_o)
+        uv = u if rng == "uniform" else None
+        want = ts.sample(x, hist, steps, seeds, -1, cfg, uniform_values=uv, rng="philox").cpu().numpy()
+        if rng == "uniform":
+            _, want_o, _, _ = H.run_oracle(case)
+            assert np.array_equal(want, want_o)
         shards = 8
         Vs = I.THINKER_V // shards
-        cand = [vs.shard_candidates(x[:, s * Vs:(s + 1) * Vs].contiguous(), s * Vs, hist, steps, cfg, cap=256)
-                for s in range(shards)]
+        xs = [x[:, s * Vs:(s + 1) * Vs].contiguous() for s in range(shards)]
+        status = torch.zeros(1, dtype=torch.int32, device=DEV)
+        cand = [vs.shard_candidates(xs[s], s * Vs, hist, steps, cfg, status=status) for s in range(shards)]
+        assert cand[0][0].shape[1] == max(cfg.top_k, 1)  # cap = k
+        tok, pend = vs.merge([c[0] for c in cand], [c[1] for c in cand], [c[2] for c in cand], I.THINKER_V, steps,
+                             seeds, cfg, uniform_values=uv, rng="philox", status=status)
+        pending_seen += int((tok == -2).sum())
         got = vs.merge_candidates([c[0] for c in cand], [c[1] for c in cand], [c[2] for c in cand], I.THINKER_V,
-                                  steps, seeds, cfg, uniform_values=u).cpu().numpy()
-        assert np.array_equal(got, want), kind
+                                  steps, seeds, cfg, shard_logits=xs, offsets=[s * Vs for s in range(shards)],
+                                  history=hist, uniform_values=uv, rng="philox", status=status).cpu().numpy()
+        assert int(status.item()) == 0
+        assert np.array_equal(got, want), (kind, got, want)
+    assert pending_seen > 0  # some draws fell among unsent ties and were resolved by their shard
 
 
 @pytest.mark.parametrize("sem", ["omni", "hf"])

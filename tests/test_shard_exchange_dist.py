@@ -1,10 +1,12 @@
 """Vocabulary-sharded sampling, host side, on two gloo ranks (CPU).
 
 Each rank holds half of the vocabulary.  It builds its shard's candidate list the way
-``b2s_shard_candidates`` defines it (omni-processed values, every element >= the shard's k-th largest,
-ties kept), packs it and runs ``vocab_shard.exchange`` -- the same single ``all_gather_into_tensor`` the
-NCCL path uses.  The merged candidates, set into an otherwise -inf row, must give the token the oracle
-draws from the unsharded row: the decomposition the sharded path relies on.
+``b2s_shard_candidates`` defines it (omni-processed values: every element above the shard's k-th largest, then
+elements equal to it up to ``cap = k``, and the count of every element >= the k-th), packs it and runs
+``vocab_shard.exchange`` -- the same single ``all_gather_into_tensor`` the NCCL path uses.  From the gathered lists
+and counts alone, the row's value multiset above the threshold (the sent values plus the unsent ties' copies) must
+give the oracle's threshold on the unsharded row, and so its kept set and token: the decomposition the sharded
+path relies on, with ties heavy enough that shards leave many unsent.
 """
 
 from __future__ import annotations
@@ -61,12 +63,31 @@ def shard_list(p: np.ndarray, lo: int, hi: int, cap: int):
     for r in range(p.shape[0]):
         s = p[r, lo:hi]
         kth = np.sort(s)[-K]
-        sel = np.nonzero(s >= kth)[0]
-        assert len(sel) <= cap
-        vals[r, :len(sel)] = s[sel]
-        ids[r, :len(sel)] = sel + lo
+        sel = np.concatenate([np.nonzero(s > kth)[0], np.nonzero(s == kth)[0]])  # above first, then ties
+        m = min(len(sel), cap)
+        vals[r, :m] = s[sel[:m]]
+        ids[r, :m] = sel[:m] + lo
         cnt[r] = len(sel)
     return vals, ids, cnt
+
+
+def threshold_from_lists(vv, ii, nn, cap, r):
+    """The row's value multiset relevant to top-k (sent values, plus up to K copies of each shard's unsent ties at
+    its smallest sent value), placed in an otherwise -inf row, and its omni threshold from the oracle."""
+    vals = []
+    for s in range(vv.shape[0]):
+        c = int(nn[s, r])
+        sent = vv[s, r, :min(c, cap)]
+        vals.extend(sent.tolist())
+        if c > cap:
+            vals.extend([float(sent.min())] * min(c - cap, K))
+    row = np.full((1, V), -np.inf, np.float32)
+    row[0, :len(vals)] = np.array(vals, np.float32)
+    cfg = orc.Cfg(temperature=1.0, top_p=TOP_P, top_k=K, repetition_penalty=1.0, window=0, min_new_tokens=0,
+                  max_new_tokens=1 << 40, min_keep=1, semantics="omni")
+    proc, _, _, _ = orc.sample(row, np.zeros((1, 0), np.int64), np.full(1, 5, np.int64), None, -1, cfg,
+                               uniforms=np.zeros(1, np.float32))
+    return proc[0][~np.isneginf(proc[0])].min()
 
 
 def _worker(rank: int, world: int, port: int, cap: int):
@@ -89,26 +110,27 @@ def _worker(rank: int, world: int, port: int, cap: int):
             ref = shard_list(p, bounds[s], bounds[s + 1], cap)
             assert np.array_equal(vv[s].numpy().view(np.uint32), ref[0].view(np.uint32))
             assert np.array_equal(ii[s].numpy(), ref[1]) and np.array_equal(nn[s].numpy(), ref[2])
-        # merged candidates in a -inf row -> the same token as the unsharded row
-        row = np.full((B, V), -np.inf, np.float32)
-        for s in range(world):
-            for r in range(B):
-                c = int(nn[s, r])
-                row[r, ii[s, r, :c].numpy()] = vv[s, r, :c].numpy()
         steps = np.full(B, 5, np.int64)
         seeds = np.arange(B, dtype=np.int64)
         full = orc.Cfg(temperature=T, top_p=TOP_P, top_k=K, repetition_penalty=PEN, window=W, min_new_tokens=0,
                        max_new_tokens=1 << 40, min_keep=1, semantics="omni", presence_penalty=PRES,
                        frequency_penalty=FREQ)
-        merged = orc.Cfg(temperature=1.0, top_p=TOP_P, top_k=K, repetition_penalty=1.0, window=0, min_new_tokens=0,
-                         max_new_tokens=1 << 40, min_keep=1, semantics="omni")
-        _, want, _, _ = orc.sample(x, hist, steps, seeds, -1, full, uniforms=u)
-        p_full, _, _, _ = orc.sample(x, hist, steps, seeds, -1, full, uniforms=u)
-        _, got, _, _ = orc.sample(row, np.zeros((B, 0), np.int64), steps, seeds, -1, merged, uniforms=u)
-        assert np.array_equal(got, want), (got, want)
-        # the numpy restatement of the omni processing agrees with the oracle on every kept element
+        p_full, want, _, _ = orc.sample(x, hist, steps, seeds, -1, full, uniforms=u)
         kept = ~np.isneginf(p_full)
+        # the numpy restatement of the omni processing agrees with the oracle on every kept element
         assert np.array_equal(p_full[kept].view(np.uint32), p[kept].view(np.uint32))
+        unsent = 0
+        for r in range(B):
+            thr = threshold_from_lists(vv.numpy(), ii.numpy(), nn.numpy(), cap, r)
+            # the threshold from the capped lists and tie counts is the unsharded row's ...
+            assert thr == p_full[r][kept[r]].min(), r
+            # ... so the kept set (every element >= it) and the oracle's draw over it are the unsharded row's
+            assert np.array_equal(p[r] >= thr, kept[r]), r
+            unsent += int(sum(max(0, int(nn[s, r]) - cap) for s in range(world)))
+        assert unsent > 0  # the heavy ties left elements unsent
+        row = np.where(kept, p, np.float32(-np.inf)).astype(np.float32)
+        got, _ = orc.draw(row, u)
+        assert np.array_equal(got, want), (got, want)
     finally:
         dist.destroy_process_group()
 
@@ -123,4 +145,4 @@ def _free_port() -> int:
 def test_two_rank_exchange_matches_unsharded(world):
     import torch.multiprocessing as mp
 
-    mp.spawn(_worker, args=(world, _free_port(), 64), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), K), nprocs=world, join=True)
