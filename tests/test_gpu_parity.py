@@ -449,6 +449,15 @@ def test_shard_candidates_merge_equal_unsharded(pkg, rng):
     pending_seen = 0
     for kind, B in (("cfg5", 64), ("cfg3", 16), ("cfg4", 8)):
         case = _full_size(ts, kind, B, 7 + B)
+        if kind == "cfg5":
+            # rows whose largest values are one block of ties inside one shard: more of them than a shard sends, all
+            # kept, so the draw falls among unsent ties -- stage 3 finishes those rows
+            g = I.rng(55)
+            Vs = I.THINKER_V // 8
+            for r in range(0, B, 3):
+                s = int(g.integers(0, 8))
+                n_tie = int(g.integers(80, 400))
+                case.logits[r, s * Vs + g.choice(Vs, n_tie, replace=False)] = 12.0
         x = gpu_logits(case)
         hist = torch.from_numpy(case.history).to(DEV)
         steps = torch.from_numpy(case.steps).to(DEV)
