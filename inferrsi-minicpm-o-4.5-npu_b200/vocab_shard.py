@@ -18,12 +18,31 @@ The tokens equal the unsharded kernel's on the concatenated row, however many el
 
 from __future__ import annotations
 
+from datetime import timedelta
 from typing import Optional, Sequence
 
 import torch
 
 from . import _native
 from . import talker_sampler as ts
+
+
+class ShardExchangeError(RuntimeError):
+    """A collective of the sharded step failed or did not finish within the caller's timeout (a rank left, or
+    stopped answering).  The step's tokens are not valid; the caller fails the rows of the step, as the reference
+    fails the requests of a tick that raised (``engine/runtime/backend.py:197-203``), and rebuilds the group."""
+
+
+def _wait(work, what: str, timeout: Optional[float]) -> None:
+    try:
+        if timeout is None:
+            work.wait()
+        elif not work.wait(timedelta(seconds=float(timeout))):
+            raise ShardExchangeError(f"{what} did not finish within {timeout} s")
+    except ShardExchangeError:
+        raise
+    except Exception as e:  # the backend's own error (a peer that left, a timeout of its own)
+        raise ShardExchangeError(f"{what} failed: {type(e).__name__}: {e}") from e
 
 
 def _k(cfg) -> int:
@@ -112,36 +131,55 @@ def unpack(buf: torch.Tensor, shards: int, rows: int, cap: int):
             b[:, :, 2 * cap].contiguous())
 
 
-def exchange(values: torch.Tensor, ids: torch.Tensor, counts: torch.Tensor, *, group=None):
+def exchange(values: torch.Tensor, ids: torch.Tensor, counts: torch.Tensor, *, group=None,
+             timeout: Optional[float] = None):
     """Every shard's candidate lists on every rank: one ``all_gather_into_tensor`` of the packed buffer.
     Returns (values [S, B, cap], ids [S, B, cap], counts [S, B]) in rank order.  Works on any backend that
-    gathers into one tensor (NCCL on the GPUs; gloo on the CPU for the host-side tests)."""
+    gathers into one tensor (NCCL on the GPUs; gloo on the CPU for the host-side tests).  ``timeout`` (seconds):
+    raise ShardExchangeError when the gather has not finished by then (None: the process group's own timeout)."""
     import torch.distributed as dist
 
     mine = pack(values, ids, counts)
     world = dist.get_world_size(group)
     allb = torch.empty((world * mine.shape[0], mine.shape[1]), dtype=torch.int32, device=mine.device)
-    dist.all_gather_into_tensor(allb, mine, group=group)
+    try:
+        work = dist.all_gather_into_tensor(allb, mine, group=group, async_op=True)
+    except Exception as e:
+        raise ShardExchangeError(f"candidate all-gather failed: {type(e).__name__}: {e}") from e
+    _wait(work, "candidate all-gather", timeout)
     return unpack(allb, world, mine.shape[0], values.shape[1])
+
+
+def publish(tokens: torch.Tensor, *, group=None, timeout: Optional[float] = None) -> torch.Tensor:
+    """The max over the shards' stage-3 tokens, in place (a max-all-reduce of [B] int64)."""
+    import torch.distributed as dist
+
+    try:
+        work = dist.all_reduce(tokens, op=dist.ReduceOp.MAX, group=group, async_op=True)
+    except Exception as e:
+        raise ShardExchangeError(f"token all-reduce failed: {type(e).__name__}: {e}") from e
+    _wait(work, "token all-reduce", timeout)
+    return tokens
 
 
 def sample_sharded(logits: torch.Tensor, offset: int, vocab: int, history: Optional[torch.Tensor],
                    steps: torch.Tensor, seeds: Optional[torch.Tensor], cfg, *, group=None, cap: Optional[int] = None,
                    uniform_values: Optional[torch.Tensor] = None, requests: Optional[torch.Tensor] = None,
-                   rng: str = "philox", status: Optional[torch.Tensor] = None) -> torch.Tensor:
+                   rng: str = "philox", status: Optional[torch.Tensor] = None,
+                   timeout: Optional[float] = None) -> torch.Tensor:
     """One sampled token per row of the full vocabulary, from this rank's shard; every rank returns the same
     tokens.  ``group``: the torch.distributed process group of the shards (rank order = shard order).  Two
-    collectives: the all-gather of the candidate lists and a max-all-reduce of [B] int64 tokens."""
+    collectives: the all-gather of the candidate lists and a max-all-reduce of [B] int64 tokens.  ``timeout``
+    (seconds) bounds each of them: a rank that left or hangs turns into ShardExchangeError, not a hang."""
     import torch.distributed as dist
 
     cap = cap or default_cap(cfg)
     v, i, n = shard_candidates(logits, offset, history, steps, cfg, cap=cap, status=status)
-    vv, ii, nn = exchange(v, i, n, group=group)
+    vv, ii, nn = exchange(v, i, n, group=group, timeout=timeout)
     tok, pend = merge(vv, ii, nn, vocab, steps, seeds, cfg, uniform_values=uniform_values, requests=requests, rng=rng,
                       status=status)
     out = resolve(logits, offset, dist.get_rank(group), history, steps, cfg, tok, pend, status=status)
-    dist.all_reduce(out, op=dist.ReduceOp.MAX, group=group)
-    return out
+    return publish(out, group=group, timeout=timeout)
 
 
 def shard_bounds(vocab: int, shards: int) -> Sequence[int]:
