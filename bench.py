@@ -44,6 +44,10 @@ WORKLOADS = {
     "talker": dict(rows=8, vocab=6562, dtype="bf16", window=64, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05,
                    order="hf", min_keep=3, eos=6561, min_new=8, row_temperature=(0.6, 0.8, 1.0),
                    row_top_k=(20, 25, 50), row_top_p=(0.7, 0.85, 0.95)),
+    # BASELINE config 2 decoded K = 16 frames per launch (the K-frame device block of decode_k): a step is 16 frames
+    "talker_k": dict(rows=8, vocab=6562, dtype="bf16", window=64, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05,
+                     order="hf", min_keep=3, eos=6561, min_new=8, row_temperature=(0.6, 0.8, 1.0),
+                     row_top_k=(20, 25, 50), row_top_p=(0.7, 0.85, 0.95), frames=16),
     # the single-stream Talker (one row, fp32, hf order, 16-token history)
     "talker1": dict(rows=1, vocab=6562, dtype="f32", window=16, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05,
                     order="hf", min_keep=3, eos=6561, min_new=0),
@@ -308,7 +312,7 @@ def config_of(args, w, world: int) -> dict:
             "l2": f"{nbuf} rotating logits buffers ({nbuf * B * V * (2 if w['dtype'] == 'bf16' else 4) / 2**20:.0f}"
                   " MiB > L2)",
             "cuda_graph_steps": 0 if args.eager else min(args.steps, 1000), "kernel_path": args.path,
-            "cluster": args.cluster}
+            "cluster": args.cluster, "frames_per_step": w.get("frames", 1)}
 
 
 def run_vocab_shard(args, w, rank: int, world: int, local: int):
@@ -522,9 +526,22 @@ def main():
     kw = None if greedy else ts._cfg_kwargs(cfg, state.history, dev, rp)
     ops = pkg._native.ops()
 
+    K = w.get("frames", 1)
+    if K > 1:  # [n, B, V] frames: step i decodes frames (i * K) mod n ... + K - 1 in one launch
+        frames_all = torch.stack(bufs)
+        del bufs[:]
+        nfr = frames_all.shape[0] - K
+
     def one_step(i):
         if greedy:
             return ops.argmax(bufs[i % nbuf])
+        if K > 1:
+            f0 = (i * K) % nfr
+            return ops.sample_frames_(frames_all[f0:f0 + K], state.history, state.steps, state.finished, state.seeds,
+                                      None, state.active, kw["alpha"], None, None if rp is None else rp.temperature,
+                                      None if rp is None else rp.top_p, None if rp is None else rp.top_k,
+                                      kw["temperature"], cfg.top_p, cfg.top_k, kw["min_keep"], cfg.min_new_tokens,
+                                      cfg.max_new_tokens, eos, kw["semantics"], ts.RNG_PHILOX, kw["max_top_k"])
         return ops.sample_state_(bufs[i % nbuf], state.history, state.steps, state.finished, state.seeds, None,
                                  state.active, kw["alpha"], None, None if rp is None else rp.temperature,
                                  None if rp is None else rp.top_p, None if rp is None else rp.top_k,
@@ -582,21 +599,27 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     ms_per_step = ms / args.steps
-    value = B * world * args.steps / (ms / 1e3)
+    value = B * K * world * args.steps / (ms / 1e3)  # sampled rows (row-frames) per second
     peak, peak_kind = measured_peak_gbs()
-    achieved = step_bytes / (ms_per_step / 1e3) / 1e9
+    achieved = K * step_bytes / (ms_per_step / 1e3) / 1e9
 
     # end to end through the public API: pinned host logits -> device, sample, tokens -> host, every step
     e2e_steps = max(1, args.e2e_steps)
-    host = torch.from_numpy(logits_h).to(tdt).pin_memory()
+    host = torch.from_numpy(logits_h).to(tdt)
+    host = (host[None].expand(K, B, V) if K > 1 else host).contiguous().pin_memory()
     dbuf = torch.empty_like(host, device=dev)
-    tok_h = torch.empty(B, dtype=torch.int64).pin_memory()
+    tok_h = torch.empty((K, B) if K > 1 else (B,), dtype=torch.int64).pin_memory()
     hist_e = state.history.clone()
     steps_e = torch.ones(B, dtype=torch.int64, device=dev)
     seeds_e = state.seeds.clone()
+    st_e = ts.DecodeState(seeds=seeds_e, steps=steps_e, history=hist_e, finished=state.finished.clone(),
+                          active=state.active.clone())
+
     def api_step():
         if greedy:
             return pkg.thinker_sampler.argmax(dbuf)
+        if K > 1:  # the public K-frame entry (its counter RNG; per-row parameters are the sample-level form)
+            return ts.decode_k(st_e, dbuf, eos, cfg)
         return ts.sample(dbuf, hist_e, steps_e, seeds_e, eos, cfg, rng="philox", row_params=rp)
 
     for i in range(3 if args.e2e_steps else 0):
@@ -617,7 +640,7 @@ def main():
     et = torch.tensor([e0.elapsed_time(e1)], device=dev)
     if world > 1:
         dist.all_reduce(et, op=dist.ReduceOp.MAX)
-    e2e_value = B * world * e2e_steps / (float(et.item()) / 1e3)
+    e2e_value = B * K * world * e2e_steps / (float(et.item()) / 1e3)
 
     cb = cb_port = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -643,7 +666,7 @@ def main():
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "bytes_per_row": row_bytes, "peak_source": peak_kind},
         "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": host.numel() * host.element_size(),
-                "d2h_bytes_per_step": B * 8, "steps": e2e_steps},
+                "d2h_bytes_per_step": B * K * 8, "steps": e2e_steps},
         "gpu_launches": args.steps,
         "clocks": ck,
         "cpu_baseline": cb,

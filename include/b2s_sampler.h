@@ -127,6 +127,19 @@ typedef struct b2s_sample_args {
 int b2s_sample(const b2s_sample_args* args, void* stream);
 
 /*
+ * K frames of the step() state machine in one launch (the K-frame device block of the Talker decode loop):
+ * frame f samples from the rows of logits + f * frame_stride elements, writes tokens[f * rows + row] (PAD for
+ * rows that are not live), and advances the state in place -- history_out == history, steps_out == steps and
+ * finished_out == finished (non-NULL) are required -- so that frame f + 1 sees it; a row that draws EOS is
+ * frozen for the frames after it.  uniform_values (B2S_RNG_UNIFORM) are [frames, rows].  The tokens and the
+ * final state equal `frames` calls of b2s_sample.  No processed output; cluster must be 0 (one CTA per row
+ * takes the row's frames in order, prefetching the next frame's logits under the current frame's draw).
+ * Replaces: engine/talker_sampler.py:252-254 decode_k and the K-frame graph bodies of
+ * engine/runtime/talker_decode.py:120-128, engine/runtime/talker_block_graph.py:70-89.
+ */
+int b2s_sample_frames(const b2s_sample_args* args, int32_t frames, int64_t frame_stride, void* stream);
+
+/*
  * Greedy next token: argmax over each row (first index among equal maxima, NaN wins).
  * Replaces the Thinker sampling step F.linear(h, lm_head).float().argmax(-1) at
  * engine/runtime/thinker_decode.py:83,107, engine/runtime/backend_s.py:893,

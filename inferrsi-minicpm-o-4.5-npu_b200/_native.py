@@ -45,6 +45,7 @@ class SampleArgs(ctypes.Structure):
 # every entry point of include/b2s_sampler.h with its ctypes signature
 CAPI_SIGNATURES = {
     "b2s_sample": (ctypes.c_int, [ctypes.POINTER(SampleArgs), ctypes.c_void_p]),
+    "b2s_sample_frames": (ctypes.c_int, [ctypes.POINTER(SampleArgs), ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p]),
     "b2s_argmax": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
                                   ctypes.c_void_p, ctypes.c_void_p]),
     "b2s_uniform": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,

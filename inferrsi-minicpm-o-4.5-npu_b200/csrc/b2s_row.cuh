@@ -78,6 +78,10 @@ struct Params {
     // the row slice live, and the slice capacity in 16-byte vectors
     int cl, ltot, slice_vecs;
     uint32_t off_bar, off_slice;
+    // several frames in one launch (b2s_sample_frames): logits of frame f start f * fstride elements after frame 0's;
+    // tokens and uniform values are [frames, rows]; the state advances in place from frame to frame
+    int frames;
+    int64_t fstride;
 };
 
 struct Ctl {

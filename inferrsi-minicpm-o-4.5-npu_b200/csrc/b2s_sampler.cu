@@ -69,9 +69,14 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     const Scr sc{hist, ctl->rctl, &ctl->gather_n, &ctl->kn, &ctl->thr, ctl->red_d, ctl->red_f, ctl->red_i};
     pdl_wait_then_release();  // nothing global is read before the previous kernel of the stream is done
 
-    // 16-byte-aligned interior of row r: head elements before it, vectors in it
-    auto geometry = [&](int r, int& nh, int& nvec, const uint4*& gvec) {
-        const unsigned char* rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
+    // logits row of work item w: frame w / rows (p.fstride elements apart), row w % rows
+    auto row_of = [&](int w) {
+        return reinterpret_cast<const unsigned char*>(p.logits) +
+               ((int64_t)(w / p.rows) * p.fstride + (int64_t)(w % p.rows) * p.lstride) * ES;
+    };
+    // 16-byte-aligned interior of work item w's row: head elements before it, vectors in it
+    auto geometry = [&](int w, int& nh, int& nvec, const uint4*& gvec) {
+        const unsigned char* rowp = row_of(w);
         const uintptr_t a = reinterpret_cast<uintptr_t>(rowp);
         const uintptr_t b = a + (uintptr_t)V * ES;
         const uintptr_t ace = (a + 15) & ~(uintptr_t)15, bfl = b & ~(uintptr_t)15;
@@ -107,13 +112,17 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
     // cluster barrier ends each row, so the helper never overwrites structures still in use.
     const bool split = p.csplit != 0;
     const bool helper = split && cg::this_cluster().block_rank() == 1;
+    // Work items w = frame * rows + row.  With several frames (b2s_sample_frames) the grid has one CTA per row, so a
+    // CTA takes its row's frames in order and the state each frame writes in place is the next frame's input.
     const int rstep = split ? (int)gridDim.x / 2 : (int)gridDim.x;
-    for (int r = split ? (int)blockIdx.x / 2 : (int)blockIdx.x; r < p.rows; r += rstep) {
+    const int nwork = p.rows * p.frames;
+    for (int w = split ? (int)blockIdx.x / 2 : (int)blockIdx.x; w < nwork; w += rstep) {
+        const int r = w % p.rows;
         // ---------------- geometry; the first chunk's loads go out before anything else
         Row<E> R;
-        R.rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
+        R.rowp = row_of(w);
         R.V = V;
-        geometry(r, R.nh, R.nvec, R.gvec);
+        geometry(w, R.nh, R.nvec, R.gvec);
         R.e0 = R.nh;
         const int nchunks = (R.nvec + VPC - 1) / VPC;
         auto load_chunk = [&](int c, uint4* q) { load_chunk_of(R.gvec, R.nvec, c, q); };
@@ -161,7 +170,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
         if (cout_n && mode != MODE_FILTER) mode = MODE_FAIL;
         const bool topk_only = (p.flags & B2S_FLAG_TOPK_ONLY) != 0;
         if (tid == 32) {  // one thread: the row's uniform (read after the next barrier)
-            ctl->u = (p.rng == B2S_RNG_UNIFORM || !p.seeds) ? (p.uvals ? p.uvals[r] : 0.0f)
+            ctl->u = (p.rng == B2S_RNG_UNIFORM || !p.seeds) ? (p.uvals ? p.uvals[w] : 0.0f)
                      : p.rng == B2S_RNG_PHILOX ? uniform_philox(p.seeds[r], step, p.requests ? p.requests[r] : 0)
                                                : uniform_counter(p.seeds[r], step);
         }
@@ -454,10 +463,10 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             }
         }
         // this row's stream is done: start the first chunk of the CTA's next row
-        if (r + rstep < p.rows) {
+        if (w + rstep < nwork) {
             int nh2, nvec2;
             const uint4* g2;
-            geometry(r + rstep, nh2, nvec2, g2);
+            geometry(w + rstep, nh2, nvec2, g2);
             if (nvec2 > 0) load_chunk_of(g2, nvec2, 0, nq);
             next_row_in = true;
         }
@@ -581,7 +590,7 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(const Params p) {
             const bool adv = is_live && tok_drawn != PAD;
             const int64_t tok = adv ? tok_drawn : PAD;
             if (tid == 0) {
-                if (p.tokens) p.tokens[r] = tok;
+                if (p.tokens) p.tokens[w] = tok;
                 if (p.steps_out) p.steps_out[r] = step + (adv ? 1 : 0);
                 if (p.fin_out) {
                     const bool f0 = p.finished ? p.finished[r] != 0 : false;
@@ -1066,7 +1075,8 @@ static bool resident_layout(b2s::Params& p, const b2s_sample_args* a, int CL, in
     return off <= 227 * 1024;
 }
 
-static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut* so) {
+static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut* so, int frames = 1,
+                         int64_t fstride = 0) {
     using namespace b2s;
     if (!a || !a->logits || a->rows < 0 || a->vocab <= 0) return B2S_ERR_INVALID;
     if (a->rows == 0) return B2S_OK;
@@ -1095,6 +1105,8 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
 
     Params p;
     memset(&p, 0, sizeof(p));
+    p.frames = frames;
+    p.fstride = fstride;
     p.logits = a->logits;
     p.lstride = a->logits_row_stride;
     p.rows = a->rows;
@@ -1210,7 +1222,7 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     // clusters, and one CTA per row for hf (its full-row normaliser is taken from the resident row).
     // `cluster` > 0 asks for it with that many CTAs per row; 0 lets the launcher pick the smallest that fits.
     {
-        const bool streamed = (a->flags & B2S_FLAG_STREAM) != 0;
+        const bool streamed = (a->flags & B2S_FLAG_STREAM) != 0 || frames > 1;
         if (a->cluster != 0 && (streamed || !(a->cluster == 1 || a->cluster == 2 || a->cluster == 4 || a->cluster == 8)))
             return B2S_ERR_INVALID;
         const bool res_ok = lean && draws && !identity && !streamed && kmax <= KLIST;
@@ -1298,9 +1310,10 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
     {
         const int64_t row_chunks = ((int64_t)a->vocab * es / 16 + VPC - 1) / VPC;
         p.csplit = (!so && !a->processed && !identity && p.W > 0 && row_chunks >= 4 && row_chunks <= p.tmc_chunks &&
-                    (int64_t)a->rows * 2 <= sm_count()) ? 1 : 0;
+                    (int64_t)a->rows * 2 <= sm_count() && frames == 1) ? 1 : 0;
     }
-    const int64_t grid_rows = a->rows < 65535 * 8 ? a->rows : 65535 * 8;
+    // several frames: one CTA per row, which takes the row's frames in order (b2s_sample_frames checks the size)
+    const int64_t grid_rows = frames > 1 ? a->rows : (a->rows < 65535 * 8 ? a->rows : 65535 * 8);
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3((unsigned)(p.csplit ? 2 * grid_rows : grid_rows), 1, 1);
@@ -1323,6 +1336,19 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
 }
 
 int b2s_sample(const b2s_sample_args* a, void* stream) { return launch_sample(a, stream, nullptr); }
+
+int b2s_sample_frames(const b2s_sample_args* a, int32_t frames, int64_t frame_stride, void* stream) {
+    if (!a || frames < 1 || !a->tokens) return B2S_ERR_INVALID;
+    if (frames == 1) return launch_sample(a, stream, nullptr);
+    if (a->semantics == B2S_SEM_IDENTITY || a->processed || a->cluster != 0) return B2S_ERR_INVALID;
+    // the state carries from frame to frame in place
+    if (!a->steps_out || a->steps_out != a->steps || !a->finished || a->finished_out != a->finished) return B2S_ERR_INVALID;
+    if (a->window > 0 && a->history_out != a->history) return B2S_ERR_INVALID;
+    if (a->window > 0 && a->history_out_row_stride != a->history_row_stride) return B2S_ERR_INVALID;
+    if (frame_stride < (int64_t)a->rows * a->logits_row_stride) return B2S_ERR_INVALID;
+    if (a->rows > 65535 * 8 || (int64_t)a->rows * frames > INT32_MAX) return B2S_ERR_UNSUPPORTED;
+    return launch_sample(a, stream, nullptr, frames, frame_stride);
+}
 
 int b2s_shard_candidates(const b2s_sample_args* a, int64_t vocab_offset, int32_t cap, float* cand_values,
                          int32_t* cand_ids, int32_t* cand_count, void* stream) {

@@ -195,6 +195,51 @@ Tensor sample_state_cuda(const Tensor& logits, Tensor& history, Tensor& steps, T
     return tokens;
 }
 
+// K frames in one launch: logits_k [K, B, V]; history / steps / finished advance in place over the frames.
+Tensor sample_frames_cuda(const Tensor& logits_k, Tensor& history, Tensor& steps, Tensor& finished,
+                          const optional<Tensor>& seeds, const optional<Tensor>& uniform_values,
+                          const optional<Tensor>& active, const optional<Tensor>& alpha, const optional<Tensor>& status,
+                          const optional<Tensor>& row_temperature, const optional<Tensor>& row_top_p,
+                          const optional<Tensor>& row_top_k, double temperature, double top_p, int64_t top_k,
+                          int64_t min_keep, int64_t min_new, int64_t max_new, int64_t eos, int64_t semantics,
+                          int64_t rng, int64_t max_top_k) {
+    c10::cuda::CUDAGuard guard(logits_k.device());
+    TORCH_CHECK(logits_k.dim() == 3 && logits_k.stride(2) == 1, "logits_k must be [K, B, V] with contiguous rows");
+    TORCH_CHECK(steps.is_contiguous() && finished.is_contiguous() && history.is_contiguous(),
+                "state tensors must be contiguous");
+    TORCH_CHECK(finished.scalar_type() == at::kBool, "finished must be bool");
+    const int64_t K = logits_k.size(0), B = logits_k.size(1);
+    optional<Tensor> u0 = c10::nullopt;
+    if (uniform_values.has_value() && uniform_values->defined()) {
+        TORCH_CHECK(uniform_values->numel() == K * B && uniform_values->is_contiguous() &&
+                        uniform_values->scalar_type() == at::kFloat && uniform_values->is_cuda(),
+                    "uniform_values must be contiguous float32 CUDA [K, B]");
+        u0 = uniform_values->reshape({K * B}).narrow(0, 0, B);
+    }
+    b2s_sample_args a;
+    fill_args(a, logits_k.select(0, 0), history, steps, seeds, c10::nullopt, u0, active, finished, row_temperature,
+              row_top_p, row_top_k, alpha, status, temperature, top_p, top_k, min_keep, min_new, max_new, 0.0, 0.0, eos,
+              semantics, rng, max_top_k, 0, 0);
+    if (u0.has_value()) a.uniform_values = uniform_values->data_ptr<float>();
+    Tensor tokens = at::empty({K, B}, logits_k.options().dtype(at::kLong));
+    a.tokens = tokens.data_ptr<int64_t>();
+    a.history_out = history.numel() ? history.data_ptr<int64_t>() : nullptr;
+    a.history_out_row_stride = history.dim() == 2 ? history.size(1) : 0;
+    a.steps_out = steps.data_ptr<int64_t>();
+    a.finished_out = reinterpret_cast<uint8_t*>(finished.data_ptr<bool>());
+    check_rc(b2s_sample_frames(&a, (int32_t)K, logits_k.stride(0), at::cuda::getCurrentCUDAStream().stream()),
+             "b2s_sample_frames");
+    return tokens;
+}
+
+Tensor sample_frames_meta(const Tensor& logits_k, Tensor&, Tensor&, Tensor&, const optional<Tensor>&,
+                          const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
+                          const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
+                          const optional<Tensor>&, double, double, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                          int64_t, int64_t) {
+    return at::empty({logits_k.size(0), logits_k.size(1)}, logits_k.options().dtype(at::kLong));
+}
+
 Tensor sample_state_meta(const Tensor& logits, Tensor&, Tensor&, Tensor&, const optional<Tensor>&,
                          const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
                          const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
@@ -394,6 +439,11 @@ TORCH_LIBRARY(minicpmo_sampler, m) {
         "Tensor? row_top_p, Tensor? row_top_k, float temperature, float top_p, int top_k, int min_keep, "
         "int min_new_tokens, int max_new_tokens, int eos, int semantics, int rng, int max_top_k, int cluster, "
         "int flags=0) -> Tensor tokens");
+    m.def(
+        "sample_frames_(Tensor logits_k, Tensor(a!) history, Tensor(b!) steps, Tensor(c!) finished, Tensor? seeds, "
+        "Tensor? uniform_values, Tensor? active, Tensor? alpha, Tensor? status, Tensor? row_temperature, "
+        "Tensor? row_top_p, Tensor? row_top_k, float temperature, float top_p, int top_k, int min_keep, "
+        "int min_new_tokens, int max_new_tokens, int eos, int semantics, int rng, int max_top_k) -> Tensor tokens");
     m.def("argmax(Tensor logits) -> Tensor");
     m.def("uniform(Tensor seeds, Tensor steps, Tensor? requests, int rng) -> Tensor");
     m.def("repetition_penalty(Tensor x, Tensor history, Tensor alpha) -> Tensor");
@@ -415,6 +465,7 @@ TORCH_LIBRARY(minicpmo_sampler, m) {
 TORCH_LIBRARY_IMPL(minicpmo_sampler, CUDA, m) {
     m.impl("sample", &sample_cuda);
     m.impl("sample_state_", &sample_state_cuda);
+    m.impl("sample_frames_", &sample_frames_cuda);
     m.impl("argmax", &argmax_cuda);
     m.impl("uniform", &uniform_cuda);
     m.impl("repetition_penalty", &penalty_cuda);
@@ -426,6 +477,7 @@ TORCH_LIBRARY_IMPL(minicpmo_sampler, CUDA, m) {
 TORCH_LIBRARY_IMPL(minicpmo_sampler, Meta, m) {
     m.impl("sample", &sample_meta);
     m.impl("sample_state_", &sample_state_meta);
+    m.impl("sample_frames_", &sample_frames_meta);
     m.impl("argmax", &argmax_meta);
     m.impl("uniform", &uniform_meta);
     m.impl("repetition_penalty", &penalty_meta);

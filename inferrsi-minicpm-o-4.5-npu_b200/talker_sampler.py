@@ -333,8 +333,40 @@ def step(state: DecodeState, logits: torch.Tensor, eos: int, cfg: TalkerSampling
 
 def decode_k(state: DecodeState, logits_k: torch.Tensor, eos: int, cfg: TalkerSampling = TalkerSampling()) -> torch.Tensor:
     """K frames from precomputed per-frame logits [K, B, V]: identical to K calls of ``step``
-    (``talker_sampler.py:252-254``); an EOS freezes its row."""
-    return torch.stack([step(state, logits_k[i], eos, cfg) for i in range(logits_k.size(0))])
+    (``talker_sampler.py:252-254``); an EOS freezes its row.  One launch runs all K frames (each row's frames in
+    order on one CTA, the next frame's logits in flight under the current draw); the new history / steps /
+    finished are fresh tensors bound to ``state``, as K ``step`` calls would leave them.  The native-generator
+    mode keeps the reference's per-frame torch calls."""
+    if cfg.uses_native_rng:
+        return torch.stack([step(state, logits_k[i], eos, cfg) for i in range(logits_k.size(0))])
+    hist, steps, fin = state.history.clone(), state.steps.clone(), state.finished.clone()
+    tok = _frames(logits_k, hist, steps, fin, state.seeds, state.active, eos, cfg, None, None)
+    if state.history.shape[-1] > 0:
+        state.history = hist
+    state.steps, state.finished = steps, fin
+    return tok
+
+
+def decode_k_(state: DecodeState, logits_k: torch.Tensor, eos: int, cfg: TalkerSampling = TalkerSampling(), *,
+              uniform_values: Optional[torch.Tensor] = None, status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``decode_k`` advancing ``state.history`` / ``steps`` / ``finished`` IN PLACE (the K-frame graph body of
+    ``engine/runtime/talker_decode.py:120-128``, ``talker_block_graph.py:70-89``); returns the [K, B] tokens.
+    ``uniform_values``: [K, B] injected uniforms instead of the counter RNG."""
+    if cfg.uses_native_rng:
+        raise ValueError("decode_k_ needs the counter RNG or injected uniforms")
+    return _frames(logits_k, state.history, state.steps, state.finished, state.seeds, state.active, eos, cfg,
+                   uniform_values, status)
+
+
+def _frames(logits_k, hist, steps, fin, seeds, active, eos, cfg, uniform_values, status) -> torch.Tensor:
+    _need_cuda(logits_k, hist, steps, fin, seeds, active, uniform_values)
+    kw = _cfg_kwargs(cfg, hist, logits_k.device)
+    r = RNG_UNIFORM if uniform_values is not None else RNG_COUNTER
+    u = None if uniform_values is None else uniform_values.to(torch.float32).contiguous()
+    return _native.ops().sample_frames_(
+        logits_k, hist, steps, fin, seeds, u, active, kw["alpha"], status, None, None, None, kw["temperature"],
+        float(cfg.top_p), int(cfg.top_k), int(kw["min_keep"]), int(cfg.min_new_tokens), int(cfg.max_new_tokens),
+        int(eos), int(kw["semantics"]), r, int(kw["max_top_k"]))
 
 
 # ---------------------------------------------------------------- fused / in-place entry points

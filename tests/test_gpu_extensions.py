@@ -205,3 +205,34 @@ def test_graph_replay_matches_eager(pkg, sem):
         assert torch.equal(graphed.finished, eager.finished)
     assert bool(eager.finished[1]) and int(eager.steps[3]) == 0
     del gr
+
+
+@pytest.mark.parametrize("sem", ["hf", "omni"])
+def test_k_frame_block_matches_step_loop(pkg, sem):
+    """decode_k (one launch for K frames) and decode_k_ (in place) == K calls of step on a copy of the state: the
+    same [K, B] tokens and final history / steps / finished, through frame 0 (hf: unfiltered), EOS masking and
+    forcing, a row that draws EOS early and freezes, and an inactive row."""
+    ts = pkg.talker_sampler
+    cfg = ts.TalkerSampling(semantics=sem, rng="counter", min_new_tokens=3, max_new_tokens=20, window=16)
+    B, V, K = 7, I.TALKER_V, 24
+    g = torch.Generator(device=DEV).manual_seed(31)
+    frames = torch.randn(K, B, V, device=DEV, generator=g) * 2.0
+    frames[6:, 2, I.TALKER_EOS] = 40.0  # row 2 draws EOS once it is allowed
+    for dt in (torch.float32, torch.bfloat16):
+        x = frames.to(dt)
+        a = ts.DecodeState.new([3, 4, 5, 6, 7, 8, 9], cfg, device=DEV)
+        a.active[5] = False
+        b = ts.DecodeState.new([3, 4, 5, 6, 7, 8, 9], cfg, device=DEV)
+        b.active[5] = False
+        c = ts.DecodeState.new([3, 4, 5, 6, 7, 8, 9], cfg, device=DEV)
+        c.active[5] = False
+        hist_c = c.history
+        want = torch.stack([ts.step(a, x[f], I.TALKER_EOS, cfg) for f in range(K)])
+        got = ts.decode_k(b, x, I.TALKER_EOS, cfg)
+        got_ = ts.decode_k_(c, x, I.TALKER_EOS, cfg)
+        for t, st in ((got, b), (got_, c)):
+            assert torch.equal(t, want), (dt, t, want)
+            assert torch.equal(st.history, a.history) and torch.equal(st.steps, a.steps)
+            assert torch.equal(st.finished, a.finished)
+        assert c.history is hist_c  # advanced in place
+        assert bool(a.finished[2]) and int(a.steps[5]) == 0 and (want[:, 5] == ts.PAD).all()
