@@ -1,24 +1,29 @@
-// B200 (sm_100a) token-sampling kernels for MiniCPM-o 4.5 and their C-ABI launchers.
+// B200 (sm_100a) streaming sampling kernel, the greedy argmax, the standalone penalty and uniform kernels, and the
+// C-ABI launchers of include/b2s_sampler.h (the row-resident kernel is in b2s_resident.cu, the vocabulary-shard
+// merge and resolve in b2s_shard.cu).
 //
-// One 512-thread CTA owns one logits row (a loop over rows when the batch is larger than the grid).  The
-// row's 16-byte-aligned interior streams through registers: each iteration a thread holds 4 x 16 bytes of
-// the row while the next 4 x 16 bytes are in flight (plain 16-byte loads, not kept in L1); the ragged head
-// and tail elements are single loads.  Everything else the row needs -- parameters, the RNG input, the
-// history ids (hashed in shared memory), the penalty table and the raw values of the history ids -- is
-// fetched alongside.  Later passes over the row (the exact path, hf's logsumexp, processed output) read it
-// again from L2.
+// Streaming kernel: one 512-thread CTA owns one logits row at a time (a loop over rows when the batch is larger than
+// the grid; over a row's frames for b2s_sample_frames).  The row's 16-byte-aligned interior streams through
+// registers in 32 KB chunks (4 x 16 bytes per thread, two register buffers in turn, plain loads kept out of L1); the
+// ragged head and tail are single loads.  Per row:
 //
-//   prologue: history ids -> bitmap + hash (id -> count); penalty table
-//   stream:   per-thread maxima; tau0 from the first chunk; every non-history element >= tau goes to the
-//             candidate list (one atomic per warp); warp 0 raises tau from a histogram of the candidates
-//   list stage (top_k <= 128): top-k values, top-p cut (one warp), value threshold, draw in vocabulary order
-//   exact path (top_k > 128 or an overflowing list): radix select of the k-th processed key over the row,
-//       sorted top-k values, top-p, and an ordered scan of the kept mass; frame-0 hf rows and draw() go
-//       straight to the ordered scan over the whole row
+//   prologue: the history ids and penalty table by cp.async; a bitmap of the history ids, the rank of each distinct
+//             id from a prefix of the bitmap's group popcounts, its count, and per-thread masks of the chunk shares
+//             that hold one;
+//   pass 1:   each (chunk, thread) share's maximum, kept in shared memory;
+//   tau:      the k-th largest of the warps' ceil(k/16) largest per-thread maxima over shares without a history id
+//             (a lower bound of the row's k-th largest non-history value);
+//   pass 2:   the shares whose maximum clears tau are re-read from L2 (listed per warp, dealt over its lanes); every
+//             non-history element >= tau goes to the candidate list, history ids by their processed values;
+//   list:     top-k values, top-p cut, value threshold and the inverse-CDF draw in vocabulary order (b2s_list.cuh);
+//   exact:    rows the list cannot serve (k > 128, overflowing lists, NaN or unusable tau) take a radix select of the
+//             k-th processed key over the row and an ordered scan; hf frame-0 rows and draw() take the ordered scan;
+//   state:    token, steps, finished and the shifted history (in place when the outputs alias the inputs).
 //
-// Selection runs on raw values: for ids outside the history the processed value is fl(x / T), monotone in
-// x, so the order and the k-th element carry over; history ids are processed exactly.  No block in this
-// file waits on another block.
+// For batches of at most half the SMs with a penalty history, the rows of the thinker shape run as CTA pairs: the
+// second CTA builds the history structures beside pass 1 and hands them over through distributed shared memory.
+// Selection runs on raw values: outside the history the processed value is fl(x / T), monotone in x.  No block in
+// this file waits on another block except at the hardware cluster barrier.
 #include "b2s_row.cuh"
 
 #include <cooperative_groups.h>
