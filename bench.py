@@ -303,6 +303,8 @@ def config_of(args, w, world: int) -> dict:
     """The workload as both arms report it."""
     B, V = w["rows"], w["vocab"]
     nbuf = rotating_buffers(w)
+    if getattr(args, "strong", False):
+        B //= world
     return {"workload": args.workload, "rows_per_gpu": B, "global_batch": B * world, "vocab": V,
             "logits_dtype": w["dtype"], "window": w["window"], "temperature": w["temperature"], "top_k": w["top_k"],
             "top_p": w["top_p"], "repetition_penalty": w["penalty"], "order": w.get("order", "omni"), "rng": "philox",
@@ -468,6 +470,8 @@ def main():
     ap.add_argument("--path", default="auto", choices=["auto", "stream", "resident"],
                     help="sampling kernel: the launcher's choice, the streaming kernel, or the row-resident kernel")
     ap.add_argument("--cluster", type=int, default=0, help="CTAs per row of the row-resident kernel (0: auto)")
+    ap.add_argument("--strong", action="store_true",
+                    help="split the workload's batch over the ranks (strong scaling) instead of B rows per rank")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     rank = int(os.environ.get("RANK", "0"))
@@ -492,6 +496,10 @@ def main():
     pkg = __graft_entry__.load_package()
     ts = pkg.talker_sampler
     B, V, W = w["rows"], w["vocab"], w["window"]
+    if args.strong:  # a fixed global batch split over the ranks (1024 rows over 1/2/4/8 GPUs)
+        if B % world:
+            raise SystemExit(f"--strong needs the batch ({B}) divisible by the rank count ({world})")
+        B //= world
     tdt = torch.bfloat16 if w["dtype"] == "bf16" else torch.float32
     row_bytes = bytes_per_row(w)
     step_bytes = B * row_bytes
@@ -660,7 +668,8 @@ def main():
     line = {
         "metric": metric_of(w),
         "value": value, "unit": "rows/s", "value_per_gpu": value / world, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
         "dtype": dtype_of(w), "data": "synthetic",
         "config": config_of(args, w, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
