@@ -157,14 +157,17 @@ def measured_peak_gbs():
     return 6650.0, "fallback"
 
 
-def profiled_traffic(workload: str, w) -> float | None:
-    """DRAM bytes per launch of the workload's kernel from the committed ncu summary, or None."""
-    kernel = "argmax_kernel" if w.get("op") == "argmax" else "sample_kernel"
-    f = ROOT / "profiles" / f"{kernel}_{workload}.md"
-    if not f.exists():
-        return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
-    return float(m.group(1)) if m else None
+def profiled_traffic(workload: str, w, path: str = "auto") -> float | None:
+    """DRAM bytes per launch of the workload's kernel from the committed ncu summary, or None (the row-resident
+    kernel's summary first where the launcher picks that kernel for the workload)."""
+    kernels = ["argmax_kernel"] if w.get("op") == "argmax" else (
+        ["sample_kernel"] if path == "stream" else ["resident_kernel", "sample_kernel"])
+    for kernel in kernels:
+        f = ROOT / "profiles" / f"{kernel}_{workload}.md"
+        if f.exists():
+            m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
+            return float(m.group(1)) if m else None
+    return None
 
 
 def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
@@ -664,7 +667,7 @@ def main():
         dist.destroy_process_group()
     if rank != 0:
         return
-    traffic = profiled_traffic(args.workload, w)
+    traffic = profiled_traffic(args.workload, w, args.path)
     line = {
         "metric": metric_of(w),
         "value": value, "unit": "rows/s", "value_per_gpu": value / world, "n_gpus": world, "steps": args.steps,
