@@ -470,68 +470,87 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
 
     // ---------------- pass 2: this CTA's candidates (processed values) into its list
     const int hshare = p.ltot / CL;  // a CTA's share of rank 0's merged list
+    // every lane of the warp calls it with its count: one shared atomic per warp, the lane's first position back
+    auto warp_reserve = [&](int cnt) {
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        int base = 0;
+        if (lane == 31 && incl > 0) base = atomicAdd(&ctl->kn, incl);
+        return __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
+    };
     if (cand_path && !ovf) {
-        // the thread's shares whose maximum clears tau; their non-history elements >= tau_low
+        // the thread's shares whose maximum clears tau, one per round of its warp; their non-history elements >=
+        // tau_low
         uint32_t hits = 0u;
 #pragma unroll
         for (int pc = 0; pc < RMAXP; ++pc) hits |= (uint32_t)(tm[pc] >= tau_low) << pc;
-        while (hits) {
-            const int pc = __ffs(hits) - 1;
-            hits &= hits - 1u;
-            const int n = min(RPV, nv - pc * RPV);
-            const int eb = R.e0 + (v0 + pc * RPV + tid) * EPV;  // element 0 of the share's first vector
+        while (__any_sync(0xffffffffu, hits != 0u)) {
             uint32_t em[RSH];
             uint4 q[RSH];
-            int cnt = 0;
+            int cnt = 0, eb = 0;
 #pragma unroll
             for (int h = 0; h < RSH; ++h) {
                 em[h] = 0u;
                 q[h] = make_uint4(0u, 0u, 0u, 0u);
-                const int vl = tid + h * NT;
-                if (vl < n) {
-                    q[h] = slice[(size_t)pc * RPV + vl];
-                    if (Elem<E>::vmax(q[h]) >= tau_low) {
-                        const uint32_t hbm = R.hbits(eb + h * NT * EPV, EPV);
-#pragma unroll
-                        for (int j = 0; j < EPV; ++j)
-                            if (Elem<E>::at(q[h], j) >= tau_low && !((hbm >> j) & 1u)) em[h] |= 1u << j;
-                    }
-                }
-                cnt += __popc(em[h]);
             }
-            if (cnt) {
-                int pos = atomicAdd(&ctl->kn, cnt);
-                if (pos + cnt > hshare) continue;  // counted: the list is flagged as overflowed below
+            if (hits) {
+                const int pc = __ffs(hits) - 1;
+                hits &= hits - 1u;
+                const int n = min(RPV, nv - pc * RPV);
+                eb = R.e0 + (v0 + pc * RPV + tid) * EPV;  // element 0 of the share's first vector
 #pragma unroll
                 for (int h = 0; h < RSH; ++h) {
-                    uint32_t m = em[h];
-                    while (m) {
-                        const int j = __ffs(m) - 1;
-                        m &= m - 1u;
+                    const int vl = tid + h * NT;
+                    if (vl < n) {
+                        q[h] = slice[(size_t)pc * RPV + vl];
+                        if (Elem<E>::vmax(q[h]) >= tau_low) {
+                            const uint32_t hbm = R.hbits(eb + h * NT * EPV, EPV);
+#pragma unroll
+                            for (int j = 0; j < EPV; ++j)
+                                if (Elem<E>::at(q[h], j) >= tau_low && !((hbm >> j) & 1u)) em[h] |= 1u << j;
+                        }
+                    }
+                    cnt += __popc(em[h]);
+                }
+            }
+            int pos = warp_reserve(cnt);
+#pragma unroll
+            for (int h = 0; h < RSH; ++h) {
+                uint32_t m = em[h];
+                while (m) {
+                    const int j = __ffs(m) - 1;
+                    m &= m - 1u;
+                    if (pos < hshare) {  // past it: counted, and the list is flagged as overflowed below
                         kv[pos] = R.f(Elem<E>::at(q[h], j));
                         ki[pos] = eb + h * NT * EPV + j;
-                        ++pos;
                     }
+                    ++pos;
                 }
             }
         }
-        if (edge_i >= 0 && edge_x >= tau_low && !R.hbit(edge_i)) {  // the ragged head / tail (rank 0)
-            const int pos = atomicAdd(&ctl->kn, 1);
-            if (pos < hshare) {
+        if (warp == NWARP - 1) {  // the ragged head / tail (rank 0)
+            const bool eh = edge_i >= 0 && edge_x >= tau_low && !R.hbit(edge_i);
+            const int pos = warp_reserve(eh ? 1 : 0);
+            if (eh && pos < hshare) {
                 kv[pos] = R.f(edge_x);
                 ki[pos] = edge_i;
             }
         }
         // the owned history ids whose processed value clears f(tau_low)
         const float p_low = R.f(tau_low);
-        for (int d = tid; d < hd; d += NT) {
-            const float hv = hb.htv[d];
-            if (hv >= p_low) {
-                const int pos = atomicAdd(&ctl->kn, 1);
-                if (pos < hshare) {
-                    kv[pos] = hv;
-                    ki[pos] = hb.hid[d];
-                }
+        for (int d0 = 0; d0 < hd; d0 += NT) {
+            const int d = d0 + tid;
+            const float hv = d < hd ? hb.htv[d] : f_ninf();
+            const bool ok = d < hd && hv >= p_low;
+            if (!__any_sync(0xffffffffu, ok)) continue;
+            const int pos = warp_reserve(ok ? 1 : 0);
+            if (ok && pos < hshare) {
+                kv[pos] = hv;
+                ki[pos] = hb.hid[d];
             }
         }
     }
@@ -566,46 +585,30 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
         }
     }
 
-    // ---------------- rank 0: the merged list, filtered by the tightest tau of the cluster (every CTA's tau bounds
-    // the row's k-th largest non-history value from below), into cand_v / cand_i
+    // ---------------- rank 0: every CTA's list, one after the other, into cand_v / cand_i
     const bool row_err = ctl->err != 0;
-    if (cand_path && !ovf && !row_err && warp == 0) {
-        float tl = tau_low;
-        for (int c = 1; c < CL; ++c) {
-            if (ctl->rx_n[c] < 0) ovf = true;
-            else tl = fmaxf(tl, ctl->rx_tau[c]);
-        }
-        const float pf = R.f(tl);
-        int m = 0;
-        for (int c = 0; c < CL && !ovf; ++c) {
+    if (cand_path && !ovf && !row_err) {
+        int off[8];
+        int tot = 0;
+        for (int c = 0; c < CL; ++c) {
             const int nc = c == 0 ? n : ctl->rx_n[c];
-            const float* rv = kv + c * hshare;
-            const int* ri = ki + c * hshare;
-            for (int i0 = 0; i0 < nc; i0 += 32) {
-                const int i = i0 + lane;
-                const float x = i < nc ? rv[i] : f_ninf();
-                const bool keep = i < nc && x >= pf;
-                const unsigned b = __ballot_sync(0xffffffffu, keep);
-                if (keep) {
-                    const int pos = m + __popc(b & ((1u << lane) - 1u));
-                    if (pos < p.ltot) {
-                        cand_v[pos] = x;
-                        cand_i[pos] = ri[i];
-                    }
-                }
-                m += __popc(b);
-            }
+            if (nc < 0) ovf = true;
+            off[c] = tot;
+            tot += max(nc, 0);
         }
-        if (lane == 0) {
-            ctl->gather_n = m;
-            ctl->lovf = ovf || m > p.ltot;
+        if (!ovf) {
+            for (int c = 0; c < CL; ++c) {
+                const int nc = (c + 1 < CL ? off[c + 1] : tot) - off[c];
+                for (int i = tid; i < nc; i += NT) {
+                    cand_v[off[c] + i] = kv[c * hshare + i];
+                    cand_i[off[c] + i] = ki[c * hshare + i];
+                }
+            }
+            n = tot;
         }
     }
     __syncthreads();
-    if (cand_path && !ovf && !row_err) {
-        n = ctl->gather_n;
-        ovf = ctl->lovf != 0 || n < k;
-    }
+    if (cand_path && !ovf && !row_err) ovf = n < k;
 
     // ---------------- rank 0: the row's token
     int64_t token = V - 1;
