@@ -61,10 +61,11 @@ static __device__ __noinline__ int64_t full_token(const Row<E> R, int drop, floa
 }
 
 // hf's full-row normaliser from the resident row (one CTA per row): max over the candidates (or, when the
-// list failed, the row), then fp64 sum of exp(P - max) in row_visit's thread layout, so the same partial sums.
+// list failed, the row), then the fp64 sum of exp(P - max) in row_visit's thread layout, so the same partial
+// sums.  Inlined: as an out-of-line call it measured about 0.7 us slower per Talker launch.
 template <typename E>
-static __device__ __noinline__ float resident_lse(const Row<E> R, const uint4* slice, int nv, const float* cv, int n,
-                                           bool from_list, Ctl* ctl) {
+__device__ __forceinline__ float resident_lse(const Row<E>& R, const uint4* slice, int nv, const float* cv, int n,
+                                              bool from_list, Ctl* ctl) {
     constexpr int EPV = Elem<E>::EPV;
     const int tid = threadIdx.x, V = R.V;
     float lm = f_ninf();
@@ -86,8 +87,9 @@ static __device__ __noinline__ float resident_lse(const Row<E> R, const uint4* s
     double sacc = 0.0;
     for (int v = tid; v < nv; v += NT) {
         const uint4 q = slice[v];
+        const int e = R.e0 + v * EPV;
 #pragma unroll
-        for (int j = 0; j < EPV; ++j) sacc += (double)b2s_expf(__fsub_rn(R.P(R.e0 + v * EPV + j, Elem<E>::at(q, j)), mu));
+        for (int j = 0; j < EPV; ++j) sacc += (double)b2s_expf(__fsub_rn(R.P(e + j, Elem<E>::at(q, j)), mu));
     }
     if (tid == 0)
         for (int i = 0; i < R.nh; ++i) sacc += (double)b2s_expf(__fsub_rn(R.P(i, Elem<E>::gld(R.rowp, i)), mu));
