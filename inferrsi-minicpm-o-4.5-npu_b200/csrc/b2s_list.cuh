@@ -384,14 +384,15 @@ __device__ __forceinline__ int64_t warp_list_small(const float* cv, const int* c
 }
 
 // The whole list stage: top-k values, top-p threshold (returned in thr_out) and, when `draw`, the token.
-// Warp 0 takes the threshold and, when at most KLIST items are kept, the draw as well -- compaction by
-// ballot, vocabulary order by ranking the (distinct) kept ids, the same inverse-CDF draw as list_draw --
-// with no block barrier in between; more kept items (heavy ties at the threshold) go to list_draw.
-// cv must be 16-byte aligned.  Result in every thread.
+// Warp 0 takes the threshold and the draw -- compaction by ballot, vocabulary order by ranking the (distinct)
+// kept ids, the same inverse-CDF draw as list_draw -- with no block barrier in between, for up to 32 kept
+// items; `in_order` (the list is in vocabulary order already, so the compaction keeps it) skips the ranking
+// and serves up to KLIST.  More kept items (heavy ties at the threshold) go to list_draw.  cv must be 16-byte
+// aligned.  Result in every thread.
 __device__ __forceinline__ int64_t list_sample(const float* cv, const int* ci, int n, int k, bool hf, float lse,
                                                float top_p, int min_keep, bool topk_only, bool draw, int drop_id,
                                                float u, int V, float* vals, float* kv, int* ki, float* sv, int* si,
-                                               const Scr& sc, float& thr_out) {
+                                               const Scr& sc, float& thr_out, bool in_order = false) {
     constexpr int FALLBACK = -2;
     list_topk_values(cv, n, k, vals, sc);
     if (threadIdx.x < 32) {
@@ -400,6 +401,9 @@ __device__ __forceinline__ int64_t list_sample(const float* cv, const int* ci, i
                                 : warp_topp_threshold(vals, k, hf, lse, top_p, min_keep, topk_only);
         int res = 0x7fffffff;
         if (draw) {
+            // the kept items in list order (in vocabulary order already: straight into sv / si)
+            float* ov = in_order ? sv : kv;
+            int* oi = in_order ? si : ki;
             int kn = 0;
             for (int i0 = 0; i0 < n; i0 += 32) {
                 const int i = i0 + lane;
@@ -407,12 +411,16 @@ __device__ __forceinline__ int64_t list_sample(const float* cv, const int* ci, i
                 const unsigned m = __ballot_sync(0xffffffffu, keep);
                 const int pos = kn + __popc(m & ((1u << lane) - 1u));
                 if (keep && pos < KLIST) {
-                    kv[pos] = cv[i];
-                    ki[pos] = ci[i];
+                    ov[pos] = cv[i];
+                    oi[pos] = ci[i];
                 }
                 kn += __popc(m);
             }
-            if (kn <= 32) {
+            if (in_order) {
+                __syncwarp();
+                res = kn <= 32 ? warp_draw32(sv[lane < kn ? lane : 0], kn, u)
+                               : kn <= KLIST ? warp_draw_sorted(sv, kn, u) : FALLBACK;
+            } else if (kn <= 32) {
                 // one kept item per lane: vocabulary order by counting the smaller ids (they are distinct)
                 __syncwarp();
                 const int id = lane < kn ? ki[lane] : 0x7fffffff;

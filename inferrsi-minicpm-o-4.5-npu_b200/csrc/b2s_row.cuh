@@ -78,6 +78,8 @@ struct Params {
     // the row slice live, and the slice capacity in 16-byte vectors
     int cl, ltot, slice_vecs;
     uint32_t off_bar, off_slice;
+    // short-row kernel (b2s_short.cu): one flag byte per element (in the history), 4 per word
+    uint32_t off_cnt, cnt_words;
     // several frames in one launch (b2s_sample_frames): logits of frame f start f * fstride elements after frame 0's;
     // tokens and uniform values are [frames, rows]; the state advances in place from frame to frame
     int frames;
@@ -542,5 +544,10 @@ __device__ float exact_threshold(const Row<E>& R, uint32_t kth, int k, bool hf, 
 // The row-resident kernel's instantiations (b2s_resident.cu): logits type, omni order fixed at compile time.
 using ResKernel = void (*)(const Params);
 ResKernel resident_kernel_for(bool bf16, bool omni);
+
+// The short-row kernel (b2s_short.cu): rows of at most SHORT_EPT * NT interior elements, each thread's share held
+// in registers; same instantiations.
+constexpr int SHORT_EPT = 16;
+ResKernel short_kernel_for(bool bf16, bool omni);
 
 }  // namespace b2s

@@ -1080,6 +1080,58 @@ static bool resident_layout(b2s::Params& p, const b2s_sample_args* a, int CL, in
     return off <= 227 * 1024;
 }
 
+// Shared-memory layout of the short-row kernel (b2s_short.cu); false when the rows are not short: more interior
+// elements than its threads hold in registers, under 64 bytes (no interior vector), or a window longer than
+// 255 (one position per thread, counted by scanning the window).  Fills p's short-row fields and list sizes.
+static bool short_layout(b2s::Params& p, const b2s_sample_args* a, int es, int kmax) {
+    using namespace b2s;
+    const int64_t row_bytes = (int64_t)a->vocab * es;
+    if (row_bytes < 64 || row_bytes / 16 > (int64_t)(SHORT_EPT * es / 16) * NT || a->window > 255) return false;
+    const int kfast = kmax < KFAST ? kmax : KFAST;
+    int lcap = next_pow2(4 * kfast + 128);
+    lcap = lcap < 256 ? 256 : (lcap > 2048 ? 2048 : lcap);
+    p.cl = 1;
+    p.lcap = lcap;
+    p.ltot = lcap;
+    p.csplit = 0;
+    p.cnt_words = (uint32_t)((a->vocab + 16 + 15) / 16 * 4);  // flag bytes: id - e0 + EPV < vocab + 16, whole 16-byte groups
+    uint32_t off = 0;
+    p.off_ctl = off;
+    off = align_up(off + (uint32_t)sizeof(Ctl), 128);
+    p.off_cnt = off;
+    off = align_up(off + p.cnt_words * 4, 16);
+    p.off_bits = off;
+    off = align_up(off + p.bitwords * 4, 16);
+    p.off_pref = off;
+    off = align_up(off + p.bitwords / 4 * 2, 16);
+    p.off_hcnt = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_hid = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_hpos = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_htv = off;
+    off = align_up(off + (uint32_t)p.hcap * 4, 16);
+    p.off_hraw = off;  // the history ids' processed values, indexed like the flag bytes
+    off = align_up(off + p.cnt_words * 16, 16);
+    p.off_hstage = off;
+    off = align_up(off + (uint32_t)a->window * 8, 16);
+    p.off_atab = off;
+    off = align_up(off + (uint32_t)(a->window <= 0 ? 0 : a->alpha_len) * 4, 16);
+    p.off_cand = off;
+    off = align_up(off + (uint32_t)p.ltot * 4, 16);
+    p.off_candi = off;
+    off = align_up(off + (uint32_t)p.ltot * 4, 16);
+    p.off_lst = off;
+    off = align_up(off + (uint32_t)p.ltot * 16, 16);
+    p.off_vals = off;
+    off = align_up(off + (uint32_t)p.nvals * 4, 16);
+    p.off_hist = off;
+    off = align_up(off + NBUCKET * 4, 16);
+    p.smem_total = off;
+    return off <= 227 * 1024;
+}
+
 static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut* so, int frames = 1,
                          int64_t fstride = 0) {
     using namespace b2s;
@@ -1233,6 +1285,41 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
         const bool res_ok = lean && draws && !identity && !streamed && kmax <= KLIST;
         int CL = 0;
         Params rp = p;
+        if (a->cluster == 0 && res_ok && short_layout(rp, a, es, kmax)) {
+            // short rows: one CTA per row, the row's elements in its threads' registers (b2s_short.cu)
+            const bool omni = a->semantics == B2S_SEM_OMNI;
+            ResKernel kern = short_kernel_for(a->logits_dtype == B2S_DTYPE_BF16, omni);
+            {
+                static std::mutex mu;
+                static uint64_t done[4] = {0, 0, 0, 0};
+                int dev = 0;
+                e = cudaGetDevice(&dev);
+                if (e != cudaSuccess) return cuda_fail(e);
+                std::lock_guard<std::mutex> g(mu);
+                const int ti = (a->logits_dtype == B2S_DTYPE_BF16 ? 2 : 0) + (omni ? 1 : 0);
+                const uint64_t bit = 1ull << (dev & 63);
+                if (!(done[ti] & bit)) {
+                    e = set_smem_attr(kern, 227 * 1024);
+                    if (e != cudaSuccess) return cuda_fail(e);
+                    done[ti] |= bit;
+                }
+            }
+            cudaLaunchConfig_t cfg;
+            memset(&cfg, 0, sizeof(cfg));
+            cfg.gridDim = dim3((unsigned)a->rows, 1, 1);
+            cfg.blockDim = dim3(NT, 1, 1);
+            cfg.dynamicSmemBytes = rp.smem_total;
+            cfg.stream = (cudaStream_t)stream;
+            cudaLaunchAttribute attr;
+            attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr.val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = &attr;
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, kern, rp);
+            if (e != cudaSuccess) return cuda_fail(e);
+            return B2S_OK;
+        }
+        rp = p;
         if (a->cluster != 0) {
             if (!res_ok || (a->semantics == B2S_SEM_HF && a->cluster > 1) || !resident_layout(rp, a, a->cluster, es, kmax))
                 return B2S_ERR_UNSUPPORTED;

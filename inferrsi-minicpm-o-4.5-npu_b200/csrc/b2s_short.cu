@@ -1,0 +1,407 @@
+// Short-row sampling kernel (sm_100a): the decode-step form of b2s_sample for rows of at most SHORT_EPT * NT
+// interior elements -- the Talker's codec vocabulary (6,562 ids) in fp32 or bf16 -- one CTA per row.
+//
+// Such a row is a few tens of KB: its step is as long as its chain of dependent phases, not as its bytes.
+// The kernel keeps that chain short and its instructions few:
+//
+//   loads:    every thread requests its interior vectors (tid, tid + NT, ...: the thread layout of the other
+//             row kernels, so the same fp64 partial sums) into registers; threads 0 / 1 the head / tail
+//             elements outside the 16-byte interior, as one more vector (slot); thread j < W its history id
+//             and, once that has landed, the id's raw value.
+//   history:  thread j counts its id's occurrences in the staged window, takes the id's processed value and
+//             writes it, with a flag byte, into tables indexed like the row (byte id - e0 + EPV), so that one
+//             aligned shared word holds the flags of a vector.  No bitmap, no ranks, no atomics.
+//   values:   each thread turns its elements into processed values in registers, taking a flagged element's
+//             value from the table, and keeps its maximum.
+//   tau:      the k-th largest of the warps' ceil(k/16) largest thread maxima, ranked by all threads at once;
+//             each maximum is a distinct element, so tau bounds the row's k-th largest processed value from
+//             below, exactly (the comparison is on processed values: no rounding margin).
+//   one pass: the elements >= tau go into the candidate list in vocabulary order (a block scan of the
+//             per-slot counts gives each thread its positions), and (hf) the fp64 sum of exp(P - max) for the
+//             full-row normaliser (talker_sampler.py:112) runs beside it.
+//
+// Then the list stage of b2s_list.cuh -- the list being in vocabulary order, one warp draws from up to 128
+// kept items -- and the state epilogue.  A row the list cannot serve (NaN, an unusable tau, more candidates
+// than the list holds) builds the history structures and takes the exact full-row path; hf frame-0 rows take
+// the ordered scan: both shared with the row-resident kernel (b2s_rowpaths.cuh) and out of line.  The kernel
+// waits on nothing but its own loads and block barriers.
+#include "b2s_rowpaths.cuh"
+
+namespace b2s {
+
+// Processed values of one vector's elements (ids e .. e + EPV - 1; past `valid`, -inf).  fw: their flag bytes
+// (an element with a history id takes its value from hval[c + j], c the table index of element e); cens: the
+// censored EOS (omni), -inf whatever its history.
+template <typename E>
+__device__ __forceinline__ void short_values(const Row<E>& R, const float* hval, int cens, uint4 q, uint64_t fw, int e,
+                                             int c, int valid, float* out, float& tmax) {
+    constexpr int EPV = Elem<E>::EPV;
+#pragma unroll
+    for (int j = 0; j < EPV; ++j) out[j] = j < valid ? R.f(Elem<E>::at(q, j)) : f_ninf();
+    if (fw != 0u) {
+#pragma unroll
+        for (int j = 0; j < EPV; ++j)
+            if ((fw >> (8 * j)) & 255u) out[j] = hval[c + j];
+    }
+    if ((unsigned)(cens - e) < (unsigned)valid) {
+#pragma unroll
+        for (int j = 0; j < EPV; ++j)
+            if (e + j == cens) out[j] = f_ninf();
+    }
+#pragma unroll
+    for (int j = 0; j < EPV; ++j) tmax = fmaxf(tmax, out[j]);
+}
+
+// The exact full-row path of a short row: the whole-row history structures first (the register pass keeps
+// only flags), then the radix select, threshold and ordered draw that every row kernel falls back on.
+template <typename E>
+static __device__ __noinline__ int64_t short_exact(const Params p, Row<E> R, HistBufs hb, int k, bool hf, float lse,
+                                                   float top_p, bool topk_only, int drop, bool pen_hist, bool censor,
+                                                   float T, float u, uint32_t* hist, float* vals, Ctl* ctl) {
+    const bool use_ht = pen_hist || censor;
+    R.bits = use_ht ? hb.bits : nullptr;
+    R.pref = hb.pref;
+    R.htv = hb.htv;
+    R.censor = censor ? p.eos : -1;
+    if (use_ht) hist_rebuild<E>(p, R, hb, hf, pen_hist, censor, T, ctl);
+    return exact_token<E>(R, k, hf, lse, top_p, p.min_keep, topk_only, drop, u, hist, vals, ctl);
+}
+
+template <typename E, int SEM>
+__global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int EPV = Elem<E>::EPV, ES = Elem<E>::SZ, SV = SHORT_EPT / EPV;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int r = (int)blockIdx.x;
+    Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
+    uint32_t* flags = reinterpret_cast<uint32_t*>(smem + p.off_cnt);  // byte id - e0 + EPV: id is in the history
+    float* hval = reinterpret_cast<float*>(smem + p.off_hraw);        // [id - e0 + EPV]: its processed value
+    HistBufs hb;
+    hb.bits = reinterpret_cast<uint32_t*>(smem + p.off_bits);
+    hb.pref = reinterpret_cast<uint16_t*>(smem + p.off_pref);
+    hb.hcnt = reinterpret_cast<uint32_t*>(smem + p.off_hcnt);
+    hb.hid = reinterpret_cast<int*>(smem + p.off_hid);
+    hb.hpos = reinterpret_cast<int*>(smem + p.off_hpos);
+    hb.htv = reinterpret_cast<float*>(smem + p.off_htv);
+    int64_t* hstage = reinterpret_cast<int64_t*>(smem + p.off_hstage);
+    float* atab = reinterpret_cast<float*>(smem + p.off_atab);
+    hb.hstage = hstage;
+    hb.atab = atab;
+    float* cand_v = reinterpret_cast<float*>(smem + p.off_cand);
+    int* cand_i = reinterpret_cast<int*>(smem + p.off_candi);
+    float* kv = reinterpret_cast<float*>(smem + p.off_lst);
+    int* ki = reinterpret_cast<int*>(kv + p.ltot);
+    float* sv = kv + 2 * p.ltot;
+    int* si = reinterpret_cast<int*>(kv + 3 * p.ltot);
+    float* vals = reinterpret_cast<float*>(smem + p.off_vals);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + p.off_hist);
+    const int V = p.V;
+    pdl_wait_then_release();  // nothing global is read before the previous kernel of the stream is done
+
+    // ---------------- loads: this thread's row elements and history id (registers), the penalty table
+    const int64_t* hrow = p.hist ? p.hist + (int64_t)r * p.hstride : nullptr;
+    const bool hthread = hrow != nullptr && tid < p.W;  // W <= 255 < NT: one history position per thread
+    const int64_t hv = hthread ? hrow[tid] : -1;
+    if (hrow && p.W > 0 && p.alpha)
+        for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], p.alpha + (int64_t)r * p.alpha_stride + j);
+    Row<E> R;
+    R.rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
+    R.V = V;
+    {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(R.rowp), b = a + (uintptr_t)V * ES;
+        const uintptr_t ace = (a + 15) & ~(uintptr_t)15, bfl = b & ~(uintptr_t)15;
+        // the launcher sends only rows of >= 64 bytes: the interior holds at least one vector
+        R.nh = (int)((ace - a) / ES);
+        R.nvec = (int)((bfl - ace) / 16);
+        R.gvec = reinterpret_cast<const uint4*>(ace);
+        R.e0 = R.nh;
+    }
+    uint4 q[SV + 1];  // interior vectors tid + s * NT, then (threads 0 / 1) the head / tail as one more vector
+#pragma unroll
+    for (int s = 0; s < SV; ++s) {
+        const int v = tid + s * NT;
+        q[s] = v < R.nvec ? ldg_stream(R.gvec + v) : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
+    }
+    const int i_end = R.e0 + R.nvec * EPV;
+    const int x0 = tid == 0 ? 0 : i_end;                       // first element of the edge slot
+    const int nx = tid == 0 ? R.nh : tid == 1 ? V - i_end : 0;  // < EPV
+    {
+        uint32_t w[4] = {Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG};
+#pragma unroll
+        for (int j = 0; j < EPV - 1; ++j) {
+            if (j < nx) {
+                const uint32_t b = __float_as_uint(Elem<E>::gld(R.rowp, x0 + j));
+                if constexpr (ES == 4) {
+                    w[j] = b;
+                } else {  // element j is the low (even j) or high (odd j) half of word j / 2
+                    w[j >> 1] = (j & 1) ? ((w[j >> 1] & 0x0000ffffu) | (b & 0xffff0000u)) : ((w[j >> 1] & 0xffff0000u) | (b >> 16));
+                }
+            }
+        }
+        q[SV] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    const int64_t step = p.steps ? p.steps[r] : 0;
+    const bool is_live = (p.active ? p.active[r] != 0 : true) && !(p.finished ? p.finished[r] != 0 : false);
+    const float T = p.rT ? p.rT[r] : p.T;
+    const float top_p = p.rP ? p.rP[r] : p.top_p;
+    const int top_k = p.rK ? p.rK[r] : p.top_k;
+    const int64_t min_new = p.rminn ? p.rminn[r] : p.min_new, max_new = p.rmaxn ? p.rmaxn[r] : p.max_new;
+    if (tid == 0) ctl->thr = f_ninf();  // tau, until a rank finds it
+
+    // ---------------- mode
+    const bool hf = SEM >= 0 ? SEM == B2S_SEM_HF : p.sem == B2S_SEM_HF;
+    const bool eos_ok = p.eos >= 0 && p.eos < V;
+    const bool masked_eos = eos_ok && step < min_new;
+    int mode;
+    if (!is_live) mode = MODE_SKIP;
+    else if (step >= max_new - 1) mode = MODE_FORCED;
+    else if (hf && step <= 0) mode = MODE_FULL;
+    else mode = MODE_FILTER;
+    int k = 0;
+    if (mode == MODE_FILTER) {
+        k = min(max(top_k, max(p.min_keep, 1)), V);
+        if (k > p.kbuf) {
+            mode = MODE_FAIL;
+            if (tid == 0) set_status(p, B2S_STATUS_TOPK_LIMIT);
+        }
+    }
+    if (tid == 32) {
+        ctl->u = (p.rng == B2S_RNG_UNIFORM || !p.seeds) ? (p.uvals ? p.uvals[r] : 0.0f)
+                 : p.rng == B2S_RNG_PHILOX ? uniform_philox(p.seeds[r], step, p.requests ? p.requests[r] : 0)
+                                           : uniform_counter(p.seeds[r], step);
+    }
+    R.T = T;
+    R.identity = false;
+    R.bits = nullptr;  // the register pass keeps flags; the full-row paths build their own structures
+    R.pref = nullptr;
+    R.htv = nullptr;
+    R.censor = -1;
+    const bool pen_hist = mode == MODE_FILTER && p.W > 0 && hrow != nullptr;
+    const bool censor = mode == MODE_FILTER && !hf && masked_eos;  // omni: EOS is -inf before anything else
+    const int cens = censor ? p.eos : -1;
+    if (pen_hist)
+        for (uint32_t g = tid; g < p.cnt_words / 4; g += NT) reinterpret_cast<uint4*>(flags)[g] = make_uint4(0u, 0u, 0u, 0u);
+    // the history id's raw value, requested as soon as the id has landed
+    const bool hvalid = pen_hist && hthread && hv >= 0 && hv < V;
+    float hx = 0.0f;
+    if (hvalid) hx = Elem<E>::gld(R.rowp, hv);
+    if (hthread) hstage[tid] = hv;
+    cp_async_wait_all();
+    __syncthreads();  // the window and the penalty table are staged; the flags are zero
+
+    // ---------------- history: occurrences, processed value, flag
+    if (pen_hist && hthread) {
+        if (hv >= V) set_status(p, B2S_STATUS_HISTORY_RANGE);
+        if (hvalid) {
+            int n = 0;
+            for (int j = 0; j < p.W; ++j) n += hstage[j] == hv;
+            const float v = hv == cens ? f_ninf() : hist_proc_value(p, atab, hf, false, T, n, hx);
+            const int c = (int)hv - R.e0 + EPV;
+            hval[c] = v;  // every position of the id writes the same value
+            reinterpret_cast<uint8_t*>(flags)[c] = 1u;
+        }
+    }
+    __syncthreads();  // the history's values and flags are complete
+
+    // ---------------- processed values and the thread's maximum
+    float P[(SV + 1) * EPV];
+    float tmax = f_ninf();
+    auto flags_at = [&](int b) -> uint64_t {  // the EPV flag bytes from byte b (a multiple of EPV)
+        if (!pen_hist) return 0u;
+        if constexpr (EPV == 4) return (uint64_t)flags[b >> 2];
+        else return reinterpret_cast<const uint64_t*>(flags)[b >> 3];
+    };
+#pragma unroll
+    for (int s = 0; s < SV; ++s) {
+        const int v = tid + s * NT;
+        const int valid = v < R.nvec ? EPV : 0;
+        const uint64_t fw = valid ? flags_at((v + 1) * EPV) : 0u;
+        short_values<E>(R, hval, cens, q[s], fw, R.e0 + v * EPV, (v + 1) * EPV, valid, &P[s * EPV], tmax);
+    }
+    {
+        // the head's flags end at byte EPV, the tail's start at the vector boundary after the interior
+        uint64_t fw = 0u;
+        if (nx > 0) fw = tid == 0 ? flags_at(0) >> (8 * (EPV - R.nh)) : flags_at((R.nvec + 1) * EPV);
+        short_values<E>(R, hval, cens, q[SV], fw, x0, x0 - R.e0 + EPV, nx, &P[SV * EPV], tmax);
+    }
+
+    // ---------------- tau: the k-th largest of the warps' jw largest thread maxima; the row's maximum
+    const bool cand_path = mode == MODE_FILTER && k <= KFAST && !(p.flags & B2S_FLAG_FORCE_GENERAL) && T >= 1e-6f &&
+                           T <= 1e6f;
+    const int jw = (k + NWARP - 1) / NWARP;
+    const int ng = NWARP * jw;  // gathered maxima, a multiple of 16, <= 128
+    int ngp = 16;
+    while (ngp < ng) ngp <<= 1;  // ranked as ngp values (the rest -inf)
+    bool has_nan = false;
+#pragma unroll
+    for (int j = 0; j < (SV + 1) * EPV; ++j) has_nan |= P[j] != P[j];
+    {
+        uint32_t key = okey(tmax);  // tmax is never NaN (fmaxf keeps the other operand)
+        const int jx = cand_path ? jw : 1;
+        for (int t = 0; t < jx; ++t) {
+            const uint32_t mk = __reduce_max_sync(0xffffffffu, key);
+            const unsigned who = __ballot_sync(0xffffffffu, key == mk);
+            if (lane == __ffs(who) - 1) key = 0u;  // below every key: taken
+            if (lane == 0) {
+                if (cand_path) vals[warp * jw + t] = okey_to_f(mk);
+                if (t == 0) ctl->red_u[warp] = mk;
+            }
+        }
+        if (cand_path && tid < ngp - ng) vals[ng + tid] = f_ninf();
+    }
+    has_nan = __syncthreads_or(has_nan) != 0;
+    uint32_t mkey = ctl->red_u[0];
+#pragma unroll
+    for (int w = 1; w < NWARP; ++w) mkey = max(mkey, ctl->red_u[w]);
+    const float m = okey_to_f(mkey);  // the row's largest processed value (NaN aside)
+    if (cand_path && !has_nan) {
+        // value i of the ngp is ranked by S threads of one warp, each over L of the values
+        const int S = min(NT / ngp, ngp), L = ngp / S;
+        const int i = tid / S, sg = tid % S;
+        if (i < ngp) {
+            const float x = vals[i];
+            int gt = 0, eq = 0;
+            for (int j = sg * L; j < sg * L + L; ++j) {
+                const float y = vals[j];
+                gt += y > x;
+                eq += y == x;
+            }
+            for (int o = 1; o < S; o <<= 1) {
+                gt += __shfl_xor_sync(0xffffffffu, gt, o);
+                eq += __shfl_xor_sync(0xffffffffu, eq, o);
+            }
+            if (sg == 0 && x > f_ninf() && gt < k && k <= gt + eq) ctl->thr = x;  // ties: the same value
+        }
+    }
+    __syncthreads();
+    const float tau = ctl->thr;
+    bool ovf = !cand_path || has_nan || !(tau > f_ninf()) || tau == f_inf();
+
+    // ---------------- one pass over the registers: the candidates in vocabulary order, and hf's normaliser sum
+    int n = 0;
+    if (!ovf) {
+        // slots in vocabulary order: thread 0's head, interior slot 0 of every thread, ..., thread 1's tail
+        int cs[SV + 1], inc[SV];
+#pragma unroll
+        for (int s = 0; s <= SV; ++s) {
+            cs[s] = 0;
+#pragma unroll
+            for (int j = 0; j < EPV; ++j) cs[s] += P[s * EPV + j] >= tau;
+        }
+#pragma unroll
+        for (int s = 0; s < SV; ++s) inc[s] = cs[s];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+            for (int s = 0; s < SV; ++s) {
+                const int t = __shfl_up_sync(0xffffffffu, inc[s], o);
+                if (lane >= o) inc[s] += t;
+            }
+        }
+        int* tot = reinterpret_cast<int*>(hist);  // [slot][warp] totals, then the head and tail counts
+        if (lane == 31)
+#pragma unroll
+            for (int s = 0; s < SV; ++s) tot[s * NWARP + warp] = inc[s];
+        if (tid < 2) tot[SV * NWARP + tid] = cs[SV];
+        __syncthreads();
+        int base = tot[SV * NWARP];
+        int off[SV + 1];
+        off[SV] = 0;  // thread 0's head
+#pragma unroll
+        for (int s = 0; s < SV; ++s) {
+            const int4* t4 = reinterpret_cast<const int4*>(tot + s * NWARP);
+            int all = 0, pre = 0;
+#pragma unroll
+            for (int w4 = 0; w4 < NWARP / 4; ++w4) {
+                const int4 x = t4[w4];
+                all += x.x + x.y + x.z + x.w;
+                pre += (4 * w4 < warp ? x.x : 0) + (4 * w4 + 1 < warp ? x.y : 0) + (4 * w4 + 2 < warp ? x.z : 0) +
+                       (4 * w4 + 3 < warp ? x.w : 0);
+            }
+            off[s] = base + pre + inc[s] - cs[s];
+            base += all;
+        }
+        if (tid == 1) off[SV] = base;  // thread 1's tail follows the interior
+        n = base + tot[SV * NWARP + 1];
+#pragma unroll
+        for (int s = 0; s <= SV; ++s) {
+            int pos = off[s];
+#pragma unroll
+            for (int j = 0; j < EPV; ++j) {
+                if (P[s * EPV + j] >= tau) {
+                    if (pos < p.ltot) {  // past it: the row takes the exact path
+                        cand_v[pos] = P[s * EPV + j];
+                        cand_i[pos] = s < SV ? R.e0 + (tid + s * NT) * EPV + j : x0 + j;
+                    }
+                    ++pos;
+                }
+            }
+        }
+        if (n > p.ltot || n < k) ovf = true;
+    }
+    float lse = 0.0f;
+    if (mode == MODE_FILTER && hf) {
+        // max, then the fp64 sum of exp(P - max) in the other row kernels' order (vectors, then the edges)
+        const float mu = (m == f_inf() || m == f_ninf()) ? 0.0f : m;
+        double sacc = 0.0;
+#pragma unroll
+        for (int s = 0; s <= SV; ++s) {
+            const bool live = s < SV ? tid + s * NT < R.nvec : nx > 0;
+            if (live) {
+#pragma unroll
+                for (int j = 0; j < EPV; ++j)
+                    if (s < SV || j < nx) sacc += (double)b2s_expf(__fsub_rn(P[s * EPV + j], mu));
+            }
+        }
+        lse = __fadd_rn((float)log((double)(float)block_sum(sacc, ctl->red_d)), mu);
+    } else {
+        __syncthreads();
+    }
+
+    // ---------------- the row's token
+    int64_t token = V - 1;
+    const int drop = (hf && masked_eos) ? p.eos : -1;
+    const bool topk_only = (p.flags & B2S_FLAG_TOPK_ONLY) != 0;
+    if (mode == MODE_FILTER) {
+        if (!ovf && n <= 2 * KLIST) {
+            const Scr sc{hist, ctl->rctl, &ctl->gather_n, &ctl->kn, &ctl->thr, ctl->red_d, ctl->red_f, ctl->red_i};
+            float thr;
+            token = list_sample(cand_v, cand_i, n, k, hf, lse, top_p, p.min_keep, topk_only, true, drop, ctl->u, V, vals,
+                                kv, ki, sv, si, sc, thr, true);
+        } else if (!ovf) {
+            token = block_list_token(cand_v, cand_i, kv, ki, sv, si, n, k, hf, lse, top_p, p.min_keep, topk_only, drop,
+                                     ctl->u, V, vals, hist, ctl);
+        } else {
+            token = short_exact<E>(p, R, hb, k, hf, lse, top_p, topk_only, drop, pen_hist, censor, T, ctl->u, hist,
+                                   vals, ctl);
+        }
+    }
+    if (mode == MODE_FORCED) token = eos_ok ? (int64_t)p.eos : (int64_t)(V - 1);
+    if (mode == MODE_FULL) token = full_token<E>(R, drop, ctl->u, ctl);
+
+    // ---------------- state epilogue
+    const int64_t tok_drawn = (mode == MODE_SKIP || mode == MODE_FAIL) ? PAD : token;
+    const bool adv = is_live && tok_drawn != PAD;
+    const int64_t tok = adv ? tok_drawn : PAD;
+    if (tid == 0) {
+        if (p.tokens) p.tokens[r] = tok;
+        if (p.steps_out) p.steps_out[r] = step + (adv ? 1 : 0);
+        if (p.fin_out) {
+            const bool f0 = p.finished ? p.finished[r] != 0 : false;
+            p.fin_out[r] = (uint8_t)(f0 || (adv && tok == (int64_t)p.eos));
+        }
+    }
+    if (p.hist_out && p.W > 0) {
+        int64_t* ho = p.hist_out + (int64_t)r * p.hostride;
+        for (int j = tid; j < p.W; j += NT) ho[j] = adv ? (j + 1 < p.W ? hstage[j + 1] : tok) : hstage[j];
+    }
+}
+
+ResKernel short_kernel_for(bool bf16, bool omni) {
+    static const ResKernel k[2][2] = {
+        {short_kernel<float, -1>, short_kernel<float, B2S_SEM_OMNI>},
+        {short_kernel<__nv_bfloat16, -1>, short_kernel<__nv_bfloat16, B2S_SEM_OMNI>}};
+    return k[bf16 ? 1 : 0][omni ? 1 : 0];
+}
+
+}  // namespace b2s

@@ -85,7 +85,8 @@ def test_sample_matches_oracle_and_reference(pkg, group, case):
     "edge_quantised_hf", "edge_quantised_omni", "edge_temperature_3.0_omni", "edge_penalty_big_hf",
     "edge_min_new_boundary_hf", "edge_bf16_hf", "edge_small_vocab_omni")])
 def test_every_kernel_path_agrees(pkg, group, case):
-    """The streaming kernel (candidate path and forced exact path, with and without processed output) and the
+    """The streaming kernel (candidate path and forced exact path, with and without processed output), the
+    launcher's own pick for a decode step (the short-row kernel for rows it holds in registers), and the
     row-resident kernel at every cluster size it accepts for the case (1, 2, 4 or 8 CTAs per row; candidate
     and forced exact path) give the oracle's bits."""
     ts = pkg.talker_sampler
@@ -96,6 +97,8 @@ def test_every_kernel_path_agrees(pkg, group, case):
         assert np.array_equal(got_t, want_t), (exact, got_t, want_t)
         _, got_t, _ = run_gpu(ts, case, exact=exact, processed=False, flags=ts.FLAG_STREAM)
         assert np.array_equal(got_t, want_t), ("stream", exact, got_t, want_t)
+        _, got_t, _ = run_gpu(ts, case, exact=exact, processed=False)
+        assert np.array_equal(got_t, want_t), ("auto", exact, got_t, want_t)
     ran = []
     k = max(max(c["top_k"] for c in case.cfgs), 1)
     for cluster in (1, 2, 4, 8):
@@ -114,6 +117,42 @@ def test_every_kernel_path_agrees(pkg, group, case):
             assert np.array_equal(got_t, want_t), ("resident", cluster, exact, got_t, want_t)
             ran.append(cluster)
     assert ran or k > 128
+
+
+@pytest.mark.parametrize("group,case", list(_cases()))
+def test_decode_step_matches_oracle(pkg, group, case):
+    """The launcher's pick for a decode step (tokens only: the short-row kernel on Talker rows, the row-resident
+    kernel on Thinker rows) against the oracle, with injected uniforms and with the Philox RNG."""
+    ts = pkg.talker_sampler
+    _, want_t, _, _ = H.run_oracle(case)
+    _, got_t, status = run_gpu(ts, case, processed=False)
+    assert np.array_equal(got_t, want_t), (got_t, want_t)
+    assert status == 0
+
+
+def _kernel_names(fn):
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type.name == "CUDA"}
+
+
+def test_short_rows_take_the_short_kernel(pkg):
+    """Talker-shaped decode steps (fp32 and bf16, hf and omni) launch the short-row kernel; Thinker rows the
+    row-resident kernel; a cluster size asks for the row-resident kernel."""
+    ts = pkg.talker_sampler
+    case = C.talker_batched_cfg2()
+    names = _kernel_names(lambda: run_gpu(ts, case, processed=False))
+    if not names:
+        pytest.skip("the profiler recorded no CUDA kernels here")
+    assert any("short_kernel" in n for n in names), names
+    assert any("short_kernel" in n for n in _kernel_names(lambda: run_gpu(ts, C.talker_order(5, "omni"), processed=False)))
+    names = _kernel_names(lambda: run_gpu(ts, case, processed=False, cluster=1))
+    assert any("resident_kernel" in n for n in names) and not any("short_kernel" in n for n in names), names
+    names = _kernel_names(lambda: run_gpu(ts, C.thinker_cfg3(), processed=False))
+    assert any("resident_kernel" in n for n in names), names
 
 
 def test_draw_matches_reference(pkg):
