@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define B2S_ABI_VERSION 3
+#define B2S_ABI_VERSION 4
 
 /* return codes */
 #define B2S_OK 0
@@ -154,6 +154,14 @@ int b2s_argmax(const void* logits, int32_t logits_dtype, int32_t rows, int32_t v
  */
 int b2s_uniform(const int64_t* seeds, const int64_t* steps, const int64_t* requests, int64_t n, int32_t rng,
                 float* out, void* stream);
+
+/*
+ * The sampler's fp32 exp (its numerics spec: every exponential the kernels take) evaluated on the device, for
+ * verification against a CPU restatement (no counterpart in the reference, whose exponentials are torch's):
+ * y[i] = exp(x[i]) in the scalar form; y_pair[i] the same through the paired form the kernels use for x[i] <= 0
+ * (the scalar form elsewhere).  The two must agree bit for bit.
+ */
+int b2s_expf_spec(const float* x, int64_t n, float* y, float* y_pair, void* stream);
 
 /*
  * Vocabulary-sharded head, stage 1 (no counterpart in the reference, which has no multi-device code).

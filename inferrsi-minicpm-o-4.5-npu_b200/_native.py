@@ -61,6 +61,7 @@ CAPI_SIGNATURES = {
                                               ctypes.c_int64, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                               ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                               ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
+    "b2s_expf_spec": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "b2s_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "b2s_last_cuda_error": (ctypes.c_char_p, []),
     "b2s_abi_version": (ctypes.c_int, []),

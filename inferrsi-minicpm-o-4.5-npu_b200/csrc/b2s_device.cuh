@@ -43,6 +43,37 @@ __device__ __forceinline__ float b2s_expf(float x) {
     return x != x ? x : res;
 }
 
+// b2s_expf of two non-positive (or NaN) arguments at once: the same rounded operations, the range reduction and
+// the polynomial in packed fp32x2 arithmetic (each lane one IEEE rn operation, so the same bits as the scalar
+// form).  For x <= 0 the overflow side of b2s_expf (its upper clamp, the scale-down by two and the +inf case)
+// never applies and is left out; every other step is kept.
+__device__ __forceinline__ float2 b2s_expf2_nonpos(float2 x) {
+    const float2 xc = make_float2(fmaxf(x.x, -104.0f), fmaxf(x.y, -104.0f));
+    const float2 t = __fmul2_rn(xc, make_float2(1.44269502162933349609375f, 1.44269502162933349609375f));
+    const float2 n = make_float2(rintf(t.x), rintf(t.y));
+    float2 r = __ffma2_rn(n, make_float2(-0.693145751953125f, -0.693145751953125f), xc);
+    r = __ffma2_rn(n, make_float2(-1.428606765330187045037746429443359375e-6f, -1.428606765330187045037746429443359375e-6f), r);
+    float2 p = make_float2(1.98412701138295233249664306640625e-4f, 1.98412701138295233249664306640625e-4f);
+    p = __ffma2_rn(p, r, make_float2(1.3888889225199818611145019531250e-3f, 1.3888889225199818611145019531250e-3f));
+    p = __ffma2_rn(p, r, make_float2(8.3333337679505348205566406250000e-3f, 8.3333337679505348205566406250000e-3f));
+    p = __ffma2_rn(p, r, make_float2(4.1666667908430099487304687500000e-2f, 4.1666667908430099487304687500000e-2f));
+    p = __ffma2_rn(p, r, make_float2(1.6666667163372039794921875000000e-1f, 1.6666667163372039794921875000000e-1f));
+    p = __ffma2_rn(p, r, make_float2(0.5f, 0.5f));
+    p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
+    p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
+    int n0 = (int)n.x, n1 = (int)n.y;  // [-150, 0]
+    const bool lo0 = n0 < -126, lo1 = n1 < -126;
+    const float2 pl = __fmul2_rn(p, make_float2(5.42101086242752217003726400434970855712890625e-20f,
+                                                5.42101086242752217003726400434970855712890625e-20f));
+    p = make_float2(lo0 ? pl.x : p.x, lo1 ? pl.y : p.y);
+    n0 = lo0 ? n0 + 64 : n0;
+    n1 = lo1 ? n1 + 64 : n1;
+    float2 res = __fmul2_rn(p, make_float2(__uint_as_float((uint32_t)(n0 + 127) << 23), __uint_as_float((uint32_t)(n1 + 127) << 23)));
+    res.x = x.x < -103.97208404541015625f ? 0.0f : res.x;
+    res.y = x.y < -103.97208404541015625f ? 0.0f : res.y;
+    return make_float2(x.x != x.x ? x.x : res.x, x.y != x.y ? x.y : res.y);
+}
+
 __device__ __forceinline__ float f_inf() { return __int_as_float(0x7f800000); }
 __device__ __forceinline__ float f_ninf() { return __int_as_float(0xff800000); }
 

@@ -150,18 +150,6 @@ static __device__ __noinline__ float warp_topp_threshold(const float* vals, int 
     return vals[kept - 1];
 }
 
-// Top-k values + top-p threshold for the whole CTA (k <= KLIST, n >= k); same value in every thread.
-__device__ __forceinline__ float list_threshold(const float* cv, int n, int k, bool hf, float lse, float top_p,
-                                                int min_keep, bool topk_only, float* vals, const Scr& sc) {
-    list_topk_values(cv, n, k, vals, sc);
-    if (threadIdx.x < 32) {
-        const float t = warp_topp_threshold(vals, k, hf, lse, top_p, min_keep, topk_only);
-        if (threadIdx.x == 0) *sc.thr = t;
-    }
-    __syncthreads();
-    return *sc.thr;
-}
-
 // Warp 0: the draw over kn <= 128 items whose values sv[0..kn) are in vocabulary order -- softmax over them,
 // fp64 prefix of the probabilities (rounded to fp32 per prefix), the first position whose prefix exceeds
 // u * total (talker_sampler.py:168-172).  Returns that position in every lane, or 0x7fffffff when none does.
@@ -287,6 +275,55 @@ __device__ __forceinline__ float warp_topp_threshold32(const float* vals, int k,
     return vals[kept - 1];
 }
 
+// Warp 0, 32 < k <= 64: warp_topp_threshold with two values per lane (vals[2 * lane], vals[2 * lane + 1]).  The
+// same fp32 values and fp64 accumulation, associated in pairs (exact whenever the fp64 sums are, as they are for
+// probabilities within 2^29 of each other).
+__device__ __forceinline__ float warp_topp_threshold64(const float* vals, int k, bool hf, float lse, float top_p,
+                                                       int min_keep, bool topk_only) {
+    const int lane = threadIdx.x & 31;
+    const float m = vals[0];
+    const float2 v2 = reinterpret_cast<const float2*>(vals)[lane];
+    float pk[2];
+    double ls = 0.0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const float v = j ? v2.y : v2.x;
+        const float e = 2 * lane + j < k ? b2s_expf(__fsub_rn(v, hf ? lse : m)) : 0.0f;
+        pk[j] = e;
+        ls += (double)e;
+    }
+    if (!hf) {
+        const float sf = (float)warp_sum(ls);
+        ls = 0.0;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            pk[j] = __fdiv_rn(pk[j], sf);  // 0 stays 0 (sf >= 1)
+            ls += (double)pk[j];
+        }
+    }
+    const double incl = warp_incl_scan(ls);
+    double acc = incl - ls;
+    int cnt = 0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        if (2 * lane + j < k) {
+            acc += (double)pk[j];
+            cnt += __fsub_rn((float)acc, pk[j]) < top_p;
+        }
+    }
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    const int kept = topk_only ? k : max(min(min_keep, k), min(cnt, k));
+    return vals[kept - 1];
+}
+
+// The top-p threshold over the sorted top-k values vals[0..k), in warp 0: one, two or four values per lane.
+__device__ __forceinline__ float warp_topp(const float* vals, int k, bool hf, float lse, float top_p, int min_keep,
+                                           bool topk_only) {
+    return k <= 32 ? warp_topp_threshold32(vals, k, hf, lse, top_p, min_keep, topk_only)
+           : k <= 64 ? warp_topp_threshold64(vals, k, hf, lse, top_p, min_keep, topk_only)
+                     : warp_topp_threshold(vals, k, hf, lse, top_p, min_keep, topk_only);
+}
+
 // Warp 0, kn <= 32 items, lane i holding the value v of the i-th item in vocabulary order (any value past
 // kn): warp_draw_sorted with one item per lane.  Returns the position drawn in every lane, or 0x7fffffff.
 __device__ __forceinline__ int warp_draw32(float v, int kn, float u) {
@@ -303,28 +340,27 @@ __device__ __forceinline__ int warp_draw32(float v, int kn, float u) {
     return hit ? __ffs(hit) - 1 : 0x7fffffff;
 }
 
-// One warp (no block barrier): the whole list stage for n <= 128 items and k <= 32 (n >= k).  Lane l takes
-// items l, l + 32, l + 64, l + 96: its rank among the n values (value descending, position ascending -- a
-// permutation, as list_topk_values) from 16-byte loads of cv (16-byte aligned) gives the sorted top-k values;
-// then warp_topp_threshold32, the kept items (value >= threshold, id != drop_id) compacted by ballot, their
-// vocabulary order by counting smaller ids, and warp_draw32.  vals: >= 32 floats; sv: >= 32 floats; si: >= 64
-// ints (16-byte aligned), all private to the warp.  Returns the token in every lane (V - 1 when no prefix
-// exceeds u * total), or -2 when more than 32 items are kept (the caller then runs list_sample).
-__device__ __forceinline__ int64_t warp_list_small(const float* cv, const int* ci, int n, int k, bool hf, float lse,
-                                                   float top_p, int min_keep, bool topk_only, int drop_id, float u,
-                                                   int V, float* vals, float* sv, int* si, float& thr_out) {
+// One warp (no block barrier): the whole list stage for n <= 128 items already in vocabulary order, n >= k.  Lane
+// l takes items l, l + 32, l + 64, l + 96: their ranks among the n values (value descending, position ascending --
+// a permutation, as list_topk_values) from 16-byte loads of cv (16-byte aligned) give the sorted top-k values in
+// vals; then warp_topp, the kept items (value >= threshold, id != drop_id) compacted by ballot into sv / si in list
+// order, which is vocabulary order, and the draw (warp_draw32 / warp_draw_sorted, as list_sample).  Returns the
+// position drawn in si in every lane, or 0x7fffffff; the threshold in thr_out.
+__device__ __forceinline__ int warp_list_ordered(const float* cv, const int* ci, int n, int k, bool hf, float lse,
+                                                 float top_p, int min_keep, bool topk_only, int drop_id, float u,
+                                                 float* vals, float* sv, int* si, float& thr_out) {
     const int lane = threadIdx.x & 31;
+    const int nt = (n + 31) >> 5;  // items per lane, <= 4
     float x[4];
-    int id[4], rk[4];
+    int rk[4];
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
         const int i = lane + 32 * t;
         x[t] = i < n ? cv[i] : __int_as_float(0xff800000);
-        id[t] = i < n ? ci[i] : -1;
         rk[t] = 0;
     }
-    const int nt = (n + 31) >> 5;
     const float4* c4 = reinterpret_cast<const float4*>(cv);
+#pragma unroll 2
     for (int j4 = 0; j4 < ((n + 3) >> 2); ++j4) {
         const float4 v = c4[j4];
         const int j = 4 * j4;
@@ -334,8 +370,7 @@ __device__ __forceinline__ int64_t warp_list_small(const float* cv, const int* c
             if (t < nt) {
                 const int i = lane + 32 * t;
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    rk[t] += (j + c < n) & ((w[c] > x[t]) | ((w[c] == x[t]) & (j + c < i)));
+                for (int c = 0; c < 4; ++c) rk[t] += (j + c < n) & ((w[c] > x[t]) | ((w[c] == x[t]) & (j + c < i)));
             }
         }
     }
@@ -343,44 +378,26 @@ __device__ __forceinline__ int64_t warp_list_small(const float* cv, const int* c
     for (int t = 0; t < 4; ++t)
         if (lane + 32 * t < n && rk[t] < k) vals[rk[t]] = x[t];
     __syncwarp();
-    const float thr = warp_topp_threshold32(vals, k, hf, lse, top_p, min_keep, topk_only);
+    const float thr = warp_topp(vals, k, hf, lse, top_p, min_keep, topk_only);
     thr_out = thr;
-    // the kept items, compacted by ballot
     int kn = 0;
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-        const bool keep = lane + 32 * t < n && x[t] >= thr && id[t] != drop_id;
-        const unsigned m = __ballot_sync(0xffffffffu, keep);
-        const int pos = kn + __popc(m & ((1u << lane) - 1u));
-        if (keep && pos < 32) {
-            sv[pos] = x[t];
-            si[pos] = id[t];
+        if (t < nt) {
+            const int i = lane + 32 * t;
+            const int id = i < n ? ci[i] : -1;
+            const bool keep = i < n && x[t] >= thr && id != drop_id;
+            const unsigned m = __ballot_sync(0xffffffffu, keep);
+            const int pos = kn + __popc(m & ((1u << lane) - 1u));
+            if (keep) {
+                sv[pos] = x[t];
+                si[pos] = id;
+            }
+            kn += __popc(m);
         }
-        kn += __popc(m);
-    }
-    if (kn > 32) return -2;
-    __syncwarp();
-    // vocabulary order: the rank of each kept id among the kept ids (distinct)
-    const int myid = lane < kn ? si[lane] : 0x7fffffff;
-    const float myv = lane < kn ? sv[lane] : 0.0f;
-    int r = 0;
-    const int4* s4 = reinterpret_cast<const int4*>(si);
-    for (int j4 = 0; j4 < ((kn + 3) >> 2); ++j4) {
-        const int4 q = s4[j4];
-        const int j = 4 * j4;
-        r += (j < kn) & (q.x < myid);
-        r += (j + 1 < kn) & (q.y < myid);
-        r += (j + 2 < kn) & (q.z < myid);
-        r += (j + 3 < kn) & (q.w < myid);
     }
     __syncwarp();
-    if (lane < kn) {
-        vals[r] = myv;
-        si[32 + r] = myid;
-    }
-    __syncwarp();
-    const int pos = warp_draw32(vals[lane < kn ? lane : 0], kn, u);
-    return pos == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)si[32 + pos];
+    return kn <= 32 ? warp_draw32(sv[lane < kn ? lane : 0], kn, u) : warp_draw_sorted(sv, kn, u);
 }
 
 // The whole list stage: top-k values, top-p threshold (returned in thr_out) and, when `draw`, the token.
@@ -397,8 +414,7 @@ __device__ __forceinline__ int64_t list_sample(const float* cv, const int* ci, i
     list_topk_values(cv, n, k, vals, sc);
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
-        const float t = k <= 32 ? warp_topp_threshold32(vals, k, hf, lse, top_p, min_keep, topk_only)
-                                : warp_topp_threshold(vals, k, hf, lse, top_p, min_keep, topk_only);
+        const float t = warp_topp(vals, k, hf, lse, top_p, min_keep, topk_only);
         int res = 0x7fffffff;
         if (draw) {
             // the kept items in list order (in vocabulary order already: straight into sv / si)

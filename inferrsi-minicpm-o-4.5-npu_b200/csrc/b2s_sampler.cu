@@ -947,6 +947,26 @@ __global__ void __launch_bounds__(NT) penalty_kernel(const void* x, int rows, in
     }
 }
 
+// The numerics spec's exp on the device: y[i] = b2s_expf(x[i]); y2[i] = the paired non-positive form where
+// x[i] <= 0 or NaN (pairs (2j, 2j+1) when both qualify, else the scalar form).
+__global__ void expf_spec_kernel(const float* x, int64_t n, float* y, float* y2) {
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; 2 * j < n; j += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = 2 * j;
+        const float a = x[i], b = i + 1 < n ? x[i + 1] : 0.0f;
+        y[i] = b2s_expf(a);
+        if (i + 1 < n) y[i + 1] = b2s_expf(b);
+        const bool pa = !(a > 0.0f), pb = !(b > 0.0f);
+        if (pa && pb) {
+            const float2 e = b2s_expf2_nonpos(make_float2(a, b));
+            y2[i] = e.x;
+            if (i + 1 < n) y2[i + 1] = e.y;
+        } else {
+            y2[i] = b2s_expf(a);
+            if (i + 1 < n) y2[i + 1] = b2s_expf(b);
+        }
+    }
+}
+
 __global__ void uniform_kernel(const int64_t* seeds, const int64_t* steps, const int64_t* req, int64_t n, int rng,
                                float* out) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
@@ -1538,6 +1558,18 @@ int b2s_uniform(const int64_t* seeds, const int64_t* steps, const int64_t* reque
     int64_t blocks = (n + threads - 1) / threads;
     if (blocks > 4 * 148) blocks = 4 * 148;
     b2s::uniform_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(seeds, steps, requests, n, rng, out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    return B2S_OK;
+}
+
+int b2s_expf_spec(const float* x, int64_t n, float* y, float* y_pair, void* stream) {
+    if (n < 0 || (n > 0 && (!x || !y || !y_pair))) return B2S_ERR_INVALID;
+    if (n == 0) return B2S_OK;
+    const int threads = 256;
+    int64_t blocks = ((n + 1) / 2 + threads - 1) / threads;
+    if (blocks > 4 * 148) blocks = 4 * 148;
+    b2s::expf_spec_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(x, n, y, y_pair);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return B2S_OK;

@@ -143,8 +143,7 @@ __global__ void __launch_bounds__(NT, 1) shard_merge_kernel(const MergeParams p)
     const int kk = min(k, ntot);  // (every shard sends min(k, its columns) at least, so ntot >= k in practice)
     list_topk_values(cv, ntot, kk, vals, sc);
     if (tid < 32) {
-        const float t = kk <= 32 ? warp_topp_threshold32(vals, kk, false, 0.0f, top_p, p.min_keep, topk_only)
-                                 : warp_topp_threshold(vals, kk, false, 0.0f, top_p, p.min_keep, topk_only);
+        const float t = warp_topp(vals, kk, false, 0.0f, top_p, p.min_keep, topk_only);
         if (tid == 0) ctl->thr = t;
     }
     __syncthreads();

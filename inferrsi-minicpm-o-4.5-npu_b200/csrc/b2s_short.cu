@@ -16,15 +16,18 @@
 //   tau:      the k-th largest of the warps' ceil(k/16) largest thread maxima, ranked by all threads at once;
 //             each maximum is a distinct element, so tau bounds the row's k-th largest processed value from
 //             below, exactly (the comparison is on processed values: no rounding margin).
+//   lse:      (hf) the fp64 sum of exp(P - max) for the full-row normaliser (talker_sampler.py:112), as soon
+//             as the row's maximum is known, beside the ranking of tau.
 //   one pass: the elements >= tau go into the candidate list in vocabulary order (a block scan of the
-//             per-slot counts gives each thread its positions), and (hf) the fp64 sum of exp(P - max) for the
-//             full-row normaliser (talker_sampler.py:112) runs beside it.
+//             per-slot counts gives each thread its positions).
 //
-// Then the list stage of b2s_list.cuh -- the list being in vocabulary order, one warp draws from up to 128
-// kept items -- and the state epilogue.  A row the list cannot serve (NaN, an unusable tau, more candidates
+// Then the list stage of b2s_list.cuh in one warp (the list being in vocabulary order, up to 128 candidates need
+// no block barrier) and the state epilogue.  A row the list cannot serve (NaN, an unusable tau, more candidates
 // than the list holds) builds the history structures and takes the exact full-row path; hf frame-0 rows take
 // the ordered scan: both shared with the row-resident kernel (b2s_rowpaths.cuh) and out of line.  The kernel
 // waits on nothing but its own loads and block barriers.
+#include <type_traits>
+
 #include "b2s_rowpaths.cuh"
 
 namespace b2s {
@@ -193,8 +196,13 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     if (pen_hist && hthread) {
         if (hv >= V) set_status(p, B2S_STATUS_HISTORY_RANGE);
         if (hvalid) {
-            int n = 0;
-            for (int j = 0; j < p.W; ++j) n += hstage[j] == hv;
+            int n = (p.W & 1) ? (int)(hstage[p.W - 1] == hv) : 0;
+            const longlong2* h2 = reinterpret_cast<const longlong2*>(hstage);
+#pragma unroll 4
+            for (int j = 0; j < (p.W >> 1); ++j) {
+                const longlong2 q2 = h2[j];
+                n += (q2.x == hv) + (q2.y == hv);
+            }
             const float v = hv == cens ? f_ninf() : hist_proc_value(p, atab, hf, false, T, n, hx);
             const int c = (int)hv - R.e0 + EPV;
             hval[c] = v;  // every position of the id writes the same value
@@ -254,6 +262,30 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
 #pragma unroll
     for (int w = 1; w < NWARP; ++w) mkey = max(mkey, ctl->red_u[w]);
     const float m = okey_to_f(mkey);  // the row's largest processed value (NaN aside)
+    // hf's full-row normaliser: the fp64 sum of exp(P - max) in the other row kernels' order (vectors, then the
+    // edges; warp butterflies, then the warps in order), the warps' sums handed over at the next barrier
+    // (a row whose maximum is +inf sums to +inf, or NaN with a NaN in it: taken without the exponentials; every
+    // other row's arguments P - max are <= 0 or NaN, the paired form's domain)
+    const bool want_lse = mode == MODE_FILTER && hf;
+    const float mu = (m == f_inf() || m == f_ninf()) ? 0.0f : m;
+    if (want_lse && m != f_inf()) {
+        double sacc = 0.0;
+        const float2 nmu = make_float2(-mu, -mu);
+#pragma unroll
+        for (int s = 0; s <= SV; ++s) {
+            const bool live = s < SV ? tid + s * NT < R.nvec : nx > 0;
+            if (live) {
+#pragma unroll
+                for (int j = 0; j < EPV; j += 2) {
+                    const float2 e = b2s_expf2_nonpos(__fadd2_rn(make_float2(P[s * EPV + j], P[s * EPV + j + 1]), nmu));
+                    if (s < SV || j < nx) sacc += (double)e.x;
+                    if (s < SV || j + 1 < nx) sacc += (double)e.y;
+                }
+            }
+        }
+        sacc = warp_sum(sacc);
+        if (lane == 0) ctl->red_d[warp] = sacc;
+    }
     if (cand_path && !has_nan) {
         // value i of the ngp is ranked by S threads of one warp, each over L of the values
         const int S = min(NT / ngp, ngp), L = ngp / S;
@@ -276,53 +308,60 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     __syncthreads();
     const float tau = ctl->thr;
     bool ovf = !cand_path || has_nan || !(tau > f_ninf()) || tau == f_inf();
+    float lse = 0.0f;
+    if (want_lse && m != f_inf()) {
+        double sum = 0.0;
+#pragma unroll
+        for (int w = 0; w < NWARP; ++w) sum += ctl->red_d[w];
+        lse = __fadd_rn((float)log((double)(float)sum), mu);
+    } else if (want_lse) {
+        lse = has_nan ? __int_as_float(0x7fffffff) : f_inf();
+    }
 
     // ---------------- one pass over the registers: the candidates in vocabulary order, and hf's normaliser sum
     int n = 0;
     if (!ovf) {
-        // slots in vocabulary order: thread 0's head, interior slot 0 of every thread, ..., thread 1's tail
-        int cs[SV + 1], inc[SV];
+        // slots in vocabulary order: thread 0's head, interior slot 0 of every thread, ..., thread 1's tail.  The
+        // interior slots' counts are scanned packed, 16 bits per slot (a slot holds at most NT * EPV = 4096)
+        using Packed = typename std::conditional<(SV <= 2), uint32_t, uint64_t>::type;
+        int cs[SV + 1];
+        Packed c = 0;
 #pragma unroll
         for (int s = 0; s <= SV; ++s) {
             cs[s] = 0;
 #pragma unroll
             for (int j = 0; j < EPV; ++j) cs[s] += P[s * EPV + j] >= tau;
+            if (s < SV) c |= (Packed)cs[s] << (16 * s);
         }
-#pragma unroll
-        for (int s = 0; s < SV; ++s) inc[s] = cs[s];
+        Packed inc = c;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-#pragma unroll
-            for (int s = 0; s < SV; ++s) {
-                const int t = __shfl_up_sync(0xffffffffu, inc[s], o);
-                if (lane >= o) inc[s] += t;
-            }
+            const Packed t = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += t;
         }
-        int* tot = reinterpret_cast<int*>(hist);  // [slot][warp] totals, then the head and tail counts
-        if (lane == 31)
-#pragma unroll
-            for (int s = 0; s < SV; ++s) tot[s * NWARP + warp] = inc[s];
-        if (tid < 2) tot[SV * NWARP + tid] = cs[SV];
+        Packed* tot = reinterpret_cast<Packed*>(hist);  // the warps' packed totals
+        int* edge_n = reinterpret_cast<int*>(hist) + 2 * NWARP * (int)(sizeof(Packed) / 4);  // head, tail counts
+        if (lane == 31) tot[warp] = inc;
+        if (tid < 2) edge_n[tid] = cs[SV];
         __syncthreads();
-        int base = tot[SV * NWARP];
+        Packed all = 0, pre = 0;
+#pragma unroll
+        for (int w = 0; w < NWARP; ++w) {
+            const Packed x = tot[w];
+            all += x;
+            pre += w < warp ? x : (Packed)0;
+        }
+        const Packed mine = pre + inc - c;  // this thread's first position within each slot, packed
+        int base = edge_n[0];
         int off[SV + 1];
         off[SV] = 0;  // thread 0's head
 #pragma unroll
         for (int s = 0; s < SV; ++s) {
-            const int4* t4 = reinterpret_cast<const int4*>(tot + s * NWARP);
-            int all = 0, pre = 0;
-#pragma unroll
-            for (int w4 = 0; w4 < NWARP / 4; ++w4) {
-                const int4 x = t4[w4];
-                all += x.x + x.y + x.z + x.w;
-                pre += (4 * w4 < warp ? x.x : 0) + (4 * w4 + 1 < warp ? x.y : 0) + (4 * w4 + 2 < warp ? x.z : 0) +
-                       (4 * w4 + 3 < warp ? x.w : 0);
-            }
-            off[s] = base + pre + inc[s] - cs[s];
-            base += all;
+            off[s] = base + (int)((mine >> (16 * s)) & 0xffffu);
+            base += (int)((all >> (16 * s)) & 0xffffu);
         }
         if (tid == 1) off[SV] = base;  // thread 1's tail follows the interior
-        n = base + tot[SV * NWARP + 1];
+        n = base + edge_n[1];
 #pragma unroll
         for (int s = 0; s <= SV; ++s) {
             int pos = off[s];
@@ -339,24 +378,7 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
         }
         if (n > p.ltot || n < k) ovf = true;
     }
-    float lse = 0.0f;
-    if (mode == MODE_FILTER && hf) {
-        // max, then the fp64 sum of exp(P - max) in the other row kernels' order (vectors, then the edges)
-        const float mu = (m == f_inf() || m == f_ninf()) ? 0.0f : m;
-        double sacc = 0.0;
-#pragma unroll
-        for (int s = 0; s <= SV; ++s) {
-            const bool live = s < SV ? tid + s * NT < R.nvec : nx > 0;
-            if (live) {
-#pragma unroll
-                for (int j = 0; j < EPV; ++j)
-                    if (s < SV || j < nx) sacc += (double)b2s_expf(__fsub_rn(P[s * EPV + j], mu));
-            }
-        }
-        lse = __fadd_rn((float)log((double)(float)block_sum(sacc, ctl->red_d)), mu);
-    } else {
-        __syncthreads();
-    }
+    __syncthreads();  // the candidate list is complete
 
     // ---------------- the row's token
     int64_t token = V - 1;

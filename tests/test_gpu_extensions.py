@@ -236,3 +236,35 @@ def test_k_frame_block_matches_step_loop(pkg, sem):
             assert torch.equal(st.finished, a.finished)
         assert c.history is hist_c  # advanced in place
         assert bool(a.finished[2]) and int(a.steps[5]) == 0 and (want[:, 5] == ts.PAD).all()
+
+
+def _expf_spec(pkg, x: torch.Tensor):
+    N = pkg._native
+    y, y2 = torch.empty_like(x), torch.empty_like(x)
+    N.check(N.capi().b2s_expf_spec(x.data_ptr(), x.numel(), y.data_ptr(), y2.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream), "b2s_expf_spec")
+    return y, y2
+
+
+def test_device_exp_is_the_oracle_exp(pkg):
+    """The kernels' fp32 exp (b2s_expf) equals the oracle's restatement bit for bit on a dense sweep of its whole
+    range and the special values; the paired form of the normaliser equals it on every argument <= 0."""
+    special = np.array([-0.0, 0.0, -np.inf, np.inf, np.nan, -1e-45, -1e-38, -87.33654, -87.33655, -87.3366,
+                        -103.97208, -103.97209, -104.0, -150.0, 88.72283, 88.72284, 1e-30], np.float32)
+    x = np.concatenate([np.linspace(-110.0, 90.0, 4_000_001, dtype=np.float32), special])
+    y, y2 = _expf_spec(pkg, torch.from_numpy(x).to(DEV))
+    want = orc.expf(x)
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(y2.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_paired_exp_equals_scalar_exp_exhaustively(pkg):
+    """Every fp32 value in [-110, -0] (1.1e9 bit patterns, in chunks): the paired non-positive form == the scalar."""
+    lo = 0x80000000  # -0.0; bit patterns grow toward -110 (0xC2DC0000)
+    hi = int(np.array([-110.0], np.float32).view(np.uint32)[0])
+    chunk = 1 << 26
+    for start in range(lo, hi + 1, chunk):
+        n = min(chunk, hi + 1 - start)
+        bits = torch.arange(start - (1 << 32), start - (1 << 32) + n, dtype=torch.int64, device=DEV).to(torch.int32)
+        y, y2 = _expf_spec(pkg, bits.view(torch.float32))
+        assert torch.equal(y.view(torch.int32), y2.view(torch.int32)), hex(start)
