@@ -340,61 +340,78 @@ __device__ __forceinline__ int warp_draw32(float v, int kn, float u) {
     return hit ? __ffs(hit) - 1 : 0x7fffffff;
 }
 
-// One warp (no block barrier): the whole list stage for n <= 128 items already in vocabulary order, n >= k.  Lane
-// l takes items l, l + 32, l + 64, l + 96: their ranks among the n values (value descending, position ascending --
-// a permutation, as list_topk_values) from 16-byte loads of cv (16-byte aligned) give the sorted top-k values in
-// vals; then warp_topp, the kept items (value >= threshold, id != drop_id) compacted by ballot into sv / si in list
-// order, which is vocabulary order, and the draw (warp_draw32 / warp_draw_sorted, as list_sample).  Returns the
-// position drawn in si in every lane, or 0x7fffffff; the threshold in thr_out.
-__device__ __forceinline__ int warp_list_ordered(const float* cv, const int* ci, int n, int k, bool hf, float lse,
-                                                 float top_p, int min_keep, bool topk_only, int drop_id, float u,
-                                                 float* vals, float* sv, int* si, float& thr_out) {
+// Bitonic sort, descending, of the warp's 32 * E values: lane l holds elements l * E .. l * E + E - 1 in x.
+// Pairs E apart or more are exchanged across lanes by shuffles, nearer pairs inside the lane.  NaN-free input.
+template <int E>
+__device__ __forceinline__ void warp_bitonic_desc(float (&x)[E]) {
     const int lane = threadIdx.x & 31;
-    const int nt = (n + 31) >> 5;  // items per lane, <= 4
-    float x[4];
-    int rk[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        const int i = lane + 32 * t;
-        x[t] = i < n ? cv[i] : __int_as_float(0xff800000);
-        rk[t] = 0;
-    }
-    const float4* c4 = reinterpret_cast<const float4*>(cv);
-#pragma unroll 2
-    for (int j4 = 0; j4 < ((n + 3) >> 2); ++j4) {
-        const float4 v = c4[j4];
-        const int j = 4 * j4;
-        const float w[4] = {v.x, v.y, v.z, v.w};
+    for (int size = 2; size <= 32 * E; size <<= 1) {
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            if (t < nt) {
-                const int i = lane + 32 * t;
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride >= E) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) rk[t] += (j + c < n) & ((w[c] > x[t]) | ((w[c] == x[t]) & (j + c < i)));
+                for (int e = 0; e < E; ++e) {
+                    const int i = lane * E + e;
+                    const float y = __shfl_xor_sync(0xffffffffu, x[e], stride / E);
+                    // the lower index of a pair keeps the larger value in a descending block
+                    x[e] = (((i & size) == 0) == ((i & stride) == 0)) ? fmaxf(x[e], y) : fminf(x[e], y);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    const int f = e ^ stride;
+                    if (f > e) {
+                        const bool desc = ((lane * E + e) & size) == 0;
+                        const float a = x[e], b = x[f];
+                        x[e] = desc ? fmaxf(a, b) : fminf(a, b);
+                        x[f] = desc ? fminf(a, b) : fmaxf(a, b);
+                    }
+                }
             }
         }
     }
+}
+
+// The sorted top-k values of cv[0..n) (n <= 32 * E, k <= n) into vals[0..k), by one warp.
+template <int E>
+__device__ __forceinline__ void warp_topk_sorted(const float* cv, int n, int k, float* vals) {
+    const int lane = threadIdx.x & 31;
+    float x[E];
 #pragma unroll
-    for (int t = 0; t < 4; ++t)
-        if (lane + 32 * t < n && rk[t] < k) vals[rk[t]] = x[t];
+    for (int e = 0; e < E; ++e) x[e] = lane * E + e < n ? cv[lane * E + e] : __int_as_float(0xff800000);
+    warp_bitonic_desc<E>(x);
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+        if (lane * E + e < k) vals[lane * E + e] = x[e];
     __syncwarp();
+}
+
+// One warp (no block barrier): the whole list stage for n <= 128 NaN-free items already in vocabulary order,
+// n >= k.  The sorted top-k values (warp_topk_sorted), warp_topp, the kept items (value >= threshold, id !=
+// drop_id) compacted by ballot into sv / si in list order -- vocabulary order --, and the draw (warp_draw32 /
+// warp_draw_sorted, as list_sample).  Returns the position drawn in si in every lane, or 0x7fffffff.
+__device__ __forceinline__ int warp_list_sorted(const float* cv, const int* ci, int n, int k, bool hf, float lse,
+                                                float top_p, int min_keep, bool topk_only, int drop_id, float u,
+                                                float* vals, float* sv, int* si) {
+    const int lane = threadIdx.x & 31;
+    if (n <= 32) warp_topk_sorted<1>(cv, n, k, vals);
+    else if (n <= 64) warp_topk_sorted<2>(cv, n, k, vals);
+    else warp_topk_sorted<4>(cv, n, k, vals);
     const float thr = warp_topp(vals, k, hf, lse, top_p, min_keep, topk_only);
-    thr_out = thr;
     int kn = 0;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        if (t < nt) {
-            const int i = lane + 32 * t;
-            const int id = i < n ? ci[i] : -1;
-            const bool keep = i < n && x[t] >= thr && id != drop_id;
-            const unsigned m = __ballot_sync(0xffffffffu, keep);
-            const int pos = kn + __popc(m & ((1u << lane) - 1u));
-            if (keep) {
-                sv[pos] = x[t];
-                si[pos] = id;
-            }
-            kn += __popc(m);
+    for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        const float v = i < n ? cv[i] : 0.0f;
+        const int id = i < n ? ci[i] : 0;
+        const bool keep = i < n && v >= thr && id != drop_id;
+        const unsigned m = __ballot_sync(0xffffffffu, keep);
+        const int pos = kn + __popc(m & ((1u << lane) - 1u));
+        if (keep) {
+            sv[pos] = v;
+            si[pos] = id;
         }
+        kn += __popc(m);
     }
     __syncwarp();
     return kn <= 32 ? warp_draw32(sv[lane < kn ? lane : 0], kn, u) : warp_draw_sorted(sv, kn, u);

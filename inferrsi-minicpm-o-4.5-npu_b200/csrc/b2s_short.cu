@@ -21,8 +21,9 @@
 //   one pass: the elements >= tau go into the candidate list in vocabulary order (a block scan of the
 //             per-slot counts gives each thread its positions).
 //
-// Then the list stage of b2s_list.cuh in one warp (the list being in vocabulary order, up to 128 candidates need
-// no block barrier) and the state epilogue.  A row the list cannot serve (NaN, an unusable tau, more candidates
+// Then the list stage of b2s_list.cuh in one warp -- a bitonic sort of up to 128 candidate values, the top-p
+// cut, and the draw over the kept items, which the list already holds in vocabulary order -- and the state
+// epilogue.  A row the list cannot serve (NaN, an unusable tau, more candidates
 // than the list holds) builds the history structures and takes the exact full-row path; hf frame-0 rows take
 // the ordered scan: both shared with the row-resident kernel (b2s_rowpaths.cuh) and out of line.  The kernel
 // waits on nothing but its own loads and block barriers.
@@ -385,7 +386,17 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     const int drop = (hf && masked_eos) ? p.eos : -1;
     const bool topk_only = (p.flags & B2S_FLAG_TOPK_ONLY) != 0;
     if (mode == MODE_FILTER) {
-        if (!ovf && n <= 2 * KLIST) {
+        if (!ovf && n <= KLIST) {
+            // one warp: sorted top-k values, top-p cut, kept items in vocabulary order, draw
+            if (warp == 0) {
+                const int pos = warp_list_sorted(cand_v, cand_i, n, k, hf, lse, top_p, p.min_keep, topk_only, drop,
+                                                 ctl->u, vals, sv, si);
+                if (lane == 0) ctl->kn = pos;
+            }
+            __syncthreads();
+            const int pos = ctl->kn;
+            token = pos == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)si[pos];
+        } else if (!ovf && n <= 2 * KLIST) {
             const Scr sc{hist, ctl->rctl, &ctl->gather_n, &ctl->kn, &ctl->thr, ctl->red_d, ctl->red_f, ctl->red_i};
             float thr;
             token = list_sample(cand_v, cand_i, n, k, hf, lse, top_p, p.min_keep, topk_only, true, drop, ctl->u, V, vals,
