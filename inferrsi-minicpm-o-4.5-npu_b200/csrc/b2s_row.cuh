@@ -78,7 +78,7 @@ struct Params {
     // the row slice live, and the slice capacity in 16-byte vectors
     int cl, ltot, slice_vecs;
     uint32_t off_bar, off_slice;
-    // short-row kernel (b2s_short.cu): one flag byte per element (in the history), 4 per word
+    // short-row kernel (b2s_short.cu): one occurrence-count byte per element, 4 per word
     uint32_t off_cnt, cnt_words;
     // several frames in one launch (b2s_sample_frames): logits of frame f start f * fstride elements after frame 0's;
     // tokens and uniform values are [frames, rows]; the state advances in place from frame to frame

@@ -1114,7 +1114,7 @@ static bool short_layout(b2s::Params& p, const b2s_sample_args* a, int es, int k
     p.lcap = lcap;
     p.ltot = lcap;
     p.csplit = 0;
-    p.cnt_words = (uint32_t)((a->vocab + 16 + 15) / 16 * 4);  // flag bytes: id - e0 + EPV < vocab + 16, whole 16-byte groups
+    p.cnt_words = (uint32_t)((a->vocab + 16 + 15) / 16 * 4);  // count bytes: id - e0 + EPV < vocab + 16, whole 16-byte groups
     uint32_t off = 0;
     p.off_ctl = off;
     off = align_up(off + (uint32_t)sizeof(Ctl), 128);
@@ -1132,7 +1132,7 @@ static bool short_layout(b2s::Params& p, const b2s_sample_args* a, int es, int k
     off = align_up(off + (uint32_t)p.hcap * 4, 16);
     p.off_htv = off;
     off = align_up(off + (uint32_t)p.hcap * 4, 16);
-    p.off_hraw = off;  // the history ids' processed values, indexed like the flag bytes
+    p.off_hraw = off;  // the history ids' processed values, indexed like the count bytes
     off = align_up(off + p.cnt_words * 16, 16);
     p.off_hstage = off;
     off = align_up(off + (uint32_t)a->window * 8, 16);

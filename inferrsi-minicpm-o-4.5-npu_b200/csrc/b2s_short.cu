@@ -6,13 +6,14 @@
 //
 //   loads:    every thread requests its interior vectors (tid, tid + NT, ...: the thread layout of the other
 //             row kernels, so the same fp64 partial sums) into registers; threads 0 / 1 the head / tail
-//             elements outside the 16-byte interior, as one more vector (slot); thread j < W its history id
-//             and, once that has landed, the id's raw value.
-//   history:  thread j counts its id's occurrences in the staged window, takes the id's processed value and
-//             writes it, with a flag byte, into tables indexed like the row (byte id - e0 + EPV), so that one
-//             aligned shared word holds the flags of a vector.  No bitmap, no ranks, no atomics.
-//   values:   each thread turns its elements into processed values in registers, taking a flagged element's
-//             value from the table, and keeps its maximum.
+//             elements outside the 16-byte interior, as one more vector (slot); thread j < W its history id;
+//             the penalty table goes to shared memory by asynchronous copies.
+//   history:  as soon as its id lands, thread j adds one to the id's byte in a packed count array (zeroed
+//             while the previous kernel still ran) and requests the id's raw value; once the counts are
+//             complete it writes the id's processed value into a table indexed like the counts (byte
+//             id - e0 + EPV, so that one aligned shared word holds the counts of a vector).  No bitmap, no ranks.
+//   values:   meanwhile every thread divides its elements by T in registers; then an element with a non-zero
+//             count takes its value from the table, and each thread keeps its maximum.
 //   tau:      the k-th largest of the warps' ceil(k/16) largest thread maxima, ranked by all threads at once;
 //             each maximum is a distinct element, so tau bounds the row's k-th largest processed value from
 //             below, exactly (the comparison is on processed values: no rounding margin).
@@ -33,19 +34,17 @@
 
 namespace b2s {
 
-// Processed values of one vector's elements (ids e .. e + EPV - 1; past `valid`, -inf).  fw: their flag bytes
-// (an element with a history id takes its value from hval[c + j], c the table index of element e); cens: the
-// censored EOS (omni), -inf whatever its history.
+// The flagged elements of one vector (ids e .. e + EPV - 1, the first `valid` real): an element whose count byte
+// in cw is non-zero takes its processed value from hval[c + j] (c: the table index of element e); the censored
+// EOS (omni) is -inf whatever its history.  Then the thread's maximum.
 template <typename E>
-__device__ __forceinline__ void short_values(const Row<E>& R, const float* hval, int cens, uint4 q, uint64_t fw, int e,
-                                             int c, int valid, float* out, float& tmax) {
+__device__ __forceinline__ void short_patch(const float* hval, int cens, uint64_t cw, int e, int c, int valid,
+                                            float* out, float& tmax) {
     constexpr int EPV = Elem<E>::EPV;
-#pragma unroll
-    for (int j = 0; j < EPV; ++j) out[j] = j < valid ? R.f(Elem<E>::at(q, j)) : f_ninf();
-    if (fw != 0u) {
+    if (cw != 0u) {
 #pragma unroll
         for (int j = 0; j < EPV; ++j)
-            if ((fw >> (8 * j)) & 255u) out[j] = hval[c + j];
+            if ((cw >> (8 * j)) & 255u) out[j] = hval[c + j];
     }
     if ((unsigned)(cens - e) < (unsigned)valid) {
 #pragma unroll
@@ -57,7 +56,7 @@ __device__ __forceinline__ void short_values(const Row<E>& R, const float* hval,
 }
 
 // The exact full-row path of a short row: the whole-row history structures first (the register pass keeps
-// only flags), then the radix select, threshold and ordered draw that every row kernel falls back on.
+// only counts), then the radix select, threshold and ordered draw that every row kernel falls back on.
 template <typename E>
 static __device__ __noinline__ int64_t short_exact(const Params p, Row<E> R, HistBufs hb, int k, bool hf, float lse,
                                                    float top_p, bool topk_only, int drop, bool pen_hist, bool censor,
@@ -78,8 +77,8 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r = (int)blockIdx.x;
     Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
-    uint32_t* flags = reinterpret_cast<uint32_t*>(smem + p.off_cnt);  // byte id - e0 + EPV: id is in the history
-    float* hval = reinterpret_cast<float*>(smem + p.off_hraw);        // [id - e0 + EPV]: its processed value
+    uint32_t* cnts = reinterpret_cast<uint32_t*>(smem + p.off_cnt);  // byte id - e0 + EPV: the id's occurrences
+    float* hval = reinterpret_cast<float*>(smem + p.off_hraw);       // [id - e0 + EPV]: its processed value
     HistBufs hb;
     hb.bits = reinterpret_cast<uint32_t*>(smem + p.off_bits);
     hb.pref = reinterpret_cast<uint16_t*>(smem + p.off_pref);
@@ -100,14 +99,14 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     float* vals = reinterpret_cast<float*>(smem + p.off_vals);
     uint32_t* hist = reinterpret_cast<uint32_t*>(smem + p.off_hist);
     const int V = p.V;
+    // before the wait for the previous kernel (nothing global is read): the count bytes zeroed, tau's slot
+    if (p.hist && p.W > 0)
+        for (uint32_t g = tid; g < p.cnt_words / 4; g += NT) reinterpret_cast<uint4*>(cnts)[g] = make_uint4(0u, 0u, 0u, 0u);
+    if (tid == 0) ctl->thr = f_ninf();  // tau, until a rank finds it
+    __syncthreads();
     pdl_wait_then_release();  // nothing global is read before the previous kernel of the stream is done
 
     // ---------------- loads: this thread's row elements and history id (registers), the penalty table
-    const int64_t* hrow = p.hist ? p.hist + (int64_t)r * p.hstride : nullptr;
-    const bool hthread = hrow != nullptr && tid < p.W;  // W <= 255 < NT: one history position per thread
-    const int64_t hv = hthread ? hrow[tid] : -1;
-    if (hrow && p.W > 0 && p.alpha)
-        for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], p.alpha + (int64_t)r * p.alpha_stride + j);
     Row<E> R;
     R.rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
     R.V = V;
@@ -126,31 +125,23 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
         const int v = tid + s * NT;
         q[s] = v < R.nvec ? ldg_stream(R.gvec + v) : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
     }
+    const int64_t* hrow = p.hist ? p.hist + (int64_t)r * p.hstride : nullptr;
+    const bool hthread = hrow != nullptr && tid < p.W;  // W <= 255 < NT: one history position per thread
+    const int64_t hv = hthread ? hrow[tid] : -1;
+    if (hrow && p.W > 0 && p.alpha)
+        for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], p.alpha + (int64_t)r * p.alpha_stride + j);
     const int i_end = R.e0 + R.nvec * EPV;
     const int x0 = tid == 0 ? 0 : i_end;                       // first element of the edge slot
     const int nx = tid == 0 ? R.nh : tid == 1 ? V - i_end : 0;  // < EPV
-    {
-        uint32_t w[4] = {Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG};
+    uint32_t ex[EPV - 1];  // the edge elements' bits, packed into q[SV] once they are needed
 #pragma unroll
-        for (int j = 0; j < EPV - 1; ++j) {
-            if (j < nx) {
-                const uint32_t b = __float_as_uint(Elem<E>::gld(R.rowp, x0 + j));
-                if constexpr (ES == 4) {
-                    w[j] = b;
-                } else {  // element j is the low (even j) or high (odd j) half of word j / 2
-                    w[j >> 1] = (j & 1) ? ((w[j >> 1] & 0x0000ffffu) | (b & 0xffff0000u)) : ((w[j >> 1] & 0xffff0000u) | (b >> 16));
-                }
-            }
-        }
-        q[SV] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
+    for (int j = 0; j < EPV - 1; ++j) ex[j] = j < nx ? __float_as_uint(Elem<E>::gld(R.rowp, x0 + j)) : 0u;
     const int64_t step = p.steps ? p.steps[r] : 0;
     const bool is_live = (p.active ? p.active[r] != 0 : true) && !(p.finished ? p.finished[r] != 0 : false);
     const float T = p.rT ? p.rT[r] : p.T;
     const float top_p = p.rP ? p.rP[r] : p.top_p;
     const int top_k = p.rK ? p.rK[r] : p.top_k;
     const int64_t min_new = p.rminn ? p.rminn[r] : p.min_new, max_new = p.rmaxn ? p.rmaxn[r] : p.max_new;
-    if (tid == 0) ctl->thr = f_ninf();  // tau, until a rank finds it
 
     // ---------------- mode
     const bool hf = SEM >= 0 ? SEM == B2S_SEM_HF : p.sem == B2S_SEM_HF;
@@ -176,62 +167,79 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     }
     R.T = T;
     R.identity = false;
-    R.bits = nullptr;  // the register pass keeps flags; the full-row paths build their own structures
+    R.bits = nullptr;  // the register pass keeps counts; the full-row paths build their own structures
     R.pref = nullptr;
     R.htv = nullptr;
     R.censor = -1;
     const bool pen_hist = mode == MODE_FILTER && p.W > 0 && hrow != nullptr;
     const bool censor = mode == MODE_FILTER && !hf && masked_eos;  // omni: EOS is -inf before anything else
     const int cens = censor ? p.eos : -1;
-    if (pen_hist)
-        for (uint32_t g = tid; g < p.cnt_words / 4; g += NT) reinterpret_cast<uint4*>(flags)[g] = make_uint4(0u, 0u, 0u, 0u);
-    // the history id's raw value, requested as soon as the id has landed
+
+    // ---------------- history: each position counts its id (one shared atomic) and requests the id's raw value
     const bool hvalid = pen_hist && hthread && hv >= 0 && hv < V;
+    const int hc = (int)hv - R.e0 + EPV;  // the id's byte in the count array and its slot in hval
     float hx = 0.0f;
-    if (hvalid) hx = Elem<E>::gld(R.rowp, hv);
-    if (hthread) hstage[tid] = hv;
-    cp_async_wait_all();
-    __syncthreads();  // the window and the penalty table are staged; the flags are zero
-
-    // ---------------- history: occurrences, processed value, flag
-    if (pen_hist && hthread) {
-        if (hv >= V) set_status(p, B2S_STATUS_HISTORY_RANGE);
-        if (hvalid) {
-            int n = (p.W & 1) ? (int)(hstage[p.W - 1] == hv) : 0;
-            const longlong2* h2 = reinterpret_cast<const longlong2*>(hstage);
-#pragma unroll 4
-            for (int j = 0; j < (p.W >> 1); ++j) {
-                const longlong2 q2 = h2[j];
-                n += (q2.x == hv) + (q2.y == hv);
-            }
-            const float v = hv == cens ? f_ninf() : hist_proc_value(p, atab, hf, false, T, n, hx);
-            const int c = (int)hv - R.e0 + EPV;
-            hval[c] = v;  // every position of the id writes the same value
-            reinterpret_cast<uint8_t*>(flags)[c] = 1u;
-        }
+    if (hthread) {
+        hstage[tid] = hv;
+        if (pen_hist && hv >= V) set_status(p, B2S_STATUS_HISTORY_RANGE);
     }
-    __syncthreads();  // the history's values and flags are complete
+    if (hvalid) {
+        atomicAdd(&cnts[hc >> 2], 1u << ((hc & 3) * 8));
+        hx = Elem<E>::gld(R.rowp, hv);
+    }
+    cp_async_wait_all();
+    __syncthreads();  // the counts are complete; the window and the penalty table are staged
 
-    // ---------------- processed values and the thread's maximum
+    // ---------------- processed values: the history ids' into hval (history threads), x / T into registers (all)
+    if (hvalid)  // every position of the id writes the same value
+        hval[hc] = hv == cens ? f_ninf()
+                              : hist_proc_value(p, atab, hf, false, T,
+                                                (int)((cnts[hc >> 2] >> ((hc & 3) * 8)) & 255u), hx);
+    if (nx > 0) {
+        uint32_t w[4] = {Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG};
+#pragma unroll
+        for (int j = 0; j < EPV - 1; ++j) {
+            if (j < nx) {
+                if constexpr (ES == 4) {
+                    w[j] = ex[j];
+                } else {  // element j is the low (even j) or high (odd j) half of word j / 2
+                    w[j >> 1] = (j & 1) ? ((w[j >> 1] & 0x0000ffffu) | (ex[j] & 0xffff0000u))
+                                        : ((w[j >> 1] & 0xffff0000u) | (ex[j] >> 16));
+                }
+            }
+        }
+        q[SV] = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+        q[SV] = make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
+    }
     float P[(SV + 1) * EPV];
+#pragma unroll
+    for (int s = 0; s <= SV; ++s) {
+        const int valid = s < SV ? (tid + s * NT < R.nvec ? EPV : 0) : nx;
+#pragma unroll
+        for (int j = 0; j < EPV; ++j) P[s * EPV + j] = j < valid ? R.f(Elem<E>::at(q[s], j)) : f_ninf();
+    }
+    __syncthreads();  // the history ids' values are in hval
+
+    // ---------------- the flagged elements patched from hval; the thread's maximum
     float tmax = f_ninf();
-    auto flags_at = [&](int b) -> uint64_t {  // the EPV flag bytes from byte b (a multiple of EPV)
+    auto counts_at = [&](int b) -> uint64_t {  // the EPV count bytes from byte b (a multiple of EPV)
         if (!pen_hist) return 0u;
-        if constexpr (EPV == 4) return (uint64_t)flags[b >> 2];
-        else return reinterpret_cast<const uint64_t*>(flags)[b >> 3];
+        if constexpr (EPV == 4) return (uint64_t)cnts[b >> 2];
+        else return reinterpret_cast<const uint64_t*>(cnts)[b >> 3];
     };
 #pragma unroll
     for (int s = 0; s < SV; ++s) {
         const int v = tid + s * NT;
         const int valid = v < R.nvec ? EPV : 0;
-        const uint64_t fw = valid ? flags_at((v + 1) * EPV) : 0u;
-        short_values<E>(R, hval, cens, q[s], fw, R.e0 + v * EPV, (v + 1) * EPV, valid, &P[s * EPV], tmax);
+        const uint64_t cw = valid ? counts_at((v + 1) * EPV) : 0u;
+        short_patch<E>(hval, cens, cw, R.e0 + v * EPV, (v + 1) * EPV, valid, &P[s * EPV], tmax);
     }
     {
-        // the head's flags end at byte EPV, the tail's start at the vector boundary after the interior
-        uint64_t fw = 0u;
-        if (nx > 0) fw = tid == 0 ? flags_at(0) >> (8 * (EPV - R.nh)) : flags_at((R.nvec + 1) * EPV);
-        short_values<E>(R, hval, cens, q[SV], fw, x0, x0 - R.e0 + EPV, nx, &P[SV * EPV], tmax);
+        // the head's counts end at byte EPV, the tail's start at the vector boundary after the interior
+        uint64_t cw = 0u;
+        if (nx > 0) cw = tid == 0 ? counts_at(0) >> (8 * (EPV - R.nh)) : counts_at((R.nvec + 1) * EPV);
+        short_patch<E>(hval, cens, cw, x0, x0 - R.e0 + EPV, nx, &P[SV * EPV], tmax);
     }
 
     // ---------------- tau: the k-th largest of the warps' jw largest thread maxima; the row's maximum
