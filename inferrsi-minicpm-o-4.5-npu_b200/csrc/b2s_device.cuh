@@ -43,10 +43,12 @@ __device__ __forceinline__ float b2s_expf(float x) {
     return x != x ? x : res;
 }
 
-// b2s_expf of two non-positive (or NaN) arguments at once: the same rounded operations, the range reduction and
-// the polynomial in packed fp32x2 arithmetic (each lane one IEEE rn operation, so the same bits as the scalar
-// form).  For x <= 0 the overflow side of b2s_expf (its upper clamp, the scale-down by two and the +inf case)
-// never applies and is left out; every other step is kept.
+// b2s_expf of two arguments x <= 0 (not NaN) at once, with the same results: the range reduction and the
+// polynomial in packed fp32x2 arithmetic (each lane one IEEE rn operation).  The scaling by 2^n is taken as
+// (p * 2^(n + 64)) * 2^-64: the first product is exact (a normal power-of-two scaling), so the result is p * 2^n
+// rounded once, as the scalar form's single or two-step scaling gives it.  (n stays rintf of the rounded product
+// t: an add of a rounding constant to t could be fused with the multiply that made t, rounding it differently.)
+// For x <= 0 the overflow side of b2s_expf never applies and is left out.
 __device__ __forceinline__ float2 b2s_expf2_nonpos(float2 x) {
     const float2 xc = make_float2(fmaxf(x.x, -104.0f), fmaxf(x.y, -104.0f));
     const float2 t = __fmul2_rn(xc, make_float2(1.44269502162933349609375f, 1.44269502162933349609375f));
@@ -61,17 +63,14 @@ __device__ __forceinline__ float2 b2s_expf2_nonpos(float2 x) {
     p = __ffma2_rn(p, r, make_float2(0.5f, 0.5f));
     p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
     p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
-    int n0 = (int)n.x, n1 = (int)n.y;  // [-150, 0]
-    const bool lo0 = n0 < -126, lo1 = n1 < -126;
-    const float2 pl = __fmul2_rn(p, make_float2(5.42101086242752217003726400434970855712890625e-20f,
-                                                5.42101086242752217003726400434970855712890625e-20f));
-    p = make_float2(lo0 ? pl.x : p.x, lo1 ? pl.y : p.y);
-    n0 = lo0 ? n0 + 64 : n0;
-    n1 = lo1 ? n1 + 64 : n1;
-    float2 res = __fmul2_rn(p, make_float2(__uint_as_float((uint32_t)(n0 + 127) << 23), __uint_as_float((uint32_t)(n1 + 127) << 23)));
+    // n + 64 + 127 in the exponent field: n in [-150, 0], so a normal power of two
+    const float2 s = make_float2(__uint_as_float((uint32_t)((int)n.x + 191) << 23),
+                                 __uint_as_float((uint32_t)((int)n.y + 191) << 23));
+    float2 res = __fmul2_rn(__fmul2_rn(p, s), make_float2(5.42101086242752217003726400434970855712890625e-20f,
+                                                          5.42101086242752217003726400434970855712890625e-20f));
     res.x = x.x < -103.97208404541015625f ? 0.0f : res.x;
     res.y = x.y < -103.97208404541015625f ? 0.0f : res.y;
-    return make_float2(x.x != x.x ? x.x : res.x, x.y != x.y ? x.y : res.y);
+    return res;
 }
 
 __device__ __forceinline__ float f_inf() { return __int_as_float(0x7f800000); }

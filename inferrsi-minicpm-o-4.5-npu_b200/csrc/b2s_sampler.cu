@@ -948,14 +948,14 @@ __global__ void __launch_bounds__(NT) penalty_kernel(const void* x, int rows, in
 }
 
 // The numerics spec's exp on the device: y[i] = b2s_expf(x[i]); y2[i] = the paired non-positive form where
-// x[i] <= 0 or NaN (pairs (2j, 2j+1) when both qualify, else the scalar form).
+// x[i] <= 0 (pairs (2j, 2j+1) when both qualify, else the scalar form).
 __global__ void expf_spec_kernel(const float* x, int64_t n, float* y, float* y2) {
     for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; 2 * j < n; j += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = 2 * j;
         const float a = x[i], b = i + 1 < n ? x[i + 1] : 0.0f;
         y[i] = b2s_expf(a);
         if (i + 1 < n) y[i + 1] = b2s_expf(b);
-        const bool pa = !(a > 0.0f), pb = !(b > 0.0f);
+        const bool pa = a <= 0.0f, pb = b <= 0.0f;
         if (pa && pb) {
             const float2 e = b2s_expf2_nonpos(make_float2(a, b));
             y2[i] = e.x;

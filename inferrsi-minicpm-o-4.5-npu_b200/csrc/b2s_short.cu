@@ -273,11 +273,12 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     const float m = okey_to_f(mkey);  // the row's largest processed value (NaN aside)
     // hf's full-row normaliser: the fp64 sum of exp(P - max) in the other row kernels' order (vectors, then the
     // edges; warp butterflies, then the warps in order), the warps' sums handed over at the next barrier
-    // (a row whose maximum is +inf sums to +inf, or NaN with a NaN in it: taken without the exponentials; every
-    // other row's arguments P - max are <= 0 or NaN, the paired form's domain)
+    // (a row with a NaN sums to NaN, one whose maximum is +inf to +inf: taken without the exponentials; every
+    // other row's arguments P - max are <= 0, the paired form's domain)
     const bool want_lse = mode == MODE_FILTER && hf;
     const float mu = (m == f_inf() || m == f_ninf()) ? 0.0f : m;
-    if (want_lse && m != f_inf()) {
+    const bool lse_sum = want_lse && !has_nan && m != f_inf();
+    if (lse_sum) {
         double sacc = 0.0;
         const float2 nmu = make_float2(-mu, -mu);
 #pragma unroll
@@ -318,7 +319,7 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     const float tau = ctl->thr;
     bool ovf = !cand_path || has_nan || !(tau > f_ninf()) || tau == f_inf();
     float lse = 0.0f;
-    if (want_lse && m != f_inf()) {
+    if (lse_sum) {
         double sum = 0.0;
 #pragma unroll
         for (int w = 0; w < NWARP; ++w) sum += ctl->red_d[w];
