@@ -215,6 +215,15 @@ __device__ __forceinline__ void cluster_arrive_release() {
 }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
+// Named barrier `id` (1..15) of `count` threads (a multiple of 32): sync waits for all of them, arrive only counts
+// this warp in.  Both order this thread's earlier memory accesses before the barrier for the others.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Programmatic dependent launch: a kernel launched with programmatic stream serialisation may start
 // while the previous kernel of the stream is still running.  It first waits for that kernel's completion
 // (and the visibility of its writes), then lets the next kernel of the stream start early in turn.  Without

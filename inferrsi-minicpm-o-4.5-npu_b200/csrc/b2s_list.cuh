@@ -387,17 +387,21 @@ __device__ __forceinline__ void warp_topk_sorted(const float* cv, int n, int k, 
     __syncwarp();
 }
 
-// One warp (no block barrier): the whole list stage for n <= 128 NaN-free items already in vocabulary order,
-// n >= k.  The sorted top-k values (warp_topk_sorted), warp_topp, the kept items (value >= threshold, id !=
-// drop_id) compacted by ballot into sv / si in list order -- vocabulary order --, and the draw (warp_draw32 /
-// warp_draw_sorted, as list_sample).  Returns the position drawn in si in every lane, or 0x7fffffff.
-__device__ __forceinline__ int warp_list_sorted(const float* cv, const int* ci, int n, int k, bool hf, float lse,
-                                                float top_p, int min_keep, bool topk_only, int drop_id, float u,
-                                                float* vals, float* sv, int* si) {
-    const int lane = threadIdx.x & 31;
+// The sorted top-k values of cv[0..n) (n <= 128, NaN-free) into vals[0..k), by one warp.
+__device__ __forceinline__ void warp_topk_sorted_n(const float* cv, int n, int k, float* vals) {
     if (n <= 32) warp_topk_sorted<1>(cv, n, k, vals);
     else if (n <= 64) warp_topk_sorted<2>(cv, n, k, vals);
     else warp_topk_sorted<4>(cv, n, k, vals);
+}
+
+// One warp (no block barrier), after warp_topk_sorted_n: the rest of the list stage for n <= 128 items already in
+// vocabulary order, n >= k -- warp_topp, the kept items (value >= threshold, id != drop_id) compacted by ballot
+// into sv / si in list order, which is vocabulary order, and the draw (warp_draw32 / warp_draw_sorted, as
+// list_sample).  Returns the position drawn in si in every lane, or 0x7fffffff.
+__device__ __forceinline__ int warp_list_kept_draw(const float* cv, const int* ci, int n, int k, bool hf, float lse,
+                                                   float top_p, int min_keep, bool topk_only, int drop_id, float u,
+                                                   const float* vals, float* sv, int* si) {
+    const int lane = threadIdx.x & 31;
     const float thr = warp_topp(vals, k, hf, lse, top_p, min_keep, topk_only);
     int kn = 0;
     for (int i0 = 0; i0 < n; i0 += 32) {

@@ -101,6 +101,7 @@ struct Ctl {
     int rx_n[8];  // row-resident kernel: candidates each other CTA of the cluster handed over (-1: incomplete)
     int lovf;     // row-resident kernel: a CTA's candidates are incomplete or did not fit rank 0's list
     float rx_tau[8];  // row-resident kernel: each CTA's tau (every one bounds the row's k-th value from below)
+    float lse;        // short-row kernel: the normaliser, handed from warp 1 to warp 0
 };
 
 template <typename E>

@@ -318,15 +318,15 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     __syncthreads();
     const float tau = ctl->thr;
     bool ovf = !cand_path || has_nan || !(tau > f_ninf()) || tau == f_inf();
-    float lse = 0.0f;
-    if (lse_sum) {
+    // the normaliser from the warps' sums, in order (taken where it is needed: warp 1 during the list stage, every
+    // thread before the full-row paths)
+    auto finish_lse = [&]() -> float {
+        if (!lse_sum) return want_lse ? (has_nan ? __int_as_float(0x7fffffff) : f_inf()) : 0.0f;
         double sum = 0.0;
 #pragma unroll
         for (int w = 0; w < NWARP; ++w) sum += ctl->red_d[w];
-        lse = __fadd_rn((float)log((double)(float)sum), mu);
-    } else if (want_lse) {
-        lse = has_nan ? __int_as_float(0x7fffffff) : f_inf();
-    }
+        return __fadd_rn((float)log((double)(float)sum), mu);
+    };
 
     // ---------------- one pass over the registers: the candidates in vocabulary order, and hf's normaliser sum
     int n = 0;
@@ -374,6 +374,7 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
         n = base + edge_n[1];
 #pragma unroll
         for (int s = 0; s <= SV; ++s) {
+            if (cs[s] == 0) continue;  // most slots hold no candidate
             int pos = off[s];
 #pragma unroll
             for (int j = 0; j < EPV; ++j) {
@@ -394,26 +395,40 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     int64_t token = V - 1;
     const int drop = (hf && masked_eos) ? p.eos : -1;
     const bool topk_only = (p.flags & B2S_FLAG_TOPK_ONLY) != 0;
+    float lse = 0.0f;
     if (mode == MODE_FILTER) {
         if (!ovf && n <= KLIST) {
-            // one warp: sorted top-k values, top-p cut, kept items in vocabulary order, draw
+            // warp 0: sorted top-k values, top-p cut, kept items in vocabulary order, draw; warp 1 meanwhile takes
+            // the normaliser and hands it over at a barrier of the two warps (id 1)
             if (warp == 0) {
-                const int pos = warp_list_sorted(cand_v, cand_i, n, k, hf, lse, top_p, p.min_keep, topk_only, drop,
-                                                 ctl->u, vals, sv, si);
+                warp_topk_sorted_n(cand_v, n, k, vals);
+                if (want_lse) {
+                    named_bar_sync(1, 64);
+                    lse = ctl->lse;
+                }
+                const int pos = warp_list_kept_draw(cand_v, cand_i, n, k, hf, lse, top_p, p.min_keep, topk_only, drop,
+                                                    ctl->u, vals, sv, si);
                 if (lane == 0) ctl->kn = pos;
+            } else if (warp == 1 && want_lse) {
+                const float l = finish_lse();
+                if (lane == 0) ctl->lse = l;
+                named_bar_arrive(1, 64);
             }
             __syncthreads();
             const int pos = ctl->kn;
             token = pos == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)si[pos];
         } else if (!ovf && n <= 2 * KLIST) {
+            lse = finish_lse();
             const Scr sc{hist, ctl->rctl, &ctl->gather_n, &ctl->kn, &ctl->thr, ctl->red_d, ctl->red_f, ctl->red_i};
             float thr;
             token = list_sample(cand_v, cand_i, n, k, hf, lse, top_p, p.min_keep, topk_only, true, drop, ctl->u, V, vals,
                                 kv, ki, sv, si, sc, thr, true);
         } else if (!ovf) {
+            lse = finish_lse();
             token = block_list_token(cand_v, cand_i, kv, ki, sv, si, n, k, hf, lse, top_p, p.min_keep, topk_only, drop,
                                      ctl->u, V, vals, hist, ctl);
         } else {
+            lse = finish_lse();
             token = short_exact<E>(p, R, hb, k, hf, lse, top_p, topk_only, drop, pen_hist, censor, T, ctl->u, hist,
                                    vals, ctl);
         }
