@@ -101,7 +101,8 @@ struct Ctl {
     int rx_n[8];  // row-resident kernel: candidates each other CTA of the cluster handed over (-1: incomplete)
     int lovf;     // row-resident kernel: a CTA's candidates are incomplete or did not fit rank 0's list
     float rx_tau[8];  // row-resident kernel: each CTA's tau (every one bounds the row's k-th value from below)
-    float lse;        // short-row kernel: the normaliser, handed from warp 1 to warp 0
+    float lse;        // short-row kernel: the normaliser, handed from warp 4 to warp 0
+    int sr_state, sr_n;  // short-row kernel: how the row's token is taken, and the candidates in the list
 };
 
 template <typename E>

@@ -14,13 +14,13 @@
 //             id - e0 + EPV, so that one aligned shared word holds the counts of a vector).  No bitmap, no ranks.
 //   values:   meanwhile every thread divides its elements by T in registers; then an element with a non-zero
 //             count takes its value from the table, and each thread keeps its maximum.
-//   tau:      the k-th largest of the warps' ceil(k/16) largest thread maxima, ranked by all threads at once;
-//             each maximum is a distinct element, so tau bounds the row's k-th largest processed value from
-//             below, exactly (the comparison is on processed values: no rounding margin).
-//   lse:      (hf) the fp64 sum of exp(P - max) for the full-row normaliser (talker_sampler.py:112), as soon
-//             as the row's maximum is known, beside the ranking of tau.
-//   one pass: the elements >= tau go into the candidate list in vocabulary order (a block scan of the
-//             per-slot counts gives each thread its positions).
+//   gather:   the processed row goes to shared memory; each warp gathers its ceil(k/16) largest thread maxima
+//             (each a distinct element) and its maximum.
+//   split:    warps 0..3 take tau -- the k-th largest of the gathered maxima, so a lower bound of the row's
+//             k-th largest processed value, exactly (the comparison is on processed values: no rounding
+//             margin) -- and put every element >= tau into the candidate list in vocabulary order (two passes
+//             over contiguous runs of the row in shared memory, one scan); meanwhile warps 4..15 take the fp64
+//             sum of exp(P - max) for hf's full-row normaliser (talker_sampler.py:112).
 //
 // Then the list stage of b2s_list.cuh in one warp -- a bitonic sort of up to 128 candidate values, the top-p
 // cut, and the draw over the kept items, which the list already holds in vocabulary order -- and the state
@@ -241,6 +241,24 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
         if (nx > 0) cw = tid == 0 ? counts_at(0) >> (8 * (EPV - R.nh)) : counts_at((R.nvec + 1) * EPV);
         short_patch<E>(hval, cens, cw, x0, x0 - R.e0 + EPV, nx, &P[SV * EPV], tmax);
     }
+    // the processed row into shared memory (over hval, indexed alike: each slot is read and rewritten by its owner
+    // only): element id at hval[id + EPV - nh], where the candidates and the normaliser's exponentials are taken
+    const bool want_lse = mode == MODE_FILTER && hf;
+    if (mode == MODE_FILTER) {
+#pragma unroll
+        for (int s = 0; s < SV; ++s) {
+            const int v = tid + s * NT;
+            if (v < R.nvec) {
+                float4* d = reinterpret_cast<float4*>(hval + (v + 1) * EPV);
+#pragma unroll
+                for (int j = 0; j < EPV; j += 4)
+                    d[j / 4] = make_float4(P[s * EPV + j], P[s * EPV + j + 1], P[s * EPV + j + 2], P[s * EPV + j + 3]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < EPV - 1; ++j)
+            if (j < nx) hval[x0 - R.e0 + EPV + j] = P[SV * EPV + j];
+    }
 
     // ---------------- tau: the k-th largest of the warps' jw largest thread maxima; the row's maximum
     const bool cand_path = mode == MODE_FILTER && k <= KFAST && !(p.flags & B2S_FLAG_FORCE_GENERAL) && T >= 1e-6f &&
@@ -271,167 +289,190 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
 #pragma unroll
     for (int w = 1; w < NWARP; ++w) mkey = max(mkey, ctl->red_u[w]);
     const float m = okey_to_f(mkey);  // the row's largest processed value (NaN aside)
-    // hf's full-row normaliser: the fp64 sum of exp(P - max) in the other row kernels' order (vectors, then the
-    // edges; warp butterflies, then the warps in order), the warps' sums handed over at the next barrier
-    // (a row with a NaN sums to NaN, one whose maximum is +inf to +inf: taken without the exponentials; every
-    // other row's arguments P - max are <= 0, the paired form's domain)
-    const bool want_lse = mode == MODE_FILTER && hf;
+    // hf's full-row normaliser: the fp64 sum of exp(P - max) over the row in shared memory (a row with a NaN sums
+    // to NaN, one whose maximum is +inf to +inf: taken without the exponentials; every other row's arguments
+    // P - max are <= 0, the paired form's domain)
     const float mu = (m == f_inf() || m == f_ninf()) ? 0.0f : m;
     const bool lse_sum = want_lse && !has_nan && m != f_inf();
-    if (lse_sum) {
+    // this thread's part of the normaliser's sum: the row's vectors t, t + nthr, ... (t = tid - first), then the
+    // head (t == 0) and the tail (t == 1); the warp's sum in red_d[warp]
+    auto lse_part = [&](int first, int nthr) {
+        const int t = tid - first;
         double sacc = 0.0;
         const float2 nmu = make_float2(-mu, -mu);
+        for (int v = t; v < R.nvec; v += nthr) {
+            const float4* pv = reinterpret_cast<const float4*>(hval + (v + 1) * EPV);
 #pragma unroll
-        for (int s = 0; s <= SV; ++s) {
-            const bool live = s < SV ? tid + s * NT < R.nvec : nx > 0;
-            if (live) {
-#pragma unroll
-                for (int j = 0; j < EPV; j += 2) {
-                    const float2 e = b2s_expf2_nonpos(__fadd2_rn(make_float2(P[s * EPV + j], P[s * EPV + j + 1]), nmu));
-                    if (s < SV || j < nx) sacc += (double)e.x;
-                    if (s < SV || j + 1 < nx) sacc += (double)e.y;
-                }
+            for (int j = 0; j < EPV / 4; ++j) {
+                const float4 q4 = pv[j];
+                const float2 e0 = b2s_expf2_nonpos(__fadd2_rn(make_float2(q4.x, q4.y), nmu));
+                const float2 e1 = b2s_expf2_nonpos(__fadd2_rn(make_float2(q4.z, q4.w), nmu));
+                sacc += (double)e0.x;
+                sacc += (double)e0.y;
+                sacc += (double)e1.x;
+                sacc += (double)e1.y;
             }
+        }
+        if (t < 2) {
+            const int c0 = t == 0 ? EPV - R.nh : (R.nvec + 1) * EPV, ne = t == 0 ? R.nh : V - i_end;
+            for (int j = 0; j < ne; ++j) sacc += (double)b2s_expf(__fsub_rn(hval[c0 + j], mu));
         }
         sacc = warp_sum(sacc);
         if (lane == 0) ctl->red_d[warp] = sacc;
-    }
-    if (cand_path && !has_nan) {
-        // value i of the ngp is ranked by S threads of one warp, each over L of the values
-        const int S = min(NT / ngp, ngp), L = ngp / S;
-        const int i = tid / S, sg = tid % S;
-        if (i < ngp) {
-            const float x = vals[i];
-            int gt = 0, eq = 0;
-            for (int j = sg * L; j < sg * L + L; ++j) {
-                const float y = vals[j];
-                gt += y > x;
-                eq += y == x;
-            }
-            for (int o = 1; o < S; o <<= 1) {
-                gt += __shfl_xor_sync(0xffffffffu, gt, o);
-                eq += __shfl_xor_sync(0xffffffffu, eq, o);
-            }
-            if (sg == 0 && x > f_ninf() && gt < k && k <= gt + eq) ctl->thr = x;  // ties: the same value
-        }
-    }
-    __syncthreads();
-    const float tau = ctl->thr;
-    bool ovf = !cand_path || has_nan || !(tau > f_ninf()) || tau == f_inf();
-    // the normaliser from the warps' sums, in order (taken where it is needed: warp 1 during the list stage, every
-    // thread before the full-row paths)
-    auto finish_lse = [&]() -> float {
-        if (!lse_sum) return want_lse ? (has_nan ? __int_as_float(0x7fffffff) : f_inf()) : 0.0f;
-        double sum = 0.0;
-#pragma unroll
-        for (int w = 0; w < NWARP; ++w) sum += ctl->red_d[w];
-        return __fadd_rn((float)log((double)(float)sum), mu);
     };
-
-    // ---------------- one pass over the registers: the candidates in vocabulary order, and hf's normaliser sum
-    int n = 0;
-    if (!ovf) {
-        // slots in vocabulary order: thread 0's head, interior slot 0 of every thread, ..., thread 1's tail.  The
-        // interior slots' counts are scanned packed, 16 bits per slot (a slot holds at most NT * EPV = 4096)
-        using Packed = typename std::conditional<(SV <= 2), uint32_t, uint64_t>::type;
-        int cs[SV + 1];
-        Packed c = 0;
-#pragma unroll
-        for (int s = 0; s <= SV; ++s) {
-            cs[s] = 0;
-#pragma unroll
-            for (int j = 0; j < EPV; ++j) cs[s] += P[s * EPV + j] >= tau;
-            if (s < SV) c |= (Packed)cs[s] << (16 * s);
-        }
-        Packed inc = c;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const Packed t = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += t;
-        }
-        Packed* tot = reinterpret_cast<Packed*>(hist);  // the warps' packed totals
-        int* edge_n = reinterpret_cast<int*>(hist) + 2 * NWARP * (int)(sizeof(Packed) / 4);  // head, tail counts
-        if (lane == 31) tot[warp] = inc;
-        if (tid < 2) edge_n[tid] = cs[SV];
-        __syncthreads();
-        Packed all = 0, pre = 0;
-#pragma unroll
-        for (int w = 0; w < NWARP; ++w) {
-            const Packed x = tot[w];
-            all += x;
-            pre += w < warp ? x : (Packed)0;
-        }
-        const Packed mine = pre + inc - c;  // this thread's first position within each slot, packed
-        int base = edge_n[0];
-        int off[SV + 1];
-        off[SV] = 0;  // thread 0's head
-#pragma unroll
-        for (int s = 0; s < SV; ++s) {
-            off[s] = base + (int)((mine >> (16 * s)) & 0xffffu);
-            base += (int)((all >> (16 * s)) & 0xffffu);
-        }
-        if (tid == 1) off[SV] = base;  // thread 1's tail follows the interior
-        n = base + edge_n[1];
-#pragma unroll
-        for (int s = 0; s <= SV; ++s) {
-            if (cs[s] == 0) continue;  // most slots hold no candidate
-            int pos = off[s];
-#pragma unroll
-            for (int j = 0; j < EPV; ++j) {
-                if (P[s * EPV + j] >= tau) {
-                    if (pos < p.ltot) {  // past it: the row takes the exact path
-                        cand_v[pos] = P[s * EPV + j];
-                        cand_i[pos] = s < SV ? R.e0 + (tid + s * NT) * EPV + j : x0 + j;
-                    }
-                    ++pos;
-                }
-            }
-        }
-        if (n > p.ltot || n < k) ovf = true;
-    }
-    __syncthreads();  // the candidate list is complete
+    auto lse_of = [&](double sum) { return __fadd_rn((float)log((double)(float)sum), mu); };
+    const float lse_special = has_nan ? __int_as_float(0x7fffffff) : f_inf();
 
     // ---------------- the row's token
     int64_t token = V - 1;
     const int drop = (hf && masked_eos) ? p.eos : -1;
     const bool topk_only = (p.flags & B2S_FLAG_TOPK_ONLY) != 0;
     float lse = 0.0f;
-    if (mode == MODE_FILTER) {
-        if (!ovf && n <= KLIST) {
-            // warp 0: sorted top-k values, top-p cut, kept items in vocabulary order, draw; warp 1 meanwhile takes
-            // the normaliser and hands it over at a barrier of the two warps (id 1)
+    if (mode == MODE_FILTER && cand_path && !has_nan) {
+        // Two groups of warps from here.  Warps 0..3 rank tau, put every element >= tau (from the row in shared
+        // memory) into the list in vocabulary order, and warp 0 runs the list stage; warps 4..15 meanwhile take
+        // the normaliser's sum, which warp 4 hands to warp 0.  Barriers: 1 = warps 0 and 4, 2 = warps 4..15,
+        // 3 = warps 0..3.
+        constexpr int NL = 128;  // threads of warps 0..3
+        if (warp < 4) {
+            {
+                // value i of the ngp ranked by S threads of one warp, each over L of the values
+                const int S = min(NL / ngp, ngp), L = ngp / S;
+                const int i = tid / S, sg = tid % S;
+                const float x = vals[i];
+                int gt = 0, eq = 0;
+                for (int j = sg * L; j < sg * L + L; ++j) {
+                    const float y = vals[j];
+                    gt += y > x;
+                    eq += y == x;
+                }
+                for (int o = 1; o < S; o <<= 1) {
+                    gt += __shfl_xor_sync(0xffffffffu, gt, o);
+                    eq += __shfl_xor_sync(0xffffffffu, eq, o);
+                }
+                if (sg == 0 && x > f_ninf() && gt < k && k <= gt + eq) ctl->thr = x;  // ties: the same value
+            }
+            named_bar_sync(3, NL);
+            const float tau = ctl->thr;
+            bool ok = tau > f_ninf() && tau != f_inf();
+            int n = 0;
+            if (ok) {
+                // 4-element groups covering [cb, cb + V) (element id at cb + id), in contiguous runs per thread:
+                // a count pass, a scan over the 128 threads, a write pass
+                const int cb = EPV - R.nh;
+                const int g0 = cb >> 2, g1 = (cb + V + 3) >> 2;
+                const int per = (g1 - g0 + NL - 1) / NL;
+                const int ga = g0 + tid * per, gb = min(g1, ga + per);
+                const float4* pv4 = reinterpret_cast<const float4*>(hval);
+                auto take = [&](int c, float v) { return c >= cb && c < cb + V && v >= tau; };
+                int cnt = 0;
+                for (int g = ga; g < gb; ++g) {
+                    const float4 q4 = pv4[g];
+                    const int c = 4 * g;
+                    cnt += take(c, q4.x) + take(c + 1, q4.y) + take(c + 2, q4.z) + take(c + 3, q4.w);
+                }
+                int incl = cnt;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += t;
+                }
+                int* tot = reinterpret_cast<int*>(hist);
+                if (lane == 31) tot[warp] = incl;
+                named_bar_sync(3, NL);
+                int base = 0;
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    const int x = tot[w];
+                    n += x;
+                    base += w < warp ? x : 0;
+                }
+                if (n <= p.ltot && cnt > 0) {
+                    int pos = base + incl - cnt;
+                    for (int g = ga; g < gb; ++g) {
+                        const float4 q4 = pv4[g];
+                        const float w4[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const int c = 4 * g + j;
+                            if (take(c, w4[j])) {
+                                cand_v[pos] = w4[j];
+                                cand_i[pos] = c - cb;
+                                ++pos;
+                            }
+                        }
+                    }
+                }
+                ok = n <= p.ltot && n >= k;
+            }
+            named_bar_sync(3, NL);  // the list is complete
             if (warp == 0) {
-                warp_topk_sorted_n(cand_v, n, k, vals);
+                const bool one_warp = ok && n <= KLIST;
+                if (one_warp) warp_topk_sorted_n(cand_v, n, k, vals);
                 if (want_lse) {
                     named_bar_sync(1, 64);
                     lse = ctl->lse;
                 }
-                const int pos = warp_list_kept_draw(cand_v, cand_i, n, k, hf, lse, top_p, p.min_keep, topk_only, drop,
-                                                    ctl->u, vals, sv, si);
-                if (lane == 0) ctl->kn = pos;
-            } else if (warp == 1 && want_lse) {
-                const float l = finish_lse();
-                if (lane == 0) ctl->lse = l;
+                int pos = 0x7fffffff;
+                if (one_warp)
+                    pos = warp_list_kept_draw(cand_v, cand_i, n, k, hf, lse, top_p, p.min_keep, topk_only, drop, ctl->u,
+                                              vals, sv, si);
+                if (lane == 0) {
+                    ctl->kn = pos;
+                    ctl->sr_state = one_warp ? 1 : ok ? 2 : 0;
+                    ctl->sr_n = n;
+                }
+            }
+        } else if (want_lse) {
+            if (lse_sum) {
+                lse_part(NL, NT - NL);
+                named_bar_sync(2, NT - NL);
+            }
+            if (warp == 4) {
+                double sum = 0.0;
+#pragma unroll
+                for (int w = 4; w < NWARP; ++w) sum += ctl->red_d[w];
+                if (lane == 0) ctl->lse = lse_sum ? lse_of(sum) : lse_special;
                 named_bar_arrive(1, 64);
             }
-            __syncthreads();
+        }
+        __syncthreads();
+        // 1: warp 0 drew; 2: the list is complete but longer than one warp's; 0: the full-row path
+        const int state = ctl->sr_state, n = ctl->sr_n;
+        if (want_lse) lse = ctl->lse;
+        if (state == 1) {
             const int pos = ctl->kn;
             token = pos == 0x7fffffff ? (int64_t)(V - 1) : (int64_t)si[pos];
-        } else if (!ovf && n <= 2 * KLIST) {
-            lse = finish_lse();
+        } else if (state == 2 && n <= 2 * KLIST) {
+            __syncthreads();  // every thread has read the state before the list stage reuses ctl
             const Scr sc{hist, ctl->rctl, &ctl->gather_n, &ctl->kn, &ctl->thr, ctl->red_d, ctl->red_f, ctl->red_i};
             float thr;
             token = list_sample(cand_v, cand_i, n, k, hf, lse, top_p, p.min_keep, topk_only, true, drop, ctl->u, V, vals,
                                 kv, ki, sv, si, sc, thr, true);
-        } else if (!ovf) {
-            lse = finish_lse();
+        } else if (state == 2) {
+            __syncthreads();
             token = block_list_token(cand_v, cand_i, kv, ki, sv, si, n, k, hf, lse, top_p, p.min_keep, topk_only, drop,
                                      ctl->u, V, vals, hist, ctl);
         } else {
-            lse = finish_lse();
+            __syncthreads();
             token = short_exact<E>(p, R, hb, k, hf, lse, top_p, topk_only, drop, pen_hist, censor, T, ctl->u, hist,
                                    vals, ctl);
         }
+    } else if (mode == MODE_FILTER) {
+        // NaN, the exact path asked for, top_k beyond the list stage or an extreme temperature: the full-row path
+        if (lse_sum) {
+            lse_part(0, NT);
+            __syncthreads();
+            double sum = 0.0;
+#pragma unroll
+            for (int w = 0; w < NWARP; ++w) sum += ctl->red_d[w];
+            lse = lse_of(sum);
+            __syncthreads();
+        } else if (want_lse) {
+            lse = lse_special;
+        }
+        token = short_exact<E>(p, R, hb, k, hf, lse, top_p, topk_only, drop, pen_hist, censor, T, ctl->u, hist, vals,
+                               ctl);
     }
     if (mode == MODE_FORCED) token = eos_ok ? (int64_t)p.eos : (int64_t)(V - 1);
     if (mode == MODE_FULL) token = full_token<E>(R, drop, ctl->u, ctl);
