@@ -158,10 +158,11 @@ def measured_peak_gbs():
 
 
 def profiled_traffic(workload: str, w, path: str = "auto") -> float | None:
-    """DRAM bytes per launch of the workload's kernel from the committed ncu summary, or None (the row-resident
-    kernel's summary first where the launcher picks that kernel for the workload)."""
+    """DRAM bytes per launch of the workload's kernel from the committed ncu summary, or None (the summary of the
+    kernel the launcher picks for the workload first: short-row, row-resident, then streaming)."""
     kernels = ["argmax_kernel"] if w.get("op") == "argmax" else (
-        ["sample_kernel"] if path == "stream" else ["resident_kernel", "sample_kernel"])
+        ["sample_kernel"] if path == "stream" else ["resident_kernel"] if path == "resident" else
+        ["short_kernel", "resident_kernel", "sample_kernel"])
     for kernel in kernels:
         f = ROOT / "profiles" / f"{kernel}_{workload}.md"
         if f.exists():
@@ -471,12 +472,15 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--eager", action="store_true", help="time plain launches instead of CUDA graphs (profiling)")
     ap.add_argument("--path", default="auto", choices=["auto", "stream", "resident"],
-                    help="sampling kernel: the launcher's choice, the streaming kernel, or the row-resident kernel")
+                    help="sampling kernel: the launcher's choice (short-row kernel for rows of <= 8192 elements, "
+                         "else row-resident), the streaming kernel, or the row-resident kernel")
     ap.add_argument("--cluster", type=int, default=0, help="CTAs per row of the row-resident kernel (0: auto)")
     ap.add_argument("--strong", action="store_true",
                     help="split the workload's batch over the ranks (strong scaling) instead of B rows per rank")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
+    if args.path == "resident" and args.cluster == 0 and w["vocab"] <= 8192 and w.get("window", 0) <= 255:
+        args.cluster = 1  # short rows: the launcher's own choice is the short-row kernel; one CTA per row asks for this one
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -1305,7 +1305,9 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
         const bool res_ok = lean && draws && !identity && !streamed && kmax <= KLIST;
         int CL = 0;
         Params rp = p;
-        if (a->cluster == 0 && res_ok && short_layout(rp, a, es, kmax)) {
+        // the short-row kernel also takes K frames per launch (one CTA per row, frames in order)
+        const bool short_ok = lean && draws && !identity && (a->flags & B2S_FLAG_STREAM) == 0 && kmax <= KLIST;
+        if (a->cluster == 0 && short_ok && short_layout(rp, a, es, kmax)) {
             // short rows: one CTA per row, the row's elements in its threads' registers (b2s_short.cu)
             const bool omni = a->semantics == B2S_SEM_OMNI;
             ResKernel kern = short_kernel_for(a->logits_dtype == B2S_DTYPE_BF16, omni);

@@ -1,5 +1,6 @@
-// Short-row sampling kernel (sm_100a): the decode-step form of b2s_sample for rows of at most SHORT_EPT * NT
-// interior elements -- the Talker's codec vocabulary (6,562 ids) in fp32 or bf16 -- one CTA per row.
+// Short-row sampling kernel (sm_100a): the decode-step form of b2s_sample (and of b2s_sample_frames: the CTA takes
+// its row's K frames in order, the state advancing in place) for rows of at most SHORT_EPT * NT interior elements
+// -- the Talker's codec vocabulary (6,562 ids) in fp32 or bf16 -- one CTA per row.
 //
 // Such a row is a few tens of KB: its step is as long as its chain of dependent phases, not as its bytes.
 // The kernel keeps that chain short and its instructions few:
@@ -99,16 +100,21 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     float* vals = reinterpret_cast<float*>(smem + p.off_vals);
     uint32_t* hist = reinterpret_cast<uint32_t*>(smem + p.off_hist);
     const int V = p.V;
-    // before the wait for the previous kernel (nothing global is read): the count bytes zeroed, tau's slot
+    // several frames (b2s_sample_frames): this CTA takes its row's frames in order, each one's state written in
+    // place being the next one's input
+    for (int f = 0; f < p.frames; ++f) {
+    const int w = f * p.rows + r;  // work item: tokens and uniform values are [frames, rows]
+    if (f > 0) __syncthreads();  // the previous frame's state is visible to the CTA; its shared memory is free
+    // (frame 0: before the wait for the previous kernel -- nothing global is read) the count bytes zeroed, tau's slot
     if (p.hist && p.W > 0)
         for (uint32_t g = tid; g < p.cnt_words / 4; g += NT) reinterpret_cast<uint4*>(cnts)[g] = make_uint4(0u, 0u, 0u, 0u);
     if (tid == 0) ctl->thr = f_ninf();  // tau, until a rank finds it
     __syncthreads();
-    pdl_wait_then_release();  // nothing global is read before the previous kernel of the stream is done
+    if (f == 0) pdl_wait_then_release();  // nothing global is read before the previous kernel of the stream is done
 
     // ---------------- loads: this thread's row elements and history id (registers), the penalty table
     Row<E> R;
-    R.rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
+    R.rowp = reinterpret_cast<const unsigned char*>(p.logits) + ((int64_t)f * p.fstride + (int64_t)r * p.lstride) * ES;
     R.V = V;
     {
         const uintptr_t a = reinterpret_cast<uintptr_t>(R.rowp), b = a + (uintptr_t)V * ES;
@@ -161,7 +167,7 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
         }
     }
     if (tid == 32) {
-        ctl->u = (p.rng == B2S_RNG_UNIFORM || !p.seeds) ? (p.uvals ? p.uvals[r] : 0.0f)
+        ctl->u = (p.rng == B2S_RNG_UNIFORM || !p.seeds) ? (p.uvals ? p.uvals[w] : 0.0f)
                  : p.rng == B2S_RNG_PHILOX ? uniform_philox(p.seeds[r], step, p.requests ? p.requests[r] : 0)
                                            : uniform_counter(p.seeds[r], step);
     }
@@ -482,7 +488,7 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     const bool adv = is_live && tok_drawn != PAD;
     const int64_t tok = adv ? tok_drawn : PAD;
     if (tid == 0) {
-        if (p.tokens) p.tokens[r] = tok;
+        if (p.tokens) p.tokens[w] = tok;
         if (p.steps_out) p.steps_out[r] = step + (adv ? 1 : 0);
         if (p.fin_out) {
             const bool f0 = p.finished ? p.finished[r] != 0 : false;
@@ -493,6 +499,7 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
         int64_t* ho = p.hist_out + (int64_t)r * p.hostride;
         for (int j = tid; j < p.W; j += NT) ho[j] = adv ? (j + 1 < p.W ? hstage[j + 1] : tok) : hstage[j];
     }
+    }  // frames
 }
 
 ResKernel short_kernel_for(bool bf16, bool omni) {
