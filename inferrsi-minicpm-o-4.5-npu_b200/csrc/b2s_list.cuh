@@ -150,32 +150,36 @@ static __device__ __noinline__ float warp_topp_threshold(const float* vals, int 
     return vals[kept - 1];
 }
 
-// Warp 0: the draw over kn <= 128 items whose values sv[0..kn) are in vocabulary order -- softmax over them,
-// fp64 prefix of the probabilities (rounded to fp32 per prefix), the first position whose prefix exceeds
-// u * total (talker_sampler.py:168-172).  Returns that position in every lane, or 0x7fffffff when none does.
-__device__ __forceinline__ int warp_draw_sorted(const float* sv, int kn, float u) {
+// Warp 0: the draw over kn <= 32 * NPL items (NPL per lane, contiguous) whose values sv[0..kn) are in
+// vocabulary order -- softmax over them, fp64 prefix of the probabilities (rounded to fp32 per prefix), the
+// first position whose prefix exceeds u * total (talker_sampler.py:168-172).  Returns that position in every lane, or 0x7fffffff when none does.
+template <int NPL>
+__device__ __forceinline__ int warp_draw_packed(const float* sv, int kn, float u) {
     const int lane = threadIdx.x & 31;
-    float pv[4];
-    float lm = __int_as_float(0xff800000);
+    float pv[NPL];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int i = lane * 4 + j;
+    for (int j = 0; j < NPL; ++j) {
+        const int i = lane * NPL + j;
         pv[j] = i < kn ? sv[i] : __int_as_float(0xff800000);
-        lm = fmaxf(lm, pv[j]);
     }
-    const float m = warp_max(lm);
-    float e[4];
+    // the maximum by one redux on order keys (the items are never NaN; a zero maximum of either sign gives the
+    // same differences)
+    uint32_t key = okey(pv[0]);
+#pragma unroll
+    for (int j = 1; j < NPL; ++j) key = max(key, okey(pv[j]));
+    const float m = okey_to_f(__reduce_max_sync(0xffffffffu, key));
+    float e[NPL];
     double es = 0.0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        e[j] = (lane * 4 + j < kn) ? b2s_expf(__fsub_rn(pv[j], m)) : 0.0f;
+    for (int j = 0; j < NPL; ++j) {
+        e[j] = (lane * NPL + j < kn) ? b2s_expf(__fsub_rn(pv[j], m)) : 0.0f;
         es += (double)e[j];
     }
     const float sf = (float)warp_sum(es);
     double ps = 0.0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        e[j] = (lane * 4 + j < kn) ? __fdiv_rn(e[j], sf) : 0.0f;
+    for (int j = 0; j < NPL; ++j) {
+        e[j] = (lane * NPL + j < kn) ? __fdiv_rn(e[j], sf) : 0.0f;
         ps += (double)e[j];
     }
     const double incl = warp_incl_scan(ps);
@@ -184,13 +188,15 @@ __device__ __forceinline__ int warp_draw_sorted(const float* sv, int kn, float u
     double acc = incl - ps;
     int first = 0x7fffffff;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < NPL; ++j) {
         acc += (double)e[j];
-        if (first == 0x7fffffff && lane * 4 + j < kn && (float)acc > target) first = lane * 4 + j;
+        if (first == 0x7fffffff && lane * NPL + j < kn && (float)acc > target) first = lane * NPL + j;
     }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
-    return first;
+    return __reduce_min_sync(0xffffffffu, first);
+}
+// The draw over 32 < kn <= 128 items in vocabulary order: two items per lane up to 64, four beyond.
+__device__ __forceinline__ int warp_draw_sorted(const float* sv, int kn, float u) {
+    return kn <= 64 ? warp_draw_packed<2>(sv, kn, u) : warp_draw_packed<4>(sv, kn, u);
 }
 
 // Draw over the items >= thr (minus `drop_id` when >= 0): softmax over them, cumulative mass in vocabulary
