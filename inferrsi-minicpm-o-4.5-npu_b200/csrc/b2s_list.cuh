@@ -335,7 +335,9 @@ __device__ __forceinline__ float warp_topp(const float* vals, int k, bool hf, fl
 __device__ __forceinline__ int warp_draw32(float v, int kn, float u) {
     const int lane = threadIdx.x & 31;
     const bool valid = lane < kn;
-    const float m = warp_max(valid ? v : __int_as_float(0xff800000));
+    // the maximum by one redux on order keys (the items are never NaN; a zero maximum of either sign gives the
+    // same differences)
+    const float m = okey_to_f(__reduce_max_sync(0xffffffffu, okey(valid ? v : __int_as_float(0xff800000))));
     const float e = valid ? b2s_expf(__fsub_rn(v, m)) : 0.0f;
     const float sf = (float)warp_sum((double)e);
     const float pr = __fdiv_rn(e, sf);  // 0 stays 0
