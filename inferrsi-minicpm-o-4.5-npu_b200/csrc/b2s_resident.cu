@@ -117,26 +117,11 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
     uint32_t* hist = reinterpret_cast<uint32_t*>(smem + p.off_hist);
     constexpr int ES = Elem<E>::SZ, EPV = Elem<E>::EPV;
     const int V = p.V;
-    pdl_wait_then_release();  // nothing global is read before the previous kernel of the stream is done
-    // first phase of the cluster barrier: arrived here, waited on just before the first remote store, so that no
-    // CTA writes into another's shared memory before that one runs
+    // ---------------- before the wait for the previous kernel (nothing global is read): the first phase of the
+    // cluster barrier (arrived here, waited on just before the first remote store, so that no CTA writes into
+    // another's shared memory before that one runs), the row's geometry, the mbarriers, the zeroed history
+    // structures -- set-up a CTA that starts early does while the previous kernel finishes
     if (CL > 1) cluster_arrive_relaxed();
-
-    // ---------------- the history, the penalty table and the row's parameters are requested first; then the row
-    // slice's bulk copies
-    const int64_t* hrow = p.hist ? p.hist + (int64_t)r * p.hstride : nullptr;
-    if (hrow && p.W > 0) {
-        for (int j = tid; j < p.W; j += NT) cp_async8(&hstage[j], &hrow[j]);
-        const float* alpha = p.alpha ? p.alpha + (int64_t)r * p.alpha_stride : nullptr;
-        if (alpha)
-            for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], &alpha[j]);
-    }
-    const int64_t step = p.steps ? p.steps[r] : 0;
-    const bool is_live = (p.active ? p.active[r] != 0 : true) && !(p.finished ? p.finished[r] != 0 : false);
-    const float T = p.rT ? p.rT[r] : p.T;
-    const float top_p = p.rP ? p.rP[r] : p.top_p;
-    const int top_k = p.rK ? p.rK[r] : p.top_k;
-    const int64_t min_new = p.rminn ? p.rminn[r] : p.min_new, max_new = p.rmaxn ? p.rmaxn[r] : p.max_new;
     Row<E> R;
     R.rowp = reinterpret_cast<const unsigned char*>(p.logits) + (int64_t)r * p.lstride * ES;
     R.V = V;
@@ -159,14 +144,38 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
     if (tid == 0) {
         for (int i = 0; i < npc; ++i) mbar_init(&bar[i], 1u);
         fence_mbar_init();
+        ctl->err = 0;
+        ctl->kn = 0;
+    }
+    const bool may_ht = (p.W > 0 && p.hist != nullptr) || (p.eos >= 0 && p.eos < V);  // a superset of use_ht below
+    if (may_ht) {
+        for (uint32_t g = tid; g < p.bitwords / 4; g += NT) reinterpret_cast<uint4*>(bits)[g] = make_uint4(0u, 0u, 0u, 0u);
+        for (int d = tid; d < p.hcap; d += NT) hb.hcnt[d] = 0u;
+    }
+    smask[tid] = 0u;
+    pdl_wait_then_release();  // nothing global is read before the previous kernel of the stream is done
+
+    // ---------------- the history, the penalty table and the row's parameters are requested first; then the row
+    // slice's bulk copies
+    const int64_t* hrow = p.hist ? p.hist + (int64_t)r * p.hstride : nullptr;
+    if (hrow && p.W > 0) {
+        for (int j = tid; j < p.W; j += NT) cp_async8(&hstage[j], &hrow[j]);
+        const float* alpha = p.alpha ? p.alpha + (int64_t)r * p.alpha_stride : nullptr;
+        if (alpha)
+            for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], &alpha[j]);
+    }
+    const int64_t step = p.steps ? p.steps[r] : 0;
+    const bool is_live = (p.active ? p.active[r] != 0 : true) && !(p.finished ? p.finished[r] != 0 : false);
+    const float T = p.rT ? p.rT[r] : p.T;
+    const float top_p = p.rP ? p.rP[r] : p.top_p;
+    const int top_k = p.rK ? p.rK[r] : p.top_k;
+    const int64_t min_new = p.rminn ? p.rminn[r] : p.min_new, max_new = p.rmaxn ? p.rmaxn[r] : p.max_new;
+    if (tid == 0)
         for (int i = 0; i < npc; ++i) {
             const uint32_t bytes = (uint32_t)min(RPV, nv - i * RPV) * 16u;
             mbar_arrive_expect_tx(&bar[i], bytes);
             bulk_g2s(const_cast<uint4*>(slice) + (size_t)i * RPV, R.gvec + v0 + (size_t)i * RPV, bytes, &bar[i]);
         }
-        ctl->err = 0;
-        ctl->kn = 0;
-    }
     // the ids this CTA is responsible for: its slice, and (rank 0) the elements outside the 16-byte interior
     const int e_lo = R.e0 + v0 * EPV, e_hi = e_lo + nv * EPV, i_end = R.e0 + R.nvec * EPV;
     auto owns = [&](int id) { return (id >= e_lo && id < e_hi) || (lead && (id < R.e0 || id >= i_end)); };
@@ -202,11 +211,6 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
     R.pref = hb.pref;
     R.htv = hb.htv;
     R.censor = censor ? p.eos : -1;
-    if (use_ht) {
-        for (uint32_t g = tid; g < p.bitwords / 4; g += NT) reinterpret_cast<uint4*>(bits)[g] = make_uint4(0u, 0u, 0u, 0u);
-        for (int d = tid; d < p.hcap; d += NT) hb.hcnt[d] = 0u;
-    }
-    smask[tid] = 0u;
     // rank 0: the elements outside the 16-byte interior, one per lane of the last warp's lanes 16..31 (head in
     // 16..23, tail in 24..31; a row with no interior vector has at most 15 elements, all in lanes 16..31)
     int edge_i = -1;
