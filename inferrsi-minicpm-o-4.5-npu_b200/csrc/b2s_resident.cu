@@ -147,11 +147,18 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
         ctl->err = 0;
         ctl->kn = 0;
     }
+    // omni order (the Thinker's): the owned history ids go into an (id, count) hash table and a dense list instead
+    // of bitmap ranks -- the fast path reads them by list position; a row taking a full-row path rebuilds the ranks
+    constexpr bool HASH = SEM == B2S_SEM_OMNI;
+    uint32_t* ht = reinterpret_cast<uint32_t*>(smem + p.off_ht);
     const bool may_ht = (p.W > 0 && p.hist != nullptr) || (p.eos >= 0 && p.eos < V);  // a superset of use_ht below
     if (may_ht) {
         for (uint32_t g = tid; g < p.bitwords / 4; g += NT) reinterpret_cast<uint4*>(bits)[g] = make_uint4(0u, 0u, 0u, 0u);
         for (int d = tid; d < p.hcap; d += NT) hb.hcnt[d] = 0u;
+        if (HASH)
+            for (uint32_t g = tid; g < p.ht_slots; g += NT) ht[g] = HT_EMPTY;
     }
+    if (HASH && tid == 0) ctl->hd_n = 0;
     smask[tid] = 0u;
     pdl_wait_then_release();  // nothing global is read before the previous kernel of the stream is done
 
@@ -246,13 +253,24 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
                 if (!owns(id)) continue;
                 atomicOr(&bits[id >> 5], 1u << (id & 31));
                 if (id >= e_lo && id < e_hi) mark_share(id);
+                if (HASH) {
+                    uint32_t slot;
+                    if (ht_add(ht, p.ht_slots, (uint32_t)id, 1u, slot)) hb.hpos[atomicAdd(&ctl->hd_n, 1)] = (int)slot;
+                }
             }
         if (censor && tid == 0 && owns(p.eos)) {
             atomicOr(&bits[p.eos >> 5], 1u << (p.eos & 31));
             if (p.eos >= e_lo && p.eos < e_hi) mark_share(p.eos);
+            if (HASH) {
+                uint32_t slot;
+                if (ht_add(ht, p.ht_slots, (uint32_t)p.eos, 0u, slot)) hb.hpos[atomicAdd(&ctl->hd_n, 1)] = (int)slot;
+            }
         }
         __syncthreads();
-        hd = hist_rank_count<E>(p, R, hb, pen_hist, censor, owns, ctl);
+        if (HASH)
+            hd = ctl->hd_n;  // hpos[0, hd): the slots of the distinct owned ids
+        else
+            hd = hist_rank_count<E>(p, R, hb, pen_hist, censor, owns, ctl);
     }
 
     // ---------------- the slice lands piece by piece: each thread's maximum of its share of every piece
@@ -278,14 +296,25 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
     }
     __syncthreads();  // smask and the counts are complete; every piece has landed
     // the owned history ids' processed values, their raw values from the resident slice (edges: global memory)
-    if (use_ht)
-        hist_values<E>(p, R, hb, hd, hf, pen_hist, censor, T, [&](int id) {
-            if (id >= e_lo && id < e_hi) {
-                const int rel = id - e_lo;
-                return Elem<E>::at(slice[rel / EPV], rel % EPV);
-            }
-            return Elem<E>::gld(R.rowp, id);
-        });
+    auto raw_of = [&](int id) {
+        if (id >= e_lo && id < e_hi) {
+            const int rel = id - e_lo;
+            return Elem<E>::at(slice[rel / EPV], rel % EPV);
+        }
+        return Elem<E>::gld(R.rowp, id);
+    };
+    if (use_ht && HASH) {
+        // the dense list's ids and processed values from the table's (id, count) words
+        for (int d = tid; d < hd; d += NT) {
+            const uint32_t wd = ht[hb.hpos[d]];
+            const int id = (int)(wd >> HT_CNT_BITS), n = (int)(wd & ((1u << HT_CNT_BITS) - 1u));
+            hb.hid[d] = id;
+            hb.htv[d] = (censor && id == p.eos) ? f_ninf()
+                        : pen_hist ? hist_proc_value(p, atab, hf, false, T, n, raw_of(id)) : f_ninf();
+        }
+    } else if (use_ht) {
+        hist_values<E>(p, R, hb, hd, hf, pen_hist, censor, T, raw_of);
+    }
 
     // ---------------- tau of this CTA's slice
     const bool cand_path = mode == MODE_FILTER && k <= KFAST && !(p.flags & B2S_FLAG_FORCE_GENERAL) && T >= 1e-6f &&
@@ -486,7 +515,7 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
     int64_t token = V - 1;
     float lse = 0.0f;
     const int drop = (hf && masked_eos) ? p.eos : -1;
-    if (mode == MODE_FILTER && !row_err && CL > 1 && ovf)
+    if (mode == MODE_FILTER && !row_err && (CL > 1 || HASH) && ovf)
         hist_rebuild<E>(p, R, hb, hf, pen_hist, censor, T, ctl);  // the full-row path reads every history value
     if (mode == MODE_FILTER && hf && !row_err) lse = resident_lse<E>(R, slice, nv, cand_v, n, !ovf, ctl);
     const bool topk_only = (p.flags & B2S_FLAG_TOPK_ONLY) != 0;

@@ -78,6 +78,7 @@ struct Params {
     // the row slice live, and the slice capacity in 16-byte vectors
     int cl, ltot, slice_vecs;
     uint32_t off_bar, off_slice;
+    uint32_t off_ht, ht_slots;  // row-resident kernel, omni order: the owned history ids' (id, count) hash table
     // short-row kernel (b2s_short.cu): one occurrence-count byte per element, 4 per word
     uint32_t off_cnt, cnt_words;
     // several frames in one launch (b2s_sample_frames): logits of frame f start f * fstride elements after frame 0's;
@@ -102,6 +103,7 @@ struct Ctl {
     int lovf;     // row-resident kernel: a CTA's candidates are incomplete or did not fit rank 0's list
     float rx_tau[8];  // row-resident kernel: each CTA's tau (every one bounds the row's k-th value from below)
     float lse;        // short-row kernel: the normaliser, handed from warp 4 to warp 0
+    int hd_n;         // row-resident kernel, omni order: distinct owned history ids appended to the dense list
     int sr_state, sr_n;  // short-row kernel: how the row's token is taken, and the candidates in the list
 };
 
@@ -201,6 +203,29 @@ __device__ __forceinline__ void ht_insert(uint32_t* ht, uint32_t slots, uint32_t
         }
         hs = (hs + 1) & (slots - 1);
     }
+}
+// ht_insert that also tells its caller the id's slot and whether this call put the id in the table (false for an
+// id already there; slot = slots when the table is full, which a table of at least twice the distinct ids never is).
+__device__ __forceinline__ bool ht_add(uint32_t* ht, uint32_t slots, uint32_t id, uint32_t add, uint32_t& slot) {
+    uint32_t hs = ht_slot(id, slots);
+    for (uint32_t probe = 0; probe < slots; ++probe) {
+        uint32_t cur = ht[hs];
+        if (cur == HT_EMPTY) {
+            cur = atomicCAS(&ht[hs], HT_EMPTY, (id << HT_CNT_BITS) | add);
+            if (cur == HT_EMPTY) {
+                slot = hs;
+                return true;
+            }
+        }
+        if ((cur >> HT_CNT_BITS) == id) {
+            if (add) atomicAdd(&ht[hs], add);
+            slot = hs;
+            return false;
+        }
+        hs = (hs + 1) & (slots - 1);
+    }
+    slot = slots;
+    return false;
 }
 __device__ __forceinline__ int ht_find(const uint32_t* ht, uint32_t slots, uint32_t id) {
     uint32_t h = ht_slot(id, slots);

@@ -1081,6 +1081,10 @@ static bool resident_layout(b2s::Params& p, const b2s_sample_args* a, int CL, in
     off = align_up(off + (uint32_t)p.hcap * 4, 16);
     p.off_smask = off;
     off = align_up(off + NT * 4, 16);
+    // omni rows: the owned history ids' hash table, at most half full
+    p.ht_slots = (a->semantics == B2S_SEM_OMNI && p.hcap > 0) ? (uint32_t)next_pow2(2 * p.hcap) : 0u;
+    p.off_ht = off;
+    off = align_up(off + p.ht_slots * 4, 16);
     p.off_hraw = off;  // unused: the history ids' raw values are read from the resident slice
     p.off_hstage = off;
     off = align_up(off + (uint32_t)a->window * 8, 16);
