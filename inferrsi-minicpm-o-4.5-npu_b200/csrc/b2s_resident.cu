@@ -330,12 +330,13 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
         for (int pc = 0; pc < RMAXP; ++pc)
             if (!((hm >> pc) & 1u)) tmax_nh = fmaxf(tmax_nh, tm[pc]);
         if (edge_i >= 0 && !R.hbit(edge_i)) tmax_nh = fmaxf(tmax_nh, edge_x);
-        float v = tmax_nh;
+        // the warp's jw largest, one redux on order keys each (tmax_nh is never NaN: fmaxf keeps the other operand)
+        uint32_t key = okey(tmax_nh);
         for (int t = 0; t < jw; ++t) {
-            const float mj = warp_max(v);
-            const unsigned who = __ballot_sync(0xffffffffu, v == mj);
-            if (who && lane == __ffs(who) - 1) v = f_ninf();
-            if (lane == 0) vals[warp * jw + t] = mj;
+            const uint32_t mk = __reduce_max_sync(0xffffffffu, key);
+            const unsigned who = __ballot_sync(0xffffffffu, key == mk);
+            if (lane == __ffs(who) - 1) key = 0u;  // below every key: taken
+            if (lane == 0) vals[warp * jw + t] = okey_to_f(mk);
         }
     }
     __syncthreads();
@@ -347,6 +348,7 @@ __global__ void __launch_bounds__(NT, 1) resident_kernel(const Params p) {
         for (int b = 0; b < ng; b += 32) {
             const float x = b + lane < ng ? vals[b + lane] : f_ninf();
             int gt = 0, eq = 0;
+#pragma unroll 4
             for (int j4 = 0; j4 < ng / 4; ++j4) {
                 const float4 y = v4[j4];
                 gt += (y.x > x) + (y.y > x) + (y.z > x) + (y.w > x);
