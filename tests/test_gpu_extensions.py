@@ -268,3 +268,40 @@ def test_paired_exp_equals_scalar_exp_exhaustively(pkg):
         bits = torch.arange(start - (1 << 32), start - (1 << 32) + n, dtype=torch.int64, device=DEV).to(torch.int32)
         y, y2 = _expf_spec(pkg, bits.view(torch.float32))
         assert torch.equal(y.view(torch.int32), y2.view(torch.int32)), hex(start)
+
+
+def test_resident_history_edges_match_oracle(pkg):
+    """Thinker-shaped omni rows on the row-resident kernel (its omni instantiation keeps the owned history ids in
+    a hash table): the EOS id is every row's largest logit and repeats in some histories, censored on the rows
+    before min_new and live on the others; top ids repeat up to five times, PAD entries are mixed in.  Tokens of
+    the launcher's choice (two CTAs per row), of four and eight CTAs per row, and of the forced full-row path
+    (which rebuilds the ranked structures) equal the oracle's."""
+    ts = pkg.talker_sampler
+    B = 6
+    logits, _, hist = _rows("thinker", B, 77)
+    eos = 4321
+    logits[:, eos] = logits.max(axis=1) + 1.0
+    logits = I.bf16_bits_to_f32(I.to_bf16_bits(logits))
+    x = _bf16(logits)
+    hist[0, 200:203] = eos
+    hist[2, 100] = eos
+    hist[4, 50:58] = eos
+    steps = np.array([2, 9, 2, 9, 0, 20], np.int64)
+    seeds = np.arange(B, dtype=np.int64) * 31 + 7
+    u = I.rng(12).random(B, dtype=np.float32)
+    ocfg = orc.Cfg(temperature=0.8, top_p=0.85, top_k=24, repetition_penalty=1.2, window=hist.shape[1],
+                   min_new_tokens=8, max_new_tokens=1 << 40, min_keep=1, semantics="omni")
+    _, want, _, _ = orc.sample(I.to_bf16_bits(logits), hist, steps, seeds, eos, ocfg, uniforms=u)
+    tcfg = ts.TalkerSampling(temperature=0.8, top_p=0.85, top_k=24, repetition_penalty=1.2, window=hist.shape[1],
+                             min_new_tokens=8, max_new_tokens=1 << 40, min_keep=1, semantics="omni")
+    hd = torch.from_numpy(hist).to(DEV)
+    kw = ts._cfg_kwargs(tcfg, hd, DEV)
+    runs = [(0, 0), (4, 0), (8, 0), (2, ts.FLAG_FORCE_EXACT)]
+    for cluster, flags in runs:
+        status = torch.zeros(1, dtype=torch.int32, device=DEV)
+        tok, _, _, _, _ = ts._run(x, history=hd, steps=torch.from_numpy(steps).to(DEV),
+                                  uniform_values=torch.from_numpy(u).to(DEV), eos=eos, rng=ts.RNG_UNIFORM,
+                                  status=status, flags=flags, cluster=cluster, tokens=True, processed=False, **kw)
+        assert np.array_equal(tok.cpu().numpy(), want), (cluster, flags, tok.cpu().numpy(), want)
+        assert int(status.item()) == 0
+    assert want[0] != eos and want[2] != eos and want[4] != eos  # censored rows never draw the EOS
