@@ -594,6 +594,10 @@ def main():
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):  # a graph replays on the current stream: time that stream
+        # a bounded spin (about 0.1 ms, torch's own) holds the stream while the host enqueues the start event and the
+        # replays, so the start event fires when the first step can start: the host's launch latency stays out of
+        # the K steps' device time, as it does in a decode loop that launches ahead of the GPU
+        torch.cuda._sleep(200_000)
         ev0.record(stream)
         if args.eager:
             for i in range(args.steps):
