@@ -48,6 +48,11 @@ WORKLOADS = {
     "talker_k": dict(rows=8, vocab=6562, dtype="bf16", window=64, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05,
                      order="hf", min_keep=3, eos=6561, min_new=8, row_temperature=(0.6, 0.8, 1.0),
                      row_top_k=(20, 25, 50), row_top_p=(0.7, 0.85, 0.95), frames=16),
+    # BASELINE config 2's batch from the Talker's codec head (hidden 768): the bf16 head GEMM and the step in one
+    # launch (talker_post_graph.py:58-63); a step reads the whole 6562 x 768 head
+    "talker_head": dict(rows=8, vocab=6562, dtype="bf16", window=64, temperature=0.8, top_k=25, top_p=0.85,
+                        penalty=1.05, order="hf", min_keep=3, eos=6561, min_new=8, row_temperature=(0.6, 0.8, 1.0),
+                        row_top_k=(20, 25, 50), row_top_p=(0.7, 0.85, 0.95), hidden=768, op="head"),
     # the single-stream Talker (one row, fp32, hf order, 16-token history)
     "talker1": dict(rows=1, vocab=6562, dtype="f32", window=16, temperature=0.8, top_k=25, top_p=0.85, penalty=1.05,
                     order="hf", min_keep=3, eos=6561, min_new=0),
@@ -62,10 +67,30 @@ WORKLOADS = {
 L2_BYTES = 126 * 1024 * 1024
 
 
-def bytes_per_row(w) -> int:
-    """Algorithmic bytes of one sampled row: logits read once, history ids as int32, 40 B params/state/token."""
+def bytes_per_row(w) -> float:
+    """Algorithmic bytes of one sampled row: logits read once, history ids as int32, 40 B params/state/token.
+    From the codec head: the head read once per step (its share per row), the row's hidden instead of logits
+    (which stay on chip and in L2)."""
+    if w.get("op") == "head":
+        return w["vocab"] * w["hidden"] * 2 / w["rows"] + 2 * w["hidden"] + 4 * w["window"] + 40
     e = 2 if w["dtype"] == "bf16" else 4
     return w["vocab"] * e + 4 * w["window"] + 40
+
+
+def head_operands(w, rows: int, seed: int):
+    """Hidden rows [rows, H] and a head [V, H] (fp32 arrays holding bf16 values): logits ~ N(0, 2); hidden
+    column 0 is 8 and the EOS row's entry there -4, so that EOS stays far below the rest and rows stay live."""
+    from tests.golden import inputs as I
+
+    g = I.rng(seed)
+    H, V = w["hidden"], w["vocab"]
+    hid = g.standard_normal((rows, H)).astype(np.float32)
+    hid[:, 0] = 8.0
+    head = (g.standard_normal((V, H)) * (2.0 / H ** 0.5)).astype(np.float32)
+    if w.get("eos", -1) >= 0:
+        head[w["eos"], 0] = -4.0
+    bf = lambda a: I.bf16_bits_to_f32(I.to_bf16_bits(a))
+    return bf(hid), bf(head)
 
 
 def make_inputs(w, rows: int, seed: int):
@@ -160,7 +185,7 @@ def measured_peak_gbs():
 def profiled_traffic(workload: str, w, path: str = "auto") -> float | None:
     """DRAM bytes per launch of the workload's kernel from the committed ncu summary, or None (the summary of the
     kernel the launcher picks for the workload first: short-row, row-resident, then streaming)."""
-    kernels = ["argmax_kernel"] if w.get("op") == "argmax" else (
+    kernels = ["argmax_kernel"] if w.get("op") == "argmax" else ["head_kernel"] if w.get("op") == "head" else (
         ["sample_kernel"] if path == "stream" else ["resident_kernel"] if path == "resident" else
         ["short_kernel", "resident_kernel", "sample_kernel"])
     for kernel in kernels:
@@ -189,6 +214,11 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
                      row_top_p=np.array([w["row_top_p"][i % 3] for i in range(rows)], np.float32),
                      row_top_k=np.array([w["row_top_k"][i % 3] for i in range(rows)], np.int32))
     seeds = np.arange(rows, dtype=np.int64)
+    head = w.get("op") == "head"
+    if head:  # the head's matmul in fp32 (numpy), rounded to bf16, inside every step
+        hid, hw = head_operands(w, rows, 1234)
+        logits_of = lambda: I.to_bf16_bits(hid @ hw.T)
+        x = logits_of()
     if w.get("op") == "argmax":
         orc.argmax(x)
         done, t0, step = 0, time.perf_counter(), 0
@@ -209,6 +239,8 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
     t0 = time.perf_counter()
     step = 0
     while True:
+        if head:
+            x = logits_of()
         orc.sample(x, hist, np.full(rows, step + 1, np.int64), seeds, eos, cfg, rng=orc.RNG_PHILOX,
                    requests=np.zeros(rows, np.int64), want_processed=False, threads=threads, **rowkw)
         done += rows
@@ -218,7 +250,7 @@ def cpu_baseline(w, seconds: float = 10.0, threads: int = 0) -> dict:
             break
     return {"value": done / el, "unit": "rows/s", "cores": threads, "kind": "port",
             "sample": f"{step} steps x {rows} rows of the {w['vocab']}-vocab workload in {el:.1f} s "
-                      f"(oracle/sampler_oracle.c, OpenMP)"}
+                      f"({'numpy fp32 head matmul + ' if head else ''}oracle/sampler_oracle.c, OpenMP)"}
 
 
 def reference_cpu(w, *, steps: int = 0, warmup: int = 1, seconds: float = 10.0, threads: int = 0) -> dict:
@@ -242,6 +274,10 @@ def reference_cpu(w, *, steps: int = 0, warmup: int = 1, seconds: float = 10.0, 
     if w["dtype"] == "bf16":
         x = x.to(torch.bfloat16)
     h = torch.from_numpy(hist)
+    head = w.get("op") == "head"
+    if head:  # the reference graph body: F.linear(hidden, head).float() (bf16 operands) before the sampler
+        hid, hw = head_operands(w, rows, 1234)
+        hid_t, hw_t = torch.from_numpy(hid).to(torch.bfloat16), torch.from_numpy(hw).to(torch.bfloat16)
     seeds = torch.arange(rows, dtype=torch.int64)
     eos = w.get("eos", -1)
     groups = [(list(range(rows)), w["temperature"], w["top_k"], w["top_p"])]
@@ -259,8 +295,9 @@ def reference_cpu(w, *, steps: int = 0, warmup: int = 1, seconds: float = 10.0, 
         if w.get("op") == "argmax":
             return x.float().argmax(-1)
         out = []
+        xx = torch.nn.functional.linear(hid_t, hw_t).float() if head else x
         for idx, cfg in cfgs:
-            xs, hs, ss = (x, h, st) if len(cfgs) == 1 else (x[idx], h[idx], st[idx])
+            xs, hs, ss = (xx, h, st) if len(cfgs) == 1 else (xx[idx], h[idx], st[idx])
             proc = ref.processed_logits(xs, hs, ss, eos, cfg)
             out.append(ref.draw(proc, seeds[idx], ss))
         return out
@@ -275,7 +312,8 @@ def reference_cpu(w, *, steps: int = 0, warmup: int = 1, seconds: float = 10.0, 
         el = time.perf_counter() - t0
         if (steps > 0 and n >= steps) or (steps <= 0 and el >= seconds):
             break
-    what = "logits.float().argmax(-1)" if w.get("op") == "argmax" else "processed_logits + draw"
+    what = ("logits.float().argmax(-1)" if w.get("op") == "argmax" else
+            "F.linear(hidden, head).float() + processed_logits + draw" if head else "processed_logits + draw")
     return {"value": done / el, "unit": "rows/s", "cores": threads, "kind": "reference",
             "sample": f"{n} steps x {rows} rows of the {w['vocab']}-vocab workload in {el:.1f} s "
                       f"(reference engine/talker_sampler.py {what}, CPU torch {torch.__version__}, "
@@ -286,6 +324,10 @@ def metric_of(w) -> str:
     if w.get("op") == "vocab_shard":
         return (f"sampled rows/s at B={w['rows']} x V={w['vocab']} over the job's vocabulary shards "
                 "(per-shard candidates + NCCL all-gather + merged draw)")
+    if w.get("op") == "head":
+        return (f"sampled rows/s from the codec head, whole job (n_gpus x B={w['rows']} rows per GPU) at "
+                f"V={w['vocab']}, hidden {w['hidden']}; per GPU = value_per_gpu (bf16 head GEMM on the tensor cores "
+                "+ fused penalty+temperature+top-k+top-p+draw, one launch)")
     if w.get("op") == "argmax":
         return (f"greedy rows/s, whole job (n_gpus x B={w['rows']} rows per GPU) at V={w['vocab']}; per GPU = "
                 "value_per_gpu (argmax, first index on ties)")
@@ -298,8 +340,9 @@ def dtype_of(w) -> str:
 
 
 def rotating_buffers(w) -> int:
-    """Distinct logits buffers: one sweep exceeds twice the L2 and 640 MiB (>= 32 thinker steps)."""
-    buf = w["rows"] * w["vocab"] * (2 if w["dtype"] == "bf16" else 4)
+    """Distinct logits buffers (heads, for the codec head): one sweep exceeds twice the L2 and 640 MiB."""
+    buf = (w["vocab"] * w["hidden"] * 2 if w.get("op") == "head" else
+           w["rows"] * w["vocab"] * (2 if w["dtype"] == "bf16" else 4))
     return max(2, min(8192, math.ceil(max(2 * L2_BYTES, 640 * 2**20) / buf)))
 
 
@@ -315,8 +358,10 @@ def config_of(args, w, world: int) -> dict:
             "min_keep": w.get("min_keep", 1), "eos": w.get("eos", -1), "min_new_tokens": w.get("min_new", 0),
             "per_row": {k: list(w[k]) for k in ("row_temperature", "row_top_k", "row_top_p") if k in w} or None,
             "parallelism": f"rows x{world}",
-            "l2": f"{nbuf} rotating logits buffers ({nbuf * B * V * (2 if w['dtype'] == 'bf16' else 4) / 2**20:.0f}"
-                  " MiB > L2)",
+            "l2": (f"{nbuf} rotating heads ({nbuf * V * w['hidden'] * 2 / 2**20:.0f} MiB > L2)" if w.get("op") == "head"
+                   else f"{nbuf} rotating logits buffers "
+                        f"({nbuf * B * V * (2 if w['dtype'] == 'bf16' else 4) / 2**20:.0f} MiB > L2)"),
+            "hidden": w.get("hidden"),
             "cuda_graph_steps": 0 if args.eager else min(args.steps, 1000), "kernel_path": args.path,
             "cluster": args.cluster, "frames_per_step": w.get("frames", 1)}
 
@@ -460,6 +505,195 @@ def run_reference(args, w, rank: int):
     print(json.dumps(line))
 
 
+def run_head(args, w, rank: int, world: int, local: int):
+    """The codec head and the step in one launch (``CodecHead``): each step reads a whole head -- one of
+    ``rotating_buffers`` distinct copies, so that the heads of a sweep exceed the L2 as the Talker's layer weights
+    evict it between two head calls in a decode loop -- and advances the state in place."""
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    pkg = __graft_entry__.load_package()
+    ts = pkg.talker_sampler
+    B, V, W, Hd = w["rows"], w["vocab"], w["window"], w["hidden"]
+    eos = w.get("eos", -1)
+    nbuf = rotating_buffers(w)
+    hid_h, head_h = head_operands(w, B, 1000 + rank)
+    _, hist_h = make_inputs(dict(w, vocab=V, dtype="f32"), B, 1000 + rank)
+    head0 = torch.from_numpy(head_h).to(dev).to(torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    heads, hiddens = [], []
+    hid0 = torch.from_numpy(hid_h).to(dev).to(torch.bfloat16)
+    for i in range(nbuf):  # distinct heads: a per-copy permutation of the ids (EOS stays in place)
+        perm = torch.randperm(V - 1 if eos >= 0 else V, device=dev, generator=g)
+        if eos >= 0:
+            perm = torch.cat([perm, torch.tensor([V - 1], device=dev)])
+        heads.append(head0[perm].contiguous())
+        hiddens.append(torch.cat([hid0[:, :1], torch.roll(hid0[:, 1:], i, dims=1)], dim=1).contiguous())
+    del head0
+    cfg = ts.TalkerSampling(temperature=w["temperature"], top_p=w["top_p"], top_k=w["top_k"],
+                            repetition_penalty=w["penalty"], window=W, min_new_tokens=w.get("min_new", 0),
+                            max_new_tokens=1 << 62, min_keep=w.get("min_keep", 1), semantics=w.get("order", "omni"),
+                            rng="counter")
+    state = ts.DecodeState.new(list(range(rank * B, rank * B + B)), cfg, device=dev)
+    state.history.copy_(torch.from_numpy(hist_h).to(dev))
+    state.steps.fill_(1)
+    rp = ts.RowParams(
+        temperature=torch.tensor([w["row_temperature"][i % 3] for i in range(B)], dtype=torch.float32, device=dev),
+        top_p=torch.tensor([w["row_top_p"][i % 3] for i in range(B)], dtype=torch.float32, device=dev),
+        top_k=torch.tensor([w["row_top_k"][i % 3] for i in range(B)], dtype=torch.int32, device=dev),
+        max_top_k=max(w["row_top_k"]))
+    kw = ts._cfg_kwargs(cfg, state.history, dev, rp)
+    ops = pkg._native.ops()
+    ch = ts.CodecHead(heads[0], B)
+
+    def one_step(i):
+        return ops.head_sample_state_(hiddens[i % nbuf], heads[i % nbuf], ch.logits, ch.sync, state.history,
+                                      state.steps, state.finished, state.seeds, None, state.active, kw["alpha"], None,
+                                      rp.temperature, rp.top_p, rp.top_k, kw["temperature"], cfg.top_p, cfg.top_k,
+                                      kw["min_keep"], cfg.min_new_tokens, cfg.max_new_tokens, eos, kw["semantics"],
+                                      ts.RNG_PHILOX, kw["max_top_k"])
+
+    ms, ck, graphs = time_steps(args, one_step, dev, local, world)
+    ms_per_step = ms / args.steps
+    value = B * world * args.steps / (ms / 1e3)
+    step_bytes = V * Hd * 2 + B * (2 * Hd + 4 * W + 40)
+    achieved = step_bytes / (ms_per_step / 1e3) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+
+    # end to end through the public API: pinned host hidden rows -> device, CodecHead.step_, tokens -> host
+    e2e_steps = max(1, args.e2e_steps)
+    host = torch.from_numpy(hid_h).to(torch.bfloat16).contiguous().pin_memory()
+    dbuf = torch.empty_like(host, device=dev)
+    tok_h = torch.empty(B, dtype=torch.int64).pin_memory()
+    st_e = ts.DecodeState(seeds=state.seeds.clone(), steps=torch.ones(B, dtype=torch.int64, device=dev),
+                          history=state.history.clone(), finished=state.finished.clone(), active=state.active.clone())
+    ch_e = ts.CodecHead(heads[0], B)
+
+    def api_step():
+        dbuf.copy_(host, non_blocking=True)
+        tok = ch_e.step_(st_e, dbuf, eos, cfg, row_params=rp, rng="philox")
+        tok_h.copy_(tok, non_blocking=True)
+
+    for _ in range(3 if args.e2e_steps else 0):
+        api_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        api_step()
+    e1.record()
+    torch.cuda.synchronize()
+    et = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_value = B * world * e2e_steps / (float(et.item()) / 1e3)
+
+    cb = cb_port = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import ref_build
+
+        cb_port = cpu_baseline(w, seconds=min(args.cpu_seconds, 5.0))
+        cb = reference_cpu(w, seconds=args.cpu_seconds) if ref_build.available() else cb_port
+    for gr, _ in graphs:
+        del gr
+    graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": metric_of(w),
+        "value": value, "unit": "rows/s", "value_per_gpu": value / world, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (head GEMM, fp32 accumulation) -> f32 (sampling)", "data": "synthetic",
+        "config": config_of(args, w, world),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": profiled_traffic(args.workload, w, args.path), "bytes_per_step": step_bytes,
+                     "peak_source": peak_kind},
+        "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": host.numel() * host.element_size(),
+                "d2h_bytes_per_step": B * 8, "steps": e2e_steps},
+        "gpu_launches": args.steps,
+        "clocks": ck,
+        "cpu_baseline": cb,
+        "cpu_baseline_port": cb_port,
+    }
+    print(json.dumps(line))
+
+
+def time_steps(args, one_step, dev, local: int, world: int):
+    """W untimed steps, then exactly K steps (CUDA graphs of up to 1000 steps, each replayed once untimed before
+    the timed replays) between CUDA events on the launching stream, with nvidia-smi clocks sampled meanwhile;
+    the max over ranks.  Returns (ms over the K steps, clocks, graphs -- released by the caller)."""
+    import torch
+    import torch.distributed as dist
+
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            one_step(i)
+    torch.cuda.synchronize()
+    # the K timed steps as CUDA graphs (G steps per graph): no host launch cost between steps
+    G = min(args.steps, 1000)
+    reps, rem = divmod(args.steps, G)
+    graphs = []
+    for n in ([] if args.eager else ([G] if reps else []) + ([rem] if rem else [])):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for i in range(n):
+                one_step(i)
+        graphs.append((gr, n))
+    # one untimed replay of each graph: its upload and the first replay's cold start stay out of the timed region
+    with torch.cuda.stream(stream):
+        for gr, _ in graphs:
+            gr.replay()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(vis.split(",")[local].strip() if vis else local)
+    clocks.start()
+    time.sleep(0.1)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):  # a graph replays on the current stream: time that stream
+        # a bounded spin (about 0.1 ms, torch's own) holds the stream while the host enqueues the start event and the
+        # replays, so the start event fires when the first step can start: the host's launch latency stays out of
+        # the K steps' device time, as it does in a decode loop that launches ahead of the GPU
+        torch.cuda._sleep(200_000)
+        ev0.record(stream)
+        if args.eager:
+            for i in range(args.steps):
+                one_step(i)
+        else:
+            for r in range(reps):
+                graphs[0][0].replay()
+            if rem:
+                graphs[-1][0].replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ck = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return ms, ck, graphs
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -488,6 +722,8 @@ def main():
         return run_reference(args, w, rank)
     if w.get("op") == "vocab_shard":
         return run_vocab_shard(args, w, rank, world, local)
+    if w.get("op") == "head":
+        return run_head(args, w, rank, world, local)
 
     import torch
     import torch.distributed as dist
@@ -564,59 +800,7 @@ def main():
                                  cfg.max_new_tokens, eos, kw["semantics"], ts.RNG_PHILOX, kw["max_top_k"],
                                  args.cluster, ts.FLAG_STREAM if args.path == "stream" else 0)
 
-    stream = torch.cuda.Stream(device=dev)
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            one_step(i)
-    torch.cuda.synchronize()
-    # the K timed steps as CUDA graphs (G steps per graph): no host launch cost between steps
-    G = min(args.steps, 1000)
-    reps, rem = divmod(args.steps, G)
-    graphs = []
-    for n in ([] if args.eager else ([G] if reps else []) + ([rem] if rem else [])):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            for i in range(n):
-                one_step(i)
-        graphs.append((gr, n))
-    # one untimed replay of each graph: its upload and the first replay's cold start stay out of the timed region
-    with torch.cuda.stream(stream):
-        for gr, _ in graphs:
-            gr.replay()
-    torch.cuda.synchronize()
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    clocks = ClockSampler(vis.split(",")[local].strip() if vis else local)
-    clocks.start()
-    time.sleep(0.1)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):  # a graph replays on the current stream: time that stream
-        # a bounded spin (about 0.1 ms, torch's own) holds the stream while the host enqueues the start event and the
-        # replays, so the start event fires when the first step can start: the host's launch latency stays out of
-        # the K steps' device time, as it does in a decode loop that launches ahead of the GPU
-        torch.cuda._sleep(200_000)
-        ev0.record(stream)
-        if args.eager:
-            for i in range(args.steps):
-                one_step(i)
-        else:
-            for r in range(reps):
-                graphs[0][0].replay()
-            if rem:
-                graphs[-1][0].replay()
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ck = clocks.stop()
-    ms = ev0.elapsed_time(ev1)
-    t = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms, ck, graphs = time_steps(args, one_step, dev, local, world)
     ms_per_step = ms / args.steps
     value = B * K * world * args.steps / (ms / 1e3)  # sampled rows (row-frames) per second
     peak, peak_kind = measured_peak_gbs()

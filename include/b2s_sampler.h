@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define B2S_ABI_VERSION 4
+#define B2S_ABI_VERSION 5
 
 /* return codes */
 #define B2S_OK 0
@@ -138,6 +138,31 @@ int b2s_sample(const b2s_sample_args* args, void* stream);
  * engine/runtime/talker_decode.py:120-128, engine/runtime/talker_block_graph.py:70-89.
  */
 int b2s_sample_frames(const b2s_sample_args* args, int32_t frames, int64_t frame_stride, void* stream);
+
+/*
+ * The Talker codec head and the sampling step in one launch (ABI 5):
+ *     logits = bf16(hidden[rows, hidden_dim] x head[vocab, hidden_dim]^T)   (fp32 accumulation, tensor cores)
+ * then b2s_sample's step on those logits.  The logits equal the bf16 output of F.linear up to the order of the
+ * fp32 accumulation; they are written to `logits` (args->logits_row_stride elements apart, args->logits NULL or
+ * equal) so that the caller can check them, and the rows' CTAs of the same launch read them there.
+ * Replaces: the head and the sampler of engine/runtime/talker_post_graph.py:58-63 (F.linear(hidden, head).float(),
+ * processed_logits, draw) and engine/runtime/talker_decode.py:120-121.
+ * Limits: rows <= 16, hidden_dim a multiple of 64 and at most 768, rows + ceil(vocab / 128) <= the GPU's SM count,
+ * bf16 only; args must be a decode step the short-row kernel takes (tokens and/or state out, no processed
+ * output, cluster 0, k <= 128, window <= 255, vocab <= 8192 * 16 / element size) -- else B2S_ERR_UNSUPPORTED.
+ * `head` is read before the launch waits for the stream's previous kernel: that kernel must not write it.
+ * `sync`: 4 words of device memory, zero before the first call, left zero by every call that completes; calls
+ * sharing one `sync` block must not overlap on the GPU (one block per stream).
+ */
+typedef struct b2s_head_args {
+    const void* hidden;        /* [rows, hidden_dim] bf16, 16-byte aligned */
+    int64_t hidden_row_stride; /* elements, a multiple of 8 */
+    const void* head;          /* [vocab, hidden_dim] bf16, contiguous rows, 16-byte aligned */
+    int32_t hidden_dim;
+    void* logits;              /* [rows, vocab] bf16 out */
+    uint32_t* sync;            /* 4 words, 16-byte aligned */
+} b2s_head_args;
+int b2s_head_sample(const b2s_head_args* head, const b2s_sample_args* args, void* stream);
 
 /*
  * Greedy next token: argmax over each row (first index among equal maxima, NaN wins).

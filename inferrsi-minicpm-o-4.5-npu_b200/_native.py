@@ -42,9 +42,18 @@ class SampleArgs(ctypes.Structure):
     ]
 
 
+class HeadArgs(ctypes.Structure):
+    """b2s_head_args of include/b2s_sampler.h."""
+    _fields_ = [
+        ("hidden", ctypes.c_void_p), ("hidden_row_stride", ctypes.c_int64), ("head", ctypes.c_void_p),
+        ("hidden_dim", ctypes.c_int32), ("logits", ctypes.c_void_p), ("sync", ctypes.c_void_p),
+    ]
+
+
 # every entry point of include/b2s_sampler.h with its ctypes signature
 CAPI_SIGNATURES = {
     "b2s_sample": (ctypes.c_int, [ctypes.POINTER(SampleArgs), ctypes.c_void_p]),
+    "b2s_head_sample": (ctypes.c_int, [ctypes.POINTER(HeadArgs), ctypes.POINTER(SampleArgs), ctypes.c_void_p]),
     "b2s_sample_frames": (ctypes.c_int, [ctypes.POINTER(SampleArgs), ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p]),
     "b2s_argmax": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
                                   ctypes.c_void_p, ctypes.c_void_p]),

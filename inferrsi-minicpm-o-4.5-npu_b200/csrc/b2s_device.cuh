@@ -152,6 +152,17 @@ __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
     return q;
 }
 
+// The same load without the read-only path: it sees data that another CTA of the same launch wrote and
+// published before this thread's acquire (the codec head's logits, b2s_head_sample).
+__device__ __forceinline__ uint4 ld_stream_coherent(const uint4* p) {
+    uint4 q;
+    asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
+                 : "l"(p)
+                 : "memory");
+    return q;
+}
+
 // Asynchronous 4 / 8-byte copies global -> shared (the issuing thread does not wait for them).
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");

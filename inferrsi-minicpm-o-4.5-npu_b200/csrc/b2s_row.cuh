@@ -5,6 +5,7 @@
 #pragma once
 
 #include <cooperative_groups.h>
+#include <cuda.h>  // CUtensorMap
 
 #include "../../include/b2s_sampler.h"
 #include "b2s_device.cuh"
@@ -85,6 +86,14 @@ struct Params {
     // tokens and uniform values are [frames, rows]; the state advances in place from frame to frame
     int frames;
     int64_t fstride;
+    // codec head in the same launch (b2s_head_sample): CTAs rows .. rows + head_tiles - 1 compute the bf16 logits
+    // rows (b2s_head.cuh) from hidden [rows, head_kb * 64] (hid_stride elements apart) into `logits`; the rows'
+    // CTAs wait on head_sync (4 words, zero between launches) before reading them
+    int head_tiles, head_kb;
+    int head_split, head_first;  // CTAs per tile (1, or 2 = a cluster splitting K); first tile CTA (rows, even if split)
+    const void* hidden;
+    int64_t hid_stride;
+    uint32_t* head_sync;
 };
 
 struct Ctl {
@@ -105,6 +114,7 @@ struct Ctl {
     float lse;        // short-row kernel: the normaliser, handed from warp 4 to warp 0
     int hd_n;         // row-resident kernel, omni order: distinct owned history ids appended to the dense list
     int sr_state, sr_n;  // short-row kernel: how the row's token is taken, and the candidates in the list
+    int head_ok;         // short-row kernel with the codec head: the row's logits are complete
 };
 
 template <typename E>
@@ -112,8 +122,9 @@ struct Elem;
 template <>
 struct Elem<float> {
     static constexpr int SZ = 4, EPV = 4;
+    // a plain (coherent) load: the logits may have been written earlier in the same launch (b2s_head_sample)
     static __device__ __forceinline__ float gld(const void* base, int64_t i) {
-        return __ldg(reinterpret_cast<const float*>(base) + i);
+        return reinterpret_cast<const float*>(base)[i];
     }
     static __device__ __forceinline__ float sld(const unsigned char* s) { return *reinterpret_cast<const float*>(s); }
     static __device__ __forceinline__ float vmax(uint4 q) {
@@ -142,7 +153,7 @@ template <>
 struct Elem<__nv_bfloat16> {
     static constexpr int SZ = 2, EPV = 8;
     static __device__ __forceinline__ float gld(const void* base, int64_t i) {
-        return bf16_bits_to_f(__ldg(reinterpret_cast<const unsigned short*>(base) + i));
+        return bf16_bits_to_f(reinterpret_cast<const unsigned short*>(base)[i]);
     }
     static __device__ __forceinline__ float sld(const unsigned char* s) {
         return bf16_bits_to_f(*reinterpret_cast<const uint16_t*>(s));
@@ -306,7 +317,7 @@ struct Row {
         if (hbit(i)) return htv[rank(i)];
         return f(x);
     }
-    __device__ __forceinline__ uint4 vec(int v) const { return __ldg(gvec + v); }
+    __device__ __forceinline__ uint4 vec(int v) const { return gvec[v]; }  // coherent, like Elem::gld
 };
 
 // Visit every element of the row as (index, raw value): interior vectors round-robin over the threads,
@@ -576,5 +587,10 @@ ResKernel resident_kernel_for(bool bf16, bool omni);
 // in registers; same instantiations.
 constexpr int SHORT_EPT = 16;
 ResKernel short_kernel_for(bool bf16, bool omni);
+
+// The short-row kernel with the Talker codec head in the same launch (b2s_short.cu, b2s_head.cuh): bf16 logits,
+// the head tile's TMA map as the second parameter.
+using HeadKernel = void (*)(const Params, const CUtensorMap);
+HeadKernel head_kernel_for(bool omni);
 
 }  // namespace b2s

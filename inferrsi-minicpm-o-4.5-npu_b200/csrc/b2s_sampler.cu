@@ -25,6 +25,7 @@
 // Selection runs on raw values: outside the history the processed value is fl(x / T), monotone in x.  No block in
 // this file waits on another block except at the hardware cluster barrier.
 #include "b2s_row.cuh"
+#include "b2s_head.cuh"
 
 #include <cooperative_groups.h>
 #include <stdio.h>
@@ -1156,8 +1157,18 @@ static bool short_layout(b2s::Params& p, const b2s_sample_args* a, int es, int k
     return off <= 227 * 1024;
 }
 
+// The codec head of b2s_head_sample: the head tiles' TMA map and operands (the rows' CTAs read `logits`).
+struct HeadLaunch {
+    CUtensorMap map;
+    int tiles, kb;
+    const void* hidden;
+    int64_t hid_stride;
+    uint32_t* sync;
+    void* logits;
+};
+
 static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut* so, int frames = 1,
-                         int64_t fstride = 0) {
+                         int64_t fstride = 0, const HeadLaunch* hl = nullptr) {
     using namespace b2s;
     if (!a || !a->logits || a->rows < 0 || a->vocab <= 0) return B2S_ERR_INVALID;
     if (a->rows == 0) return B2S_OK;
@@ -1311,6 +1322,58 @@ static int launch_sample(const b2s_sample_args* a, void* stream, const ShardOut*
         Params rp = p;
         // the short-row kernel also takes K frames per launch (one CTA per row, frames in order)
         const bool short_ok = lean && draws && !identity && (a->flags & B2S_FLAG_STREAM) == 0 && kmax <= KLIST;
+        if (hl) {
+            // the codec head and the sampling step in one launch: rows' CTAs first, then the head tiles
+            if (!(a->cluster == 0 && short_ok && frames == 1 && short_layout(rp, a, es, kmax)))
+                return B2S_ERR_UNSUPPORTED;
+            // the rows wait on the tiles: one wave.  Two CTAs per tile (K split over a cluster) where they fit
+            const int even_rows = (a->rows + 1) & ~1;
+            const int split = (hl->kb % 2 == 0 && even_rows + 2 * hl->tiles <= sm_count()) ? 2 : 1;
+            if (a->rows + hl->tiles > sm_count()) return B2S_ERR_UNSUPPORTED;
+            rp.head_split = split;
+            rp.head_first = split > 1 ? even_rows : a->rows;
+            rp.head_tiles = hl->tiles;
+            rp.head_kb = hl->kb;
+            rp.hidden = hl->hidden;
+            rp.hid_stride = hl->hid_stride;
+            rp.head_sync = hl->sync;
+            rp.logits = hl->logits;
+            const uint32_t smem = rp.smem_total > HEAD_SMEM ? rp.smem_total : HEAD_SMEM;
+            const bool omni = a->semantics == B2S_SEM_OMNI;
+            HeadKernel kern = head_kernel_for(omni);
+            {
+                static std::mutex mu;
+                static uint64_t done[2] = {0, 0};
+                int dev = 0;
+                e = cudaGetDevice(&dev);
+                if (e != cudaSuccess) return cuda_fail(e);
+                std::lock_guard<std::mutex> g(mu);
+                const uint64_t bit = 1ull << (dev & 63);
+                if (!(done[omni ? 1 : 0] & bit)) {
+                    e = set_smem_attr(kern, 227 * 1024);
+                    if (e != cudaSuccess) return cuda_fail(e);
+                    done[omni ? 1 : 0] |= bit;
+                }
+            }
+            cudaLaunchConfig_t cfg;
+            memset(&cfg, 0, sizeof(cfg));
+            cfg.gridDim = dim3((unsigned)(rp.head_first + split * hl->tiles), 1, 1);
+            cfg.blockDim = dim3(NT, 1, 1);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = (cudaStream_t)stream;
+            cudaLaunchAttribute attrs[2];
+            attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attrs[0].val.programmaticStreamSerializationAllowed = 1;
+            attrs[1].id = cudaLaunchAttributeClusterDimension;
+            attrs[1].val.clusterDim.x = 2;
+            attrs[1].val.clusterDim.y = 1;
+            attrs[1].val.clusterDim.z = 1;
+            cfg.attrs = attrs;
+            cfg.numAttrs = split > 1 ? 2 : 1;
+            e = cudaLaunchKernelEx(&cfg, kern, rp, hl->map);
+            if (e != cudaSuccess) return cuda_fail(e);
+            return B2S_OK;
+        }
         if (a->cluster == 0 && short_ok && short_layout(rp, a, es, kmax)) {
             // short rows: one CTA per row, the row's elements in its threads' registers (b2s_short.cu)
             const bool omni = a->semantics == B2S_SEM_OMNI;
@@ -1466,6 +1529,62 @@ int b2s_sample_frames(const b2s_sample_args* a, int32_t frames, int64_t frame_st
     if (frame_stride < (int64_t)a->rows * a->logits_row_stride) return B2S_ERR_INVALID;
     if (a->rows > 65535 * 8 || (int64_t)a->rows * frames > INT32_MAX) return B2S_ERR_UNSUPPORTED;
     return launch_sample(a, stream, nullptr, frames, frame_stride);
+}
+
+// cuTensorMapEncodeTiled from the driver, through the runtime (no link against libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
+
+int b2s_head_sample(const b2s_head_args* h, const b2s_sample_args* a, void* stream) {
+    using namespace b2s;
+    if (!h || !a || !h->hidden || !h->head || !h->logits || !h->sync) return B2S_ERR_INVALID;
+    if (a->rows < 1 || a->vocab < 1 || a->logits_dtype != B2S_DTYPE_BF16) return B2S_ERR_INVALID;
+    if (a->logits && a->logits != h->logits) return B2S_ERR_INVALID;
+    if (a->logits_row_stride < a->vocab) return B2S_ERR_INVALID;
+    if (h->hidden_dim < HEAD_KB || h->hidden_dim % HEAD_KB != 0 || h->hidden_row_stride < h->hidden_dim)
+        return B2S_ERR_INVALID;
+    // the hidden rows are read as 16-byte vectors, the head by TMA: 16-byte aligned rows; the sync words as one block
+    if (h->hidden_row_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(h->hidden) & 15) != 0 ||
+        (reinterpret_cast<uintptr_t>(h->head) & 15) != 0 || (reinterpret_cast<uintptr_t>(h->sync) & 15) != 0)
+        return B2S_ERR_INVALID;
+    if (a->rows > HEAD_N || h->hidden_dim > HEAD_MAX_KB * HEAD_KB) return B2S_ERR_UNSUPPORTED;
+    HeadLaunch hl;
+    memset(&hl, 0, sizeof(hl));
+    hl.tiles = (a->vocab + HEAD_M - 1) / HEAD_M;
+    hl.kb = h->hidden_dim / HEAD_KB;
+    hl.hidden = h->hidden;
+    hl.hid_stride = h->hidden_row_stride;
+    hl.sync = h->sync;
+    hl.logits = h->logits;
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return cuda_fail(cudaErrorNotSupported);
+    // head [vocab, hidden_dim] bf16, rows hidden_dim elements apart; boxes of [128 ids x 64] in the 128-byte
+    // swizzle (the MMA's K-major operand layout); ids past the vocabulary read as zero
+    const cuuint64_t dims[2] = {(cuuint64_t)h->hidden_dim, (cuuint64_t)a->vocab};
+    const cuuint64_t strides[1] = {(cuuint64_t)h->hidden_dim * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)HEAD_KB, (cuuint32_t)HEAD_M};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&hl.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(h->head), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return B2S_ERR_INVALID;
+    b2s_sample_args a2 = *a;
+    a2.logits = h->logits;
+    return launch_sample(&a2, stream, nullptr, 1, 0, &hl);
 }
 
 int b2s_shard_candidates(const b2s_sample_args* a, int64_t vocab_offset, int32_t cap, float* cand_values,

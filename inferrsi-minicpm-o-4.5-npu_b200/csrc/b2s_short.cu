@@ -31,6 +31,7 @@
 // waits on nothing but its own loads and block barriers.
 #include <type_traits>
 
+#include "b2s_head.cuh"
 #include "b2s_rowpaths.cuh"
 
 namespace b2s {
@@ -71,9 +72,10 @@ static __device__ __noinline__ int64_t short_exact(const Params p, Row<E> R, His
     return exact_token<E>(R, k, hf, lse, top_p, p.min_keep, topk_only, drop, u, hist, vals, ctl);
 }
 
-template <typename E, int SEM>
-__global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
-    extern __shared__ __align__(128) unsigned char smem[];
+// One row per CTA (blockIdx.x).  HEAD: the row's logits are written by the codec-head CTAs of the same launch
+// (b2s_head.cuh); the row waits for them after its history loads and reads them with coherent loads.
+template <typename E, int SEM, bool HEAD>
+__device__ __forceinline__ void short_rows(const Params& p, unsigned char* smem) {
     constexpr int EPV = Elem<E>::EPV, ES = Elem<E>::SZ, SV = SHORT_EPT / EPV;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r = (int)blockIdx.x;
@@ -125,17 +127,39 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
         R.gvec = reinterpret_cast<const uint4*>(ace);
         R.e0 = R.nh;
     }
-    uint4 q[SV + 1];  // interior vectors tid + s * NT, then (threads 0 / 1) the head / tail as one more vector
-#pragma unroll
-    for (int s = 0; s < SV; ++s) {
-        const int v = tid + s * NT;
-        q[s] = v < R.nvec ? ldg_stream(R.gvec + v) : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
-    }
     const int64_t* hrow = p.hist ? p.hist + (int64_t)r * p.hstride : nullptr;
     const bool hthread = hrow != nullptr && tid < p.W;  // W <= 255 < NT: one history position per thread
     const int64_t hv = hthread ? hrow[tid] : -1;
     if (hrow && p.W > 0 && p.alpha)
         for (int j = tid; j < p.alpha_len; j += NT) cp_async4(&atab[j], p.alpha + (int64_t)r * p.alpha_stride + j);
+    bool head_ok = true;
+    if constexpr (HEAD) {
+        // the codec-head tiles publish their logits with a release increment; the last row to see them all
+        // zeroes the control words for the next launch (which touches them only after this one has completed)
+        if (tid == 0) {
+            const bool seen = wait_geq_acquire(p.head_sync + HS_TILES, (uint32_t)p.head_tiles, HEAD_WAIT_NS);
+            const bool ok = seen && ld_acquire_u32(p.head_sync + HS_ERR) == 0u;
+            if (!ok) set_status(p, B2S_STATUS_WAIT_TIMEOUT);
+            ctl->head_ok = ok ? 1 : 0;
+            if (atomicAdd(p.head_sync + HS_ROWS, 1u) == (uint32_t)p.rows - 1u) {
+                p.head_sync[HS_TILES] = 0u;
+                p.head_sync[HS_ERR] = 0u;
+                p.head_sync[HS_ROWS] = 0u;
+            }
+        }
+        __syncthreads();
+        head_ok = ctl->head_ok != 0;
+    }
+    uint4 q[SV + 1];  // interior vectors tid + s * NT, then (threads 0 / 1) the head / tail as one more vector
+#pragma unroll
+    for (int s = 0; s < SV; ++s) {
+        const int v = tid + s * NT;
+        if constexpr (HEAD)
+            q[s] = v < R.nvec ? ld_stream_coherent(R.gvec + v)
+                              : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
+        else
+            q[s] = v < R.nvec ? ldg_stream(R.gvec + v) : make_uint4(Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG, Elem<E>::NEG);
+    }
     const int i_end = R.e0 + R.nvec * EPV;
     const int x0 = tid == 0 ? 0 : i_end;                       // first element of the edge slot
     const int nx = tid == 0 ? R.nh : tid == 1 ? V - i_end : 0;  // < EPV
@@ -158,6 +182,7 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     else if (step >= max_new - 1) mode = MODE_FORCED;
     else if (hf && step <= 0) mode = MODE_FULL;
     else mode = MODE_FILTER;
+    if (!head_ok && mode != MODE_SKIP) mode = MODE_FAIL;  // the head tiles did not all complete: PAD
     int k = 0;
     if (mode == MODE_FILTER) {
         k = min(max(top_k, max(p.min_keep, 1)), V);
@@ -501,6 +526,31 @@ __global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
     }
     }  // frames
 }
+
+template <typename E, int SEM>
+__global__ void __launch_bounds__(NT, 1) short_kernel(const Params p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    short_rows<E, SEM, false>(p, smem);
+}
+
+// The codec head and the sampling step in one launch: CTAs [0, rows) take the rows (above), CTAs
+// [head_first, head_first + head_split * head_tiles) the vocabulary tiles of the head (b2s_head.cuh), one or two
+// (a cluster splitting K) per tile.
+template <int SEM>
+__global__ void __launch_bounds__(NT, 1) head_kernel(const Params p, const __grid_constant__ CUtensorMap amap) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    if ((int)blockIdx.x >= p.rows) {
+        if ((int)blockIdx.x < p.head_first) return;  // the pad CTA of an odd row count (clusters of two)
+        const int tt = (int)blockIdx.x - p.head_first;
+        head_tile(tt / p.head_split, p.head_split, p.head_split > 1 ? (int)cluster_ctarank() : 0, p.rows, p.V,
+                  p.head_kb, p.hidden, p.hid_stride, static_cast<uint16_t*>(const_cast<void*>(p.logits)), p.lstride,
+                  p.head_sync, p.status, &amap, smem);
+        return;
+    }
+    short_rows<__nv_bfloat16, SEM, true>(p, smem);
+}
+
+HeadKernel head_kernel_for(bool omni) { return omni ? head_kernel<B2S_SEM_OMNI> : head_kernel<-1>; }
 
 ResKernel short_kernel_for(bool bf16, bool omni) {
     static const ResKernel k[2][2] = {

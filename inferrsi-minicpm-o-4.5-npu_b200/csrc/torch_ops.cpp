@@ -195,6 +195,56 @@ Tensor sample_state_cuda(const Tensor& logits, Tensor& history, Tensor& steps, T
     return tokens;
 }
 
+// The Talker codec head and the step in one launch: logits = bf16(hidden @ head^T) written to `logits` (bf16
+// [B, V], an output kept for inspection), then the step on them; history / steps / finished advance in place.
+// `sync`: 4 int32 words, zero before the first call, one per stream.
+Tensor head_sample_state_cuda(const Tensor& hidden, const Tensor& head, Tensor& logits, Tensor& sync, Tensor& history,
+                              Tensor& steps, Tensor& finished, const optional<Tensor>& seeds,
+                              const optional<Tensor>& uniform_values, const optional<Tensor>& active,
+                              const optional<Tensor>& alpha, const optional<Tensor>& status,
+                              const optional<Tensor>& row_temperature, const optional<Tensor>& row_top_p,
+                              const optional<Tensor>& row_top_k, double temperature, double top_p, int64_t top_k,
+                              int64_t min_keep, int64_t min_new, int64_t max_new, int64_t eos, int64_t semantics,
+                              int64_t rng, int64_t max_top_k) {
+    c10::cuda::CUDAGuard guard(logits.device());
+    TORCH_CHECK(hidden.is_cuda() && head.is_cuda() && sync.is_cuda() && hidden.device() == logits.device() &&
+                    head.device() == logits.device() && sync.device() == logits.device(),
+                "hidden, head, logits and sync must be on one CUDA device");
+    TORCH_CHECK(hidden.scalar_type() == at::kBFloat16 && head.scalar_type() == at::kBFloat16 &&
+                    logits.scalar_type() == at::kBFloat16,
+                "hidden, head and logits must be bfloat16");
+    TORCH_CHECK(hidden.dim() == 2 && hidden.stride(1) == 1, "hidden must be [rows, hidden_dim] with contiguous rows");
+    TORCH_CHECK(head.dim() == 2 && head.is_contiguous() && head.size(1) == hidden.size(1),
+                "head must be contiguous [vocab, hidden_dim]");
+    TORCH_CHECK(logits.dim() == 2 && logits.size(0) == hidden.size(0) && logits.size(1) == head.size(0),
+                "logits must be [rows, vocab]");
+    TORCH_CHECK(sync.scalar_type() == at::kInt && sync.numel() == 4 && sync.is_contiguous(),
+                "sync must be 4 contiguous int32 words");
+    TORCH_CHECK(steps.is_contiguous() && finished.is_contiguous() && history.is_contiguous(),
+                "state tensors must be contiguous");
+    TORCH_CHECK(finished.scalar_type() == at::kBool, "finished must be bool");
+    b2s_sample_args a;
+    fill_args(a, logits, history, steps, seeds, c10::nullopt, uniform_values, active, finished, row_temperature,
+              row_top_p, row_top_k, alpha, status, temperature, top_p, top_k, min_keep, min_new, max_new, 0.0, 0.0, eos,
+              semantics, rng, max_top_k, 0, 0);
+    Tensor tokens = at::empty({logits.size(0)}, logits.options().dtype(at::kLong));
+    a.tokens = tokens.data_ptr<int64_t>();
+    a.history_out = history.numel() ? history.data_ptr<int64_t>() : nullptr;
+    a.history_out_row_stride = history.dim() == 2 ? history.size(1) : 0;
+    a.steps_out = steps.data_ptr<int64_t>();
+    a.finished_out = reinterpret_cast<uint8_t*>(finished.data_ptr<bool>());
+    b2s_head_args h;
+    memset(&h, 0, sizeof(h));
+    h.hidden = hidden.data_ptr();
+    h.hidden_row_stride = hidden.size(0) > 1 ? hidden.stride(0) : hidden.size(1);
+    h.head = head.data_ptr();
+    h.hidden_dim = (int32_t)hidden.size(1);
+    h.logits = logits.data_ptr();
+    h.sync = reinterpret_cast<uint32_t*>(sync.data_ptr<int32_t>());
+    check_rc(b2s_head_sample(&h, &a, at::cuda::getCurrentCUDAStream().stream()), "b2s_head_sample");
+    return tokens;
+}
+
 // K frames in one launch: logits_k [K, B, V]; history / steps / finished advance in place over the frames.
 Tensor sample_frames_cuda(const Tensor& logits_k, Tensor& history, Tensor& steps, Tensor& finished,
                           const optional<Tensor>& seeds, const optional<Tensor>& uniform_values,
@@ -246,6 +296,14 @@ Tensor sample_state_meta(const Tensor& logits, Tensor&, Tensor&, Tensor&, const 
                          const optional<Tensor>&, double, double, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
                          int64_t, int64_t, int64_t, int64_t) {
     return at::empty({logits.size(0)}, logits.options().dtype(at::kLong));
+}
+
+Tensor head_sample_state_meta(const Tensor& hidden, const Tensor&, Tensor&, Tensor&, Tensor&, Tensor&, Tensor&,
+                              const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
+                              const optional<Tensor>&, const optional<Tensor>&, const optional<Tensor>&,
+                              const optional<Tensor>&, const optional<Tensor>&, double, double, int64_t, int64_t,
+                              int64_t, int64_t, int64_t, int64_t, int64_t, int64_t) {
+    return at::empty({hidden.size(0)}, hidden.options().dtype(at::kLong));
 }
 
 Tensor argmax_cuda(const Tensor& logits) {
@@ -444,6 +502,12 @@ TORCH_LIBRARY(minicpmo_sampler, m) {
         "Tensor? uniform_values, Tensor? active, Tensor? alpha, Tensor? status, Tensor? row_temperature, "
         "Tensor? row_top_p, Tensor? row_top_k, float temperature, float top_p, int top_k, int min_keep, "
         "int min_new_tokens, int max_new_tokens, int eos, int semantics, int rng, int max_top_k) -> Tensor tokens");
+    m.def(
+        "head_sample_state_(Tensor hidden, Tensor head, Tensor(a!) logits, Tensor(b!) sync, Tensor(c!) history, "
+        "Tensor(d!) steps, Tensor(e!) finished, Tensor? seeds, Tensor? uniform_values, Tensor? active, Tensor? alpha, "
+        "Tensor? status, Tensor? row_temperature, Tensor? row_top_p, Tensor? row_top_k, float temperature, "
+        "float top_p, int top_k, int min_keep, int min_new_tokens, int max_new_tokens, int eos, int semantics, "
+        "int rng, int max_top_k) -> Tensor tokens");
     m.def("argmax(Tensor logits) -> Tensor");
     m.def("uniform(Tensor seeds, Tensor steps, Tensor? requests, int rng) -> Tensor");
     m.def("repetition_penalty(Tensor x, Tensor history, Tensor alpha) -> Tensor");
@@ -466,6 +530,7 @@ TORCH_LIBRARY_IMPL(minicpmo_sampler, CUDA, m) {
     m.impl("sample", &sample_cuda);
     m.impl("sample_state_", &sample_state_cuda);
     m.impl("sample_frames_", &sample_frames_cuda);
+    m.impl("head_sample_state_", &head_sample_state_cuda);
     m.impl("argmax", &argmax_cuda);
     m.impl("uniform", &uniform_cuda);
     m.impl("repetition_penalty", &penalty_cuda);
@@ -478,6 +543,7 @@ TORCH_LIBRARY_IMPL(minicpmo_sampler, Meta, m) {
     m.impl("sample", &sample_meta);
     m.impl("sample_state_", &sample_state_meta);
     m.impl("sample_frames_", &sample_frames_meta);
+    m.impl("head_sample_state_", &head_sample_state_meta);
     m.impl("argmax", &argmax_meta);
     m.impl("uniform", &uniform_meta);
     m.impl("repetition_penalty", &penalty_meta);

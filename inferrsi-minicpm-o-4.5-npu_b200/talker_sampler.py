@@ -407,6 +407,56 @@ def step_(state: DecodeState, logits: torch.Tensor, eos: int, cfg: TalkerSamplin
         int(cfg.min_new_tokens), int(cfg.max_new_tokens), int(eos), int(kw["semantics"]), r, int(kw["max_top_k"]), 0)
 
 
+class CodecHead:
+    """The Talker's codec head and the decode step in ONE launch: ``F.linear(hidden, head)`` on the tensor cores
+    (bf16 operands, fp32 accumulation, logits rounded to bf16 like F.linear's bf16 output), then ``step_`` on
+    those logits -- the graph body of ``engine/runtime/talker_post_graph.py:56-76`` (``F.linear(st["hidden"],
+    self.head).float()``, ``processed_logits``, ``draw``, the state update) and the head + sampler of
+    ``engine/runtime/talker_decode.py:120-128``.
+
+    Holds the head (``[vocab, hidden]`` bf16, as ``engine/models/talker.py:106-109`` builds it), the ``[rows,
+    vocab]`` bf16 logits buffer the launch writes (kept for inspection: ``self.logits``) and 4 int32 control words
+    (``self.sync``).  One instance per stream: launches that share the control words must not overlap.  The head
+    is read while the stream's previous kernel may still run, so that kernel must not write it.  Limits: rows <= 16,
+    hidden a multiple of 64 up to 768."""
+
+    def __init__(self, head: torch.Tensor, rows: int):
+        _need_cuda(head)
+        if head.dtype != torch.bfloat16 or head.dim() != 2:
+            raise ValueError("head must be a bf16 [vocab, hidden] tensor")
+        self.head = head.contiguous()
+        self.rows = int(rows)
+        self.logits = torch.empty(self.rows, head.shape[0], dtype=torch.bfloat16, device=head.device)
+        self.sync = torch.zeros(4, dtype=torch.int32, device=head.device)
+
+    def step_(self, state: DecodeState, hidden: torch.Tensor, eos: int, cfg: TalkerSampling = TalkerSampling(), *,
+              uniform_values: Optional[torch.Tensor] = None, status: Optional[torch.Tensor] = None,
+              row_params: Optional[RowParams] = None, rng: str = "counter") -> torch.Tensor:
+        """One frame per row from ``hidden`` ([rows, hidden] bf16): advances ``state`` IN PLACE like ``step_``
+        and returns the [rows] tokens (PAD for rows that are not live).  ``rng``: ``counter`` (reference hash)
+        or ``philox``; ignored when ``uniform_values`` is given."""
+        _need_cuda(hidden, state.history, state.steps)
+        if hidden.dim() != 2 or hidden.shape[0] != self.rows or hidden.dtype != torch.bfloat16:
+            raise ValueError(f"hidden must be bf16 [{self.rows}, hidden]")
+        if cfg.uses_native_rng:
+            raise ValueError("CodecHead.step_ needs the counter / Philox RNG or injected uniforms")
+        rp = row_params
+        if rp is not None and (rp.min_new_tokens is not None or rp.max_new_tokens is not None):
+            raise ValueError("CodecHead.step_ takes per-row temperature / top_p / top_k / penalty only")
+        kw = _cfg_kwargs(cfg, state.history, hidden.device, rp)
+        if uniform_values is not None:
+            r = RNG_UNIFORM
+            uniform_values = uniform_values.to(torch.float32).contiguous()
+        else:
+            r = {"counter": RNG_COUNTER, "philox": RNG_PHILOX}[rng]
+        return _native.ops().head_sample_state_(
+            hidden, self.head, self.logits, self.sync, state.history, state.steps, state.finished, state.seeds,
+            uniform_values, state.active, kw["alpha"], status, None if rp is None else rp.temperature,
+            None if rp is None else rp.top_p, None if rp is None else rp.top_k, kw["temperature"], float(cfg.top_p),
+            int(cfg.top_k), int(kw["min_keep"]), int(cfg.min_new_tokens), int(cfg.max_new_tokens), int(eos),
+            int(kw["semantics"]), r, int(kw["max_top_k"]))
+
+
 FLAG_TOPK_ONLY = 2
 
 
