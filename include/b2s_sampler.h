@@ -165,6 +165,27 @@ typedef struct b2s_head_args {
 int b2s_head_sample(const b2s_head_args* head, const b2s_sample_args* args, void* stream);
 
 /*
+ * b2s_head_sample for callers that cannot allocate device memory: no counterpart in the reference, whose
+ * callers allocate through torch.  Some hosts of this library cannot call cudaMalloc on this path -- an embedding
+ * whose device allocator is fixed at start-up, a runtime that hands the library only the buffers it owns, or a
+ * decode loop that must not call cudaMalloc / cudaFree (which can synchronise the device) while other work is in
+ * flight.  The caller passes the inputs and outputs as for b2s_head_sample (args->logits must be NULL; the dtype
+ * and row stride of the logits are set here); the logits rows and the control words live in one fixed device
+ * array of B2S_NOALLOC_SCRATCH_BYTES inside the library, held on every GPU that uses it until the process exits.
+ * Allocates nothing and calls no allocating routine.  Limits: rows <= B2S_NOALLOC_MAX_ROWS and vocab <=
+ * B2S_NOALLOC_MAX_VOCAB, else B2S_ERR_UNSUPPORTED before anything is launched; the other limits of
+ * b2s_head_sample apply.  Each call clears the control words on `stream` (cudaMemsetAsync) before its launch.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress): make that first call
+ * before any stream capture.  Every call on a device shares the one array, which keeps the last call's contents:
+ * calls that overlap on the GPU (other streams, other threads) race and must be serialised by the caller.
+ */
+#define B2S_NOALLOC_MAX_ROWS 16
+#define B2S_NOALLOC_MAX_VOCAB 8192
+#define B2S_NOALLOC_SCRATCH_BYTES (B2S_NOALLOC_MAX_ROWS * B2S_NOALLOC_MAX_VOCAB * 2 + 256)
+int b2s_head_sample_noalloc(const void* hidden, int64_t hidden_row_stride, const void* head, int32_t hidden_dim,
+                            const b2s_sample_args* args, void* stream);
+
+/*
  * Greedy next token: argmax over each row (first index among equal maxima, NaN wins).
  * Replaces the Thinker sampling step F.linear(h, lm_head).float().argmax(-1) at
  * engine/runtime/thinker_decode.py:83,107, engine/runtime/backend_s.py:893,

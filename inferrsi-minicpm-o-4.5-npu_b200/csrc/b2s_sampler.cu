@@ -1587,6 +1587,63 @@ int b2s_head_sample(const b2s_head_args* h, const b2s_sample_args* a, void* stre
     return launch_sample(&a2, stream, nullptr, 1, 0, &hl);
 }
 
+// ---------------------------------------------------------------- the codec head without caller scratch
+// b2s_head_sample needs two device buffers beyond its inputs and outputs: the bf16 logits rows that the head's
+// tiles hand to the rows, and four control words.  A caller that cannot allocate device memory -- an embedding
+// whose allocator is fixed at start-up, a host runtime that passes in only the buffers it owns (weights, hidden
+// rows, decode state, tokens), or a decode loop that must not call cudaMalloc / cudaFree, which can synchronise
+// the device, while other work is in flight -- uses this variant instead.  Its scratch is one file-scope device
+// array of a fixed size, which every process that loads this library holds on every GPU it uses until it exits.
+// Host code must not use the array's name as a device address: it is a host-side stand-in, so the device address
+// is looked up once per device (cudaGetSymbolAddress, with that device current) and passed to the kernel.
+static __device__ __align__(256) unsigned char g_head_scratch[B2S_NOALLOC_SCRATCH_BYTES];
+static_assert(B2S_NOALLOC_SCRATCH_BYTES == B2S_NOALLOC_MAX_ROWS * B2S_NOALLOC_MAX_VOCAB * 2 + 256,
+              "the scratch holds the bf16 logits rows, then the control words");
+
+static int head_scratch_address(unsigned char** out) {
+    static std::mutex mu;
+    static unsigned char* addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev < 0 || dev >= 64) return B2S_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> g(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_head_scratch);
+        if (e != cudaSuccess) return cuda_fail(e);
+        addr[dev] = static_cast<unsigned char*>(p);
+    }
+    *out = addr[dev];
+    return B2S_OK;
+}
+
+int b2s_head_sample_noalloc(const void* hidden, int64_t hidden_row_stride, const void* head, int32_t hidden_dim,
+                            const b2s_sample_args* a, void* stream) {
+    if (!a || a->logits) return B2S_ERR_INVALID;  // the logits live in the library's scratch
+    if (a->rows > B2S_NOALLOC_MAX_ROWS || a->vocab > B2S_NOALLOC_MAX_VOCAB) return B2S_ERR_UNSUPPORTED;
+    unsigned char* scratch = nullptr;
+    int rc = head_scratch_address(&scratch);
+    if (rc != B2S_OK) return rc;
+    // the control words start at zero (a completed launch leaves them so; one that gave up may not)
+    uint32_t* sync = reinterpret_cast<uint32_t*>(scratch + (size_t)B2S_NOALLOC_MAX_ROWS * B2S_NOALLOC_MAX_VOCAB * 2);
+    cudaError_t e = cudaMemsetAsync(sync, 0, 4 * sizeof(uint32_t), (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e);
+    b2s_head_args h;
+    memset(&h, 0, sizeof(h));
+    h.hidden = hidden;
+    h.hidden_row_stride = hidden_row_stride;
+    h.head = head;
+    h.hidden_dim = hidden_dim;
+    h.logits = scratch;
+    h.sync = sync;
+    b2s_sample_args a2 = *a;
+    a2.logits = nullptr;
+    a2.logits_dtype = B2S_DTYPE_BF16;
+    a2.logits_row_stride = a->vocab;
+    return b2s_head_sample(&h, &a2, stream);
+}
+
 int b2s_shard_candidates(const b2s_sample_args* a, int64_t vocab_offset, int32_t cap, float* cand_values,
                          int32_t* cand_ids, int32_t* cand_count, void* stream) {
     if (!a || !cand_values || !cand_ids || !cand_count || cap < 1 || vocab_offset < 0) return B2S_ERR_INVALID;
