@@ -555,6 +555,12 @@ def run_head(args, w, rank: int, world: int, local: int):
     ch = ts.CodecHead(heads[0], B)
 
     def one_step(i):
+        if args.path == "unfused":  # the same step as two launches: torch's F.linear (cuBLAS), then the sampler
+            lg = torch.nn.functional.linear(hiddens[i % nbuf], heads[i % nbuf])
+            return ops.sample_state_(lg, state.history, state.steps, state.finished, state.seeds, None, state.active,
+                                     kw["alpha"], None, rp.temperature, rp.top_p, rp.top_k, kw["temperature"],
+                                     cfg.top_p, cfg.top_k, kw["min_keep"], cfg.min_new_tokens, cfg.max_new_tokens,
+                                     eos, kw["semantics"], ts.RNG_PHILOX, kw["max_top_k"], 0, 0)
         return ops.head_sample_state_(hiddens[i % nbuf], heads[i % nbuf], ch.logits, ch.sync, state.history,
                                       state.steps, state.finished, state.seeds, None, state.active, kw["alpha"], None,
                                       rp.temperature, rp.top_p, rp.top_k, kw["temperature"], cfg.top_p, cfg.top_k,
@@ -705,9 +711,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--eager", action="store_true", help="time plain launches instead of CUDA graphs (profiling)")
-    ap.add_argument("--path", default="auto", choices=["auto", "stream", "resident"],
+    ap.add_argument("--path", default="auto", choices=["auto", "stream", "resident", "unfused"],
                     help="sampling kernel: the launcher's choice (short-row kernel for rows of <= 8192 elements, "
-                         "else row-resident), the streaming kernel, or the row-resident kernel")
+                         "else row-resident), the streaming kernel, or the row-resident kernel; talker_head: "
+                         "'unfused' times torch's F.linear followed by the sampler (two launches per step)")
     ap.add_argument("--cluster", type=int, default=0, help="CTAs per row of the row-resident kernel (0: auto)")
     ap.add_argument("--strong", action="store_true",
                     help="split the workload's batch over the ranks (strong scaling) instead of B rows per rank")

@@ -28,7 +28,8 @@
 // epilogue.  A row the list cannot serve (NaN, an unusable tau, more candidates
 // than the list holds) builds the history structures and takes the exact full-row path; hf frame-0 rows take
 // the ordered scan: both shared with the row-resident kernel (b2s_rowpaths.cuh) and out of line.  The kernel
-// waits on nothing but its own loads and block barriers.
+// waits on nothing but its own loads and block barriers -- except in head_kernel (below), where the rows' CTAs
+// wait (bounded) for the codec-head tiles of the same launch to publish their logits.
 #include <type_traits>
 
 #include "b2s_head.cuh"
