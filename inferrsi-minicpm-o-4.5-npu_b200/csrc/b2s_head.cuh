@@ -109,14 +109,22 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
 __device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Waits until *p >= target (acquire), for at most limit_ns; false on timeout.
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Waits until *p >= target, for at most limit_ns (false on timeout): relaxed polls, then one acquire fence, so
+// that this thread's later reads see what the releasing threads wrote before their increments.
 __device__ __forceinline__ bool wait_geq_acquire(const uint32_t* p, uint32_t target, uint64_t limit_ns) {
-    if (ld_acquire_u32(p) >= target) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
 #pragma unroll 1
         for (int i = 0; i < 32; ++i)
-            if (ld_acquire_u32(p) >= target) return true;
+            if (ld_relaxed_u32(p) >= target) {
+                asm volatile("fence.acq_rel.gpu;" ::: "memory");
+                return true;
+            }
         if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
@@ -296,10 +304,9 @@ __device__ __forceinline__ void head_tile(int tile, int split, int rank, int row
                             __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[n])));
             }
             if (!good && lane == 0) atomicOr(&sync[HS_ERR], 1u);
-            named_bar_sync(1, 128);  // every store of the tile precedes thread 0's release below
+            named_bar_sync(1, 128);  // every store of the tile precedes thread 0's release below (cumulative)
             if (tid == 0) {
                 if (!good && status) atomicOr(status, B2S_STATUS_WAIT_TIMEOUT);
-                __threadfence();
                 red_release_add(&sync[HS_TILES], 1u);
             }
         }
