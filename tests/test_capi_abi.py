@@ -49,6 +49,39 @@ def test_host_only_calls(pkg):
     assert b"unknown" in lib.b2s_error_string(-12345).lower() or len(lib.b2s_error_string(-12345)) > 0
 
 
+def test_head_entry_points_check_arguments_on_the_host(pkg):
+    """The codec-head entry points refuse what they cannot take before touching the device (no GPU needed):
+    fake, 16-byte aligned addresses stand in for the buffers."""
+    import ctypes
+
+    lib = pkg._native.capi()
+    nat = pkg._native
+    fake = [ctypes.c_void_p(0x10000 * (i + 1)) for i in range(8)]
+
+    def args(rows=8, vocab=6562, logits=None, dtype=1):
+        a = nat.SampleArgs()
+        a.logits, a.logits_dtype, a.rows, a.vocab, a.logits_row_stride = logits, dtype, rows, vocab, vocab
+        a.steps, a.tokens, a.seeds, a.rng, a.temperature, a.top_k, a.min_keep = fake[4], fake[5], fake[6], 1, 1.0, 1, 1
+        return a
+
+    def head(hidden_dim=768, stride=768, hidden=fake[0]):
+        return nat.HeadArgs(hidden=hidden.value, hidden_row_stride=stride, head=fake[1].value, hidden_dim=hidden_dim,
+                            logits=fake[2].value, sync=fake[3].value)
+
+    call = lambda h, a: lib.b2s_head_sample(ctypes.byref(h), ctypes.byref(a), None)
+    assert call(head(), args(rows=17)) == 2            # more rows than one MMA's N: unsupported
+    assert call(head(hidden_dim=832, stride=832), args()) == 2  # more K than the tile's shared memory holds
+    assert call(head(hidden_dim=100, stride=100), args()) == 1  # K not a multiple of 64
+    assert call(head(stride=770), args()) == 1          # hidden rows not 16-byte aligned
+    assert call(head(hidden=ctypes.c_void_p(0x10008)), args()) == 1  # hidden not 16-byte aligned
+    assert call(head(), args(dtype=0)) == 1             # the head's logits are bf16
+    assert call(head(), args(logits=fake[7])) == 1      # args->logits must be NULL or the head's logits
+    noalloc = lambda a: lib.b2s_head_sample_noalloc(fake[0], 768, fake[1], 768, ctypes.byref(a), None)
+    assert noalloc(args(vocab=8193)) == 2                # beyond the library's scratch
+    assert noalloc(args(rows=17)) == 2
+    assert noalloc(args(logits=fake[7])) == 1           # the logits live in the library's scratch
+
+
 def test_sample_args_layout_matches_c(pkg, tmp_path):
     """Offsets of every field of b2s_sample_args as gcc lays them out == the ctypes mirror's."""
     fields = _struct_fields()
