@@ -60,6 +60,10 @@ WORKLOADS = {
     # candidates, one NCCL all-gather, the merged draw on every rank.  Tie-heavy bf16 logits (multiples of 1/16)
     "vocab_shard": dict(rows=256, vocab=151_936, dtype="bf16", window=0, temperature=0.8, top_k=64, top_p=0.9,
                         penalty=1.0, op="vocab_shard"),
+    # the Thinker greedy step from its LM head (hidden 4096, a 151,936 x 4096 bf16 head): the GEMM and the argmax in
+    # one launch, the logits never written (thinker_decode.py:83,107)
+    "greedy_head": dict(rows=64, vocab=151_936, dtype="bf16", window=0, temperature=0.0, top_k=1, top_p=1.0,
+                        penalty=1.0, hidden=4096, op="lmhead"),
     # the Thinker greedy step (argmax over the head's logits, first index on ties) on the thinker shape
     "greedy": dict(rows=64, vocab=151_936, dtype="bf16", window=0, temperature=0.0, top_k=1, top_p=1.0, penalty=1.0,
                    op="argmax"),
@@ -73,6 +77,8 @@ def bytes_per_row(w) -> float:
     (which stay on chip and in L2)."""
     if w.get("op") == "head":
         return w["vocab"] * w["hidden"] * 2 / w["rows"] + 2 * w["hidden"] + 4 * w["window"] + 40
+    if w.get("op") == "lmhead":
+        return w["vocab"] * w["hidden"] * 2 / w["rows"] + 2 * w["hidden"] + 8
     e = 2 if w["dtype"] == "bf16" else 4
     return w["vocab"] * e + 4 * w["window"] + 40
 
@@ -185,7 +191,8 @@ def measured_peak_gbs():
 def profiled_traffic(workload: str, w, path: str = "auto") -> float | None:
     """DRAM bytes per launch of the workload's kernel from the committed ncu summary, or None (the summary of the
     kernel the launcher picks for the workload first: short-row, row-resident, then streaming)."""
-    kernels = ["argmax_kernel"] if w.get("op") == "argmax" else ["head_kernel"] if w.get("op") == "head" else (
+    kernels = ["argmax_kernel"] if w.get("op") == "argmax" else ["head_kernel"] if w.get("op") == "head" else \
+        ["lmhead_argmax_kernel"] if w.get("op") == "lmhead" else (
         ["sample_kernel"] if path == "stream" else ["resident_kernel"] if path == "resident" else
         ["short_kernel", "resident_kernel", "sample_kernel"])
     for kernel in kernels:
@@ -324,6 +331,10 @@ def metric_of(w) -> str:
     if w.get("op") == "vocab_shard":
         return (f"sampled rows/s at B={w['rows']} x V={w['vocab']} over the job's vocabulary shards "
                 "(per-shard candidates + NCCL all-gather + merged draw)")
+    if w.get("op") == "lmhead":
+        return (f"greedy rows/s from the LM head, whole job (n_gpus x B={w['rows']} rows per GPU) at V={w['vocab']}, "
+                f"hidden {w['hidden']}; per GPU = value_per_gpu (bf16 LM-head GEMM on the tensor cores + argmax, one "
+                "launch and a finishing block, logits never written)")
     if w.get("op") == "head":
         return (f"sampled rows/s from the codec head, whole job (n_gpus x B={w['rows']} rows per GPU) at "
                 f"V={w['vocab']}, hidden {w['hidden']}; per GPU = value_per_gpu (bf16 head GEMM on the tensor cores "
@@ -341,6 +352,8 @@ def dtype_of(w) -> str:
 
 def rotating_buffers(w) -> int:
     """Distinct logits buffers (heads, for the codec head): one sweep exceeds twice the L2 and 640 MiB."""
+    if w.get("op") == "lmhead":
+        return 1  # one head already exceeds the L2
     buf = (w["vocab"] * w["hidden"] * 2 if w.get("op") == "head" else
            w["rows"] * w["vocab"] * (2 if w["dtype"] == "bf16" else 4))
     return max(2, min(8192, math.ceil(max(2 * L2_BYTES, 640 * 2**20) / buf)))
@@ -358,7 +371,8 @@ def config_of(args, w, world: int) -> dict:
             "min_keep": w.get("min_keep", 1), "eos": w.get("eos", -1), "min_new_tokens": w.get("min_new", 0),
             "per_row": {k: list(w[k]) for k in ("row_temperature", "row_top_k", "row_top_p") if k in w} or None,
             "parallelism": f"rows x{world}",
-            "l2": (f"{nbuf} rotating heads ({nbuf * V * w['hidden'] * 2 / 2**20:.0f} MiB > L2)" if w.get("op") == "head"
+            "l2": (f"{nbuf} rotating heads ({nbuf * V * w['hidden'] * 2 / 2**20:.0f} MiB > L2)"
+                   if w.get("op") in ("head", "lmhead")
                    else f"{nbuf} rotating logits buffers "
                         f"({nbuf * B * V * (2 if w['dtype'] == 'bf16' else 4) / 2**20:.0f} MiB > L2)"),
             "hidden": w.get("hidden"),
@@ -637,6 +651,108 @@ def run_head(args, w, rank: int, world: int, local: int):
     print(json.dumps(line))
 
 
+def run_lmhead(args, w, rank: int, world: int, local: int):
+    """The Thinker's greedy step from its LM head (``thinker_sampler.LMHeadArgmax``): each step reads the whole
+    1.24 GB head (larger than the L2) and a rotating set of hidden rows."""
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    pkg = __graft_entry__.load_package()
+    lm = pkg.thinker_sampler
+    B, V, Hd = w["rows"], w["vocab"], w["hidden"]
+    g = torch.Generator(device=dev).manual_seed(rank)
+    head = (torch.randn(V, Hd, device=dev, generator=g) * (2.0 / Hd ** 0.5)).to(torch.bfloat16)
+    hiddens = [torch.randn(B, Hd, device=dev, generator=g).to(torch.bfloat16) for _ in range(16)]
+    op = lm.LMHeadArgmax(head, B)
+    ops = pkg._native.ops()
+
+    def one_step(i):
+        if args.path == "unfused":  # torch's F.linear (cuBLAS, bf16 logits written), then the argmax kernel
+            return ops.argmax(torch.nn.functional.linear(hiddens[i % 16], head))
+        return ops.lmhead_argmax(hiddens[i % 16], head, op.keys, None)
+
+    ms, ck, graphs = time_steps(args, one_step, dev, local, world)
+    ms_per_step = ms / args.steps
+    value = B * world * args.steps / (ms / 1e3)
+    step_bytes = V * Hd * 2 + B * (2 * Hd + 8)
+    achieved = step_bytes / (ms_per_step / 1e3) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    host = hiddens[0].cpu().contiguous().pin_memory()
+    dbuf = torch.empty_like(host, device=dev)
+    tok_h = torch.empty(B, dtype=torch.int64).pin_memory()
+    e2e_steps = max(1, args.e2e_steps)
+
+    def api_step():
+        dbuf.copy_(host, non_blocking=True)
+        tok_h.copy_(op(dbuf), non_blocking=True)
+
+    for _ in range(3 if args.e2e_steps else 0):
+        api_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        api_step()
+    e1.record()
+    torch.cuda.synchronize()
+    et = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_value = B * world * e2e_steps / (float(et.item()) / 1e3)
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # the reference form on the host cores: F.linear on CPU bf16 tensors, .float().argmax(-1), time-bounded
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        hc, wc = hiddens[0].cpu(), head.cpu()
+        torch.nn.functional.linear(hc, wc).float().argmax(-1)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            torch.nn.functional.linear(hc, wc).float().argmax(-1)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= min(args.cpu_seconds, 10.0):
+                break
+        cb = {"value": B * n / el, "unit": "rows/s", "cores": threads, "kind": "reference",
+              "sample": f"{n} steps x {B} rows: F.linear(hidden, lm_head).float().argmax(-1) (the reference's greedy "
+                        f"step, engine/runtime/thinker_decode.py:107) on CPU torch {torch.__version__}, {threads} threads, "
+                        f"in {el:.1f} s"}
+    for gr, _ in graphs:
+        del gr
+    graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": metric_of(w),
+        "value": value, "unit": "rows/s", "value_per_gpu": value / world, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (LM-head GEMM, fp32 accumulation, bf16-rounded logits)", "data": "synthetic",
+        "config": config_of(args, w, world),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": profiled_traffic(args.workload, w, args.path), "bytes_per_step": step_bytes,
+                     "peak_source": peak_kind},
+        "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": host.numel() * host.element_size(),
+                "d2h_bytes_per_step": B * 8, "steps": e2e_steps},
+        "gpu_launches": 2 * args.steps,
+        "clocks": ck,
+        "cpu_baseline": cb,
+    }
+    print(json.dumps(line))
+
+
 def time_steps(args, one_step, dev, local: int, world: int):
     """W untimed steps, then exactly K steps (CUDA graphs of up to 1000 steps, each replayed once untimed before
     the timed replays) between CUDA events on the launching stream, with nvidia-smi clocks sampled meanwhile;
@@ -714,7 +830,8 @@ def main():
     ap.add_argument("--path", default="auto", choices=["auto", "stream", "resident", "unfused"],
                     help="sampling kernel: the launcher's choice (short-row kernel for rows of <= 8192 elements, "
                          "else row-resident), the streaming kernel, or the row-resident kernel; talker_head: "
-                         "'unfused' times torch's F.linear followed by the sampler (two launches per step)")
+                         "'unfused' times torch's F.linear followed by the sampler (two launches per step); greedy_head: F.linear "
+                         "followed by the argmax kernel")
     ap.add_argument("--cluster", type=int, default=0, help="CTAs per row of the row-resident kernel (0: auto)")
     ap.add_argument("--strong", action="store_true",
                     help="split the workload's batch over the ranks (strong scaling) instead of B rows per rank")
@@ -731,6 +848,8 @@ def main():
         return run_vocab_shard(args, w, rank, world, local)
     if w.get("op") == "head":
         return run_head(args, w, rank, world, local)
+    if w.get("op") == "lmhead":
+        return run_lmhead(args, w, rank, world, local)
 
     import torch
     import torch.distributed as dist

@@ -165,6 +165,20 @@ typedef struct b2s_head_args {
 int b2s_head_sample(const b2s_head_args* head, const b2s_sample_args* args, void* stream);
 
 /*
+ * The Thinker's greedy step from its LM head (ABI 5): tokens[n] = argmax_m bf16(hidden[n, :] . head[m, :]) (fp32
+ * accumulation on the tensor cores, each logit rounded to bf16 like F.linear's bf16 output, first index among equal
+ * maxima, NaN above every number) without writing the logits.  `keys`: `rows` 64-bit device words, zero before the
+ * first call and left zero by every call (one block per stream); `status` (optional) gets
+ * B2S_STATUS_WAIT_TIMEOUT if a bounded wait gave up (the row then returns PAD or a partial maximum).
+ * Replaces: F.linear(h, lm_head).float().argmax(-1) at engine/runtime/thinker_decode.py:83,107,
+ * engine/runtime/backend_s.py:893, engine/runtime/backend.py:238, engine/runtime/track_s.py:60.
+ * Limits: rows <= 64 (else B2S_ERR_UNSUPPORTED), hidden_dim a multiple of 64, hidden rows and head 16-byte aligned
+ * with row strides a multiple of 8 elements (the head's rows contiguous).
+ */
+int b2s_lmhead_argmax(const void* hidden, int64_t hidden_row_stride, const void* head, int32_t hidden_dim,
+                      int32_t vocab, int32_t rows, int64_t* tokens, uint64_t* keys, uint32_t* status, void* stream);
+
+/*
  * b2s_head_sample for callers that cannot allocate device memory: no counterpart in the reference, whose
  * callers allocate through torch.  Some hosts of this library cannot call cudaMalloc on this path -- an embedding
  * whose device allocator is fixed at start-up, a runtime that hands the library only the buffers it owns, or a

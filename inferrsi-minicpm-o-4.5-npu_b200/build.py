@@ -23,7 +23,8 @@ BUILD = PKG / "_build"
 LIB = PKG / "libb2s.so"
 OPS = BUILD / "b2s_torch_ops.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = [CSRC / "b2s_sampler.cu", CSRC / "b2s_resident.cu", CSRC / "b2s_short.cu", CSRC / "b2s_shard.cu"]
+CU_SOURCES = [CSRC / "b2s_sampler.cu", CSRC / "b2s_resident.cu", CSRC / "b2s_short.cu", CSRC / "b2s_shard.cu",
+              CSRC / "b2s_lmhead.cu"]
 CU_HEADERS = [CSRC / "b2s_device.cuh", CSRC / "b2s_list.cuh", CSRC / "b2s_row.cuh", CSRC / "b2s_rowpaths.cuh",
               CSRC / "b2s_head.cuh", INCLUDE / "b2s_sampler.h"]
 

@@ -1587,6 +1587,40 @@ int b2s_head_sample(const b2s_head_args* h, const b2s_sample_args* a, void* stre
     return launch_sample(&a2, stream, nullptr, 1, 0, &hl);
 }
 
+int b2s_lmhead_argmax(const void* hidden, int64_t hidden_row_stride, const void* head, int32_t hidden_dim,
+                      int32_t vocab, int32_t rows, int64_t* tokens, uint64_t* keys, uint32_t* status, void* stream) {
+    using namespace b2s;
+    if (!hidden || !head || !tokens || !keys || vocab < 1 || rows < 1) return B2S_ERR_INVALID;
+    if (hidden_dim < 64 || hidden_dim % 64 != 0 || hidden_row_stride < hidden_dim || hidden_row_stride % 8 != 0)
+        return B2S_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(hidden) & 15) != 0 || (reinterpret_cast<uintptr_t>(head) & 15) != 0 ||
+        (reinterpret_cast<uintptr_t>(keys) & 7) != 0)
+        return B2S_ERR_INVALID;
+    if (rows > LMHEAD_MAX_ROWS) return B2S_ERR_UNSUPPORTED;
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return cuda_fail(cudaErrorNotSupported);
+    // head [vocab, hidden_dim]: boxes of [128 ids x 64]; hidden [rows, hidden_dim]: boxes of [64 rows x 64] (rows
+    // past the batch read as zero); both in the 128-byte swizzle
+    CUtensorMap amap, bmap;
+    const cuuint64_t adims[2] = {(cuuint64_t)hidden_dim, (cuuint64_t)vocab};
+    const cuuint64_t astr[1] = {(cuuint64_t)hidden_dim * 2};
+    const cuuint32_t abox[2] = {64, 128};
+    const cuuint64_t bdims[2] = {(cuuint64_t)hidden_dim, (cuuint64_t)rows};
+    const cuuint64_t bstr[1] = {(cuuint64_t)hidden_row_stride * 2};
+    const cuuint32_t bbox[2] = {64, 64};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&amap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(head), adims, astr, abox, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(hidden), bdims, bstr, bbox, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return B2S_ERR_INVALID;
+    const cudaError_t e = lmhead_argmax_launch(amap, bmap, vocab, rows, hidden_dim / 64, tokens,
+                                               reinterpret_cast<unsigned long long*>(keys), status, stream);
+    return e == cudaSuccess ? B2S_OK : cuda_fail(e);
+}
+
 // ---------------------------------------------------------------- the codec head without caller scratch
 // b2s_head_sample needs two device buffers beyond its inputs and outputs: the bf16 logits rows that the head's
 // tiles hand to the rows, and four control words.  A caller that cannot allocate device memory -- an embedding

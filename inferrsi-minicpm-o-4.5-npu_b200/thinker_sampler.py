@@ -41,6 +41,29 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
     return _native.ops().argmax(logits)
 
 
+class LMHeadArgmax:
+    """The Thinker's greedy step straight from its LM head: ``F.linear(hidden, lm_head).float().argmax(-1)``
+    (``engine/runtime/thinker_decode.py:83,107``, ``engine/runtime/backend_s.py:893``) as one tensor-core GEMM whose
+    epilogue keeps each row's maximum, so the [B, V] logits are never written.  Holds the head ([V, H] bf16) and
+    ``rows`` 64-bit reduction words (zero between calls); one instance per stream.  Up to 64 rows, H a multiple of
+    64.  Each logit is the bf16 rounding of an fp32 tensor-core sum, as F.linear's bf16 output is; ties keep the
+    first index and NaN wins, as torch's argmax."""
+
+    def __init__(self, head: torch.Tensor, rows: int):
+        ts._need_cuda(head)
+        if head.dtype != torch.bfloat16 or head.dim() != 2:
+            raise ValueError("head must be a bf16 [vocab, hidden] tensor")
+        self.head = head.contiguous()
+        self.rows = int(rows)
+        self.keys = torch.zeros(self.rows, dtype=torch.int64, device=head.device)
+
+    def __call__(self, hidden: torch.Tensor, status: Optional[torch.Tensor] = None) -> torch.Tensor:
+        ts._need_cuda(hidden)
+        if hidden.dim() != 2 or hidden.shape[0] != self.rows or hidden.dtype != torch.bfloat16:
+            raise ValueError(f"hidden must be bf16 [{self.rows}, hidden]")
+        return _native.ops().lmhead_argmax(hidden, self.head, self.keys, status)
+
+
 def sample(logits: torch.Tensor, history: Optional[torch.Tensor], seeds: torch.Tensor, steps: torch.Tensor,
            cfg: ThinkerSampling = ThinkerSampling(), *, uniform_values: Optional[torch.Tensor] = None,
            requests: Optional[torch.Tensor] = None, status: Optional[torch.Tensor] = None,

@@ -190,3 +190,42 @@ def test_head_rejects_what_it_cannot_take(pkg):
     with pytest.raises(ValueError):
         ts.CodecHead(torch.zeros(V_TALKER, 768, dtype=torch.float32, device=DEV), 2)
     torch.cuda.synchronize()
+
+
+def test_head_graph_replay_matches_eager(pkg):
+    """CodecHead.step_ captured once in a CUDA graph and replayed frame by frame (new hidden rows copied into the
+    captured buffer) == eager calls on a copy of the state: the same tokens, history, steps and finished flags,
+    through EOS masking and forcing and an inactive row -- the form of the reference's graph bodies
+    (engine/runtime/talker_post_graph.py:56-76)."""
+    ts = pkg.talker_sampler
+    B, Hd, F = 6, 768, 16
+    cfg = ts.TalkerSampling(semantics="hf", rng="counter", min_new_tokens=3, max_new_tokens=12, window=16)
+    hidden_h, head_h = _operands(B, V_TALKER, Hd, 21)
+    head = head_h.to(DEV)
+    g = torch.Generator().manual_seed(22)
+    frames = torch.randn(F, B, Hd, generator=g).to(torch.bfloat16).to(DEV)
+    eager_h, graph_h = ts.CodecHead(head, B), ts.CodecHead(head, B)
+    eager = ts.DecodeState.new(list(range(40, 40 + B)), cfg, device=DEV)
+    graphed = ts.DecodeState.new(list(range(40, 40 + B)), cfg, device=DEV)
+    for st in (eager, graphed):
+        st.active[4] = False
+    static_h = frames[0].clone()
+    warm = ts.DecodeState.new(list(range(40, 40 + B)), cfg, device=DEV)
+    graph_h.step_(warm, static_h, EOS, cfg)  # builds the penalty table before capture
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream(device=DEV)
+    with torch.cuda.graph(gr, stream=s, capture_error_mode="thread_local"):
+        static_tok = graph_h.step_(graphed, static_h, EOS, cfg)
+    for f in range(F):
+        static_h.copy_(frames[f])
+        gr.replay()
+        want = eager_h.step_(eager, frames[f], EOS, cfg)
+        torch.cuda.synchronize()
+        assert torch.equal(static_tok, want), f
+        assert torch.equal(graph_h.logits, eager_h.logits), f
+        assert torch.equal(graphed.history, eager.history) and torch.equal(graphed.steps, eager.steps)
+        assert torch.equal(graphed.finished, eager.finished)
+    assert int(eager.steps[4]) == 0 and bool(eager.finished.any())  # max_new_tokens forced EOS
+    assert graph_h.sync.cpu().tolist() == [0, 0, 0, 0]
+    del gr
