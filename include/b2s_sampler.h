@@ -179,6 +179,18 @@ int b2s_lmhead_argmax(const void* hidden, int64_t hidden_row_stride, const void*
                       int32_t vocab, int32_t rows, int64_t* tokens, uint64_t* keys, uint32_t* status, void* stream);
 
 /*
+ * The same over one vocabulary shard (ABI 5; no counterpart in the reference, which has no multi-device code):
+ * head_shard holds ids vocab_offset .. vocab_offset + shard_vocab - 1.  Writes, per row, a 64-bit word whose signed
+ * maximum over the shards -- one max-all-reduce of `rows` int64 (NCCL) -- is the key of the global argmax: the
+ * order key of its bf16 value in the high word, the complement of its global id in the low word, the top bit
+ * flipped; INT64_MIN for a row that no tile reached.  The token is 0xffffffff - (word & 0xffffffff) after the top
+ * bit is flipped back.  `keys` as for b2s_lmhead_argmax.
+ */
+int b2s_lmhead_argmax_keys(const void* hidden, int64_t hidden_row_stride, const void* head_shard, int32_t hidden_dim,
+                           int32_t shard_vocab, int64_t vocab_offset, int32_t rows, int64_t* keys_out, uint64_t* keys,
+                           uint32_t* status, void* stream);
+
+/*
  * b2s_head_sample for callers that cannot allocate device memory: no counterpart in the reference, whose
  * callers allocate through torch.  Some hosts of this library cannot call cudaMalloc on this path -- an embedding
  * whose device allocator is fixed at start-up, a runtime that hands the library only the buffers it owns, or a

@@ -57,6 +57,9 @@ CAPI_SIGNATURES = {
     "b2s_lmhead_argmax": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int32,
                                          ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                          ctypes.c_void_p, ctypes.c_void_p]),
+    "b2s_lmhead_argmax_keys": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int32,
+                                              ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "b2s_head_sample_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int32,
                                                ctypes.POINTER(SampleArgs), ctypes.c_void_p]),
     "b2s_sample_frames": (ctypes.c_int, [ctypes.POINTER(SampleArgs), ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p]),

@@ -319,7 +319,9 @@ __device__ __forceinline__ void head_tile(int tile, int split, int rank, int row
 
 // The Thinker LM head's greedy step (b2s_lmhead.cu): tiles + finishing block on `stream`.
 constexpr int LMHEAD_MAX_ROWS = 64;
+// With keys_out: the shard's ordered keys (global ids from `offset`) instead of tokens.
 cudaError_t lmhead_argmax_launch(const CUtensorMap& amap, const CUtensorMap& bmap, int vocab, int rows, int nkb,
-                                 int64_t* tokens, unsigned long long* keys, uint32_t* status, void* stream);
+                                 int64_t* tokens, unsigned long long* keys, uint32_t* status, void* stream,
+                                 int64_t offset = 0, int64_t* keys_out = nullptr);
 
 }  // namespace b2s

@@ -165,9 +165,28 @@ __global__ void lmhead_finish_kernel(unsigned long long* keys, int rows, int64_t
     }
 }
 
+// Vocabulary shards: the rows' keys with the shard's first global id added, in an order that a signed 64-bit
+// maximum preserves (the top bit flipped), INT64_MIN for a row no tile reached; the keys zeroed for the next call.
+// A max-all-reduce of these words over the shards leaves every rank with the global maximum's key.
+__global__ void lmhead_keys_kernel(unsigned long long* keys, int rows, int64_t offset, int64_t* keys_out) {
+    const int r = (int)threadIdx.x;
+    if (r < rows) {
+        const unsigned long long k = keys[r];
+        int64_t out = INT64_MIN;
+        if (k) {
+            const uint64_t id = (uint64_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull)) + (uint64_t)offset;
+            const uint64_t g = (k & 0xffffffff00000000ull) | (0xffffffffull - id);
+            out = (int64_t)(g ^ 0x8000000000000000ull);
+        }
+        keys_out[r] = out;
+        keys[r] = 0ull;
+    }
+}
+
 // Launches the tiles and the finishing block on `stream` (the argument checks and TMA maps are the caller's).
 cudaError_t lmhead_argmax_launch(const CUtensorMap& amap, const CUtensorMap& bmap, int vocab, int rows, int nkb,
-                                 int64_t* tokens, unsigned long long* keys, uint32_t* status, void* stream) {
+                                 int64_t* tokens, unsigned long long* keys, uint32_t* status, void* stream,
+                                 int64_t offset, int64_t* keys_out) {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -190,7 +209,10 @@ cudaError_t lmhead_argmax_launch(const CUtensorMap& amap, const CUtensorMap& bma
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, lmhead_argmax_kernel, amap, bmap, vocab, rows, nkb, keys, status);
     if (e != cudaSuccess) return e;
-    lmhead_finish_kernel<<<1, LM_N, 0, (cudaStream_t)stream>>>(keys, rows, tokens);
+    if (keys_out)
+        lmhead_keys_kernel<<<1, LM_N, 0, (cudaStream_t)stream>>>(keys, rows, offset, keys_out);
+    else
+        lmhead_finish_kernel<<<1, LM_N, 0, (cudaStream_t)stream>>>(keys, rows, tokens);
     return cudaGetLastError();
 }
 

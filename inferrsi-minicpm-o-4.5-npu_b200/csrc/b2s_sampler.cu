@@ -1587,10 +1587,12 @@ int b2s_head_sample(const b2s_head_args* h, const b2s_sample_args* a, void* stre
     return launch_sample(&a2, stream, nullptr, 1, 0, &hl);
 }
 
-int b2s_lmhead_argmax(const void* hidden, int64_t hidden_row_stride, const void* head, int32_t hidden_dim,
-                      int32_t vocab, int32_t rows, int64_t* tokens, uint64_t* keys, uint32_t* status, void* stream) {
+static int lmhead_common(const void* hidden, int64_t hidden_row_stride, const void* head, int32_t hidden_dim,
+                         int32_t vocab, int32_t rows, int64_t* tokens, uint64_t* keys, uint32_t* status, void* stream,
+                         int64_t offset, int64_t* keys_out) {
     using namespace b2s;
-    if (!hidden || !head || !tokens || !keys || vocab < 1 || rows < 1) return B2S_ERR_INVALID;
+    if (!hidden || !head || !(tokens || keys_out) || !keys || vocab < 1 || rows < 1) return B2S_ERR_INVALID;
+    if (offset < 0 || offset + (int64_t)vocab > (int64_t)0xfffffffe) return B2S_ERR_INVALID;
     if (hidden_dim < 64 || hidden_dim % 64 != 0 || hidden_row_stride < hidden_dim || hidden_row_stride % 8 != 0)
         return B2S_ERR_INVALID;
     if ((reinterpret_cast<uintptr_t>(hidden) & 15) != 0 || (reinterpret_cast<uintptr_t>(head) & 15) != 0 ||
@@ -1617,8 +1619,24 @@ int b2s_lmhead_argmax(const void* hidden, int64_t hidden_row_stride, const void*
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return B2S_ERR_INVALID;
     const cudaError_t e = lmhead_argmax_launch(amap, bmap, vocab, rows, hidden_dim / 64, tokens,
-                                               reinterpret_cast<unsigned long long*>(keys), status, stream);
+                                               reinterpret_cast<unsigned long long*>(keys), status, stream, offset,
+                                               keys_out);
     return e == cudaSuccess ? B2S_OK : cuda_fail(e);
+}
+
+int b2s_lmhead_argmax(const void* hidden, int64_t hidden_row_stride, const void* head, int32_t hidden_dim,
+                      int32_t vocab, int32_t rows, int64_t* tokens, uint64_t* keys, uint32_t* status, void* stream) {
+    if (!tokens) return B2S_ERR_INVALID;
+    return lmhead_common(hidden, hidden_row_stride, head, hidden_dim, vocab, rows, tokens, keys, status, stream, 0,
+                         nullptr);
+}
+
+int b2s_lmhead_argmax_keys(const void* hidden, int64_t hidden_row_stride, const void* head_shard, int32_t hidden_dim,
+                           int32_t shard_vocab, int64_t vocab_offset, int32_t rows, int64_t* keys_out, uint64_t* keys,
+                           uint32_t* status, void* stream) {
+    if (!keys_out) return B2S_ERR_INVALID;
+    return lmhead_common(hidden, hidden_row_stride, head_shard, hidden_dim, shard_vocab, rows, nullptr, keys, status,
+                         stream, vocab_offset, keys_out);
 }
 
 // ---------------------------------------------------------------- the codec head without caller scratch

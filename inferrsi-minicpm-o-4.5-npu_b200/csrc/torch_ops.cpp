@@ -328,6 +328,40 @@ Tensor lmhead_argmax_cuda(const Tensor& hidden, const Tensor& head, Tensor& keys
     return tokens;
 }
 
+// One vocabulary shard of the same: [rows] int64 words whose max over the shards is the global argmax's key.
+Tensor lmhead_argmax_keys_cuda(const Tensor& hidden, const Tensor& head, Tensor& keys, int64_t offset,
+                               const optional<Tensor>& status) {
+    c10::cuda::CUDAGuard guard(hidden.device());
+    TORCH_CHECK(hidden.is_cuda() && head.is_cuda() && keys.is_cuda() && head.device() == hidden.device() &&
+                    keys.device() == hidden.device(),
+                "hidden, head and keys must be on one CUDA device");
+    TORCH_CHECK(hidden.scalar_type() == at::kBFloat16 && head.scalar_type() == at::kBFloat16,
+                "hidden and head must be bfloat16");
+    TORCH_CHECK(hidden.dim() == 2 && hidden.stride(1) == 1, "hidden must be [rows, hidden_dim] with contiguous rows");
+    TORCH_CHECK(head.dim() == 2 && head.is_contiguous() && head.size(1) == hidden.size(1),
+                "head must be contiguous [vocab, hidden_dim]");
+    TORCH_CHECK(keys.scalar_type() == at::kLong && keys.is_contiguous() && keys.numel() == hidden.size(0),
+                "keys must be [rows] int64");
+    uint32_t* st = nullptr;
+    if (status.has_value() && status->defined()) {
+        TORCH_CHECK(status->is_cuda() && status->scalar_type() == at::kInt && status->numel() == 1,
+                    "status must be a 1-element int32 CUDA tensor");
+        st = reinterpret_cast<uint32_t*>(status->data_ptr<int32_t>());
+    }
+    Tensor out = at::empty({hidden.size(0)}, hidden.options().dtype(at::kLong));
+    check_rc(b2s_lmhead_argmax_keys(hidden.data_ptr(), hidden.size(0) > 1 ? hidden.stride(0) : hidden.size(1),
+                                    head.data_ptr(), (int32_t)hidden.size(1), (int32_t)head.size(0), offset,
+                                    (int32_t)hidden.size(0), out.data_ptr<int64_t>(),
+                                    reinterpret_cast<uint64_t*>(keys.data_ptr<int64_t>()), st,
+                                    at::cuda::getCurrentCUDAStream().stream()),
+             "b2s_lmhead_argmax_keys");
+    return out;
+}
+
+Tensor lmhead_argmax_keys_meta(const Tensor& hidden, const Tensor&, Tensor&, int64_t, const optional<Tensor>&) {
+    return at::empty({hidden.size(0)}, hidden.options().dtype(at::kLong));
+}
+
 Tensor lmhead_argmax_meta(const Tensor& hidden, const Tensor&, Tensor&, const optional<Tensor>&) {
     return at::empty({hidden.size(0)}, hidden.options().dtype(at::kLong));
 }
@@ -543,6 +577,7 @@ TORCH_LIBRARY(minicpmo_sampler, m) {
         "float top_p, int top_k, int min_keep, int min_new_tokens, int max_new_tokens, int eos, int semantics, "
         "int rng, int max_top_k) -> Tensor tokens");
     m.def("lmhead_argmax(Tensor hidden, Tensor head, Tensor(a!) keys, Tensor? status) -> Tensor tokens");
+    m.def("lmhead_argmax_keys(Tensor hidden, Tensor head, Tensor(a!) keys, int offset, Tensor? status) -> Tensor");
     m.def("argmax(Tensor logits) -> Tensor");
     m.def("uniform(Tensor seeds, Tensor steps, Tensor? requests, int rng) -> Tensor");
     m.def("repetition_penalty(Tensor x, Tensor history, Tensor alpha) -> Tensor");
@@ -567,6 +602,7 @@ TORCH_LIBRARY_IMPL(minicpmo_sampler, CUDA, m) {
     m.impl("sample_frames_", &sample_frames_cuda);
     m.impl("head_sample_state_", &head_sample_state_cuda);
     m.impl("lmhead_argmax", &lmhead_argmax_cuda);
+    m.impl("lmhead_argmax_keys", &lmhead_argmax_keys_cuda);
     m.impl("argmax", &argmax_cuda);
     m.impl("uniform", &uniform_cuda);
     m.impl("repetition_penalty", &penalty_cuda);
@@ -581,6 +617,7 @@ TORCH_LIBRARY_IMPL(minicpmo_sampler, Meta, m) {
     m.impl("sample_frames_", &sample_frames_meta);
     m.impl("head_sample_state_", &head_sample_state_meta);
     m.impl("lmhead_argmax", &lmhead_argmax_meta);
+    m.impl("lmhead_argmax_keys", &lmhead_argmax_keys_meta);
     m.impl("argmax", &argmax_meta);
     m.impl("uniform", &uniform_meta);
     m.impl("repetition_penalty", &penalty_meta);

@@ -162,6 +162,39 @@ def publish(tokens: torch.Tensor, *, group=None, timeout: Optional[float] = None
     return tokens
 
 
+def lmhead_keys(hidden: torch.Tensor, head_shard: torch.Tensor, offset: int, keys: torch.Tensor,
+                status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The greedy step's per-shard words from this rank's slice of the Thinker LM head (``b2s_lmhead_argmax_keys``):
+    [B] int64 whose max over the shards is the global argmax's key.  ``keys``: [B] int64 scratch, zero between
+    calls (``thinker_sampler.LMHeadArgmax(head_shard, B).keys`` serves)."""
+    ts._need_cuda(hidden, head_shard, keys)
+    return _native.ops().lmhead_argmax_keys(hidden, head_shard, keys, int(offset), status)
+
+
+def decode_keys(words: torch.Tensor) -> torch.Tensor:
+    """Global argmax ids from the max-reduced words of ``lmhead_keys`` (PAD where no shard had a candidate)."""
+    k = torch.bitwise_xor(words, torch.tensor(-(1 << 63), dtype=torch.int64, device=words.device))
+    ids = 0xFFFFFFFF - torch.bitwise_and(k, 0xFFFFFFFF)
+    return torch.where(words == -(1 << 63), torch.full_like(ids, ts.PAD), ids)
+
+
+def lmhead_argmax_sharded(hidden: torch.Tensor, head_shard: torch.Tensor, offset: int, keys: torch.Tensor, *,
+                          group=None, timeout: Optional[float] = None) -> torch.Tensor:
+    """SURVEY's vocabulary-sharded Thinker head for the greedy step: this rank's LM-head slice (ids ``offset`` ..)
+    on the tensor cores with the argmax in its epilogue, one max-all-reduce of [B] int64 words, the global
+    argmax ids on every rank (first id among equal maxima, as torch's argmax over the whole row).  The logits are
+    never written.  ``timeout`` as for ``exchange``."""
+    import torch.distributed as dist
+
+    words = lmhead_keys(hidden, head_shard, offset, keys)
+    try:
+        work = dist.all_reduce(words, op=dist.ReduceOp.MAX, group=group, async_op=True)
+    except Exception as e:
+        raise ShardExchangeError(f"argmax all-reduce failed: {type(e).__name__}: {e}") from e
+    _wait(work, "argmax all-reduce", timeout)
+    return decode_keys(words)
+
+
 def sample_sharded(logits: torch.Tensor, offset: int, vocab: int, history: Optional[torch.Tensor],
                    steps: torch.Tensor, seeds: Optional[torch.Tensor], cfg, *, group=None, cap: Optional[int] = None,
                    uniform_values: Optional[torch.Tensor] = None, requests: Optional[torch.Tensor] = None,

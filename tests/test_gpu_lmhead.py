@@ -101,3 +101,25 @@ def test_lmhead_argmax_rejects_more_than_64_rows(pkg):
     with pytest.raises(RuntimeError, match="unsupported"):
         op(torch.zeros(65, 128, dtype=torch.bfloat16, device=DEV))
     torch.cuda.synchronize()
+
+
+def test_lmhead_shards_merge_to_the_unsharded_argmax(pkg):
+    """The vocabulary-sharded greedy step with its shards run one after another on one GPU: the signed maximum of
+    the shards' words decodes to the unsharded launch's tokens exactly (each id's sum is the same in any tile), ties
+    across shard boundaries included."""
+    lm, vs = pkg.thinker_sampler, pkg.vocab_shard
+    B, V, H = 16, 20_003, 768
+    hidden, head = _operands(B, V, H, 4)
+    w = hidden[5].float() * (8.0 / hidden[5].float().norm())
+    for j in (4999, 15000):  # a tie between shards 0 and 3: the first id must win
+        head[j] = w.to(torch.bfloat16)
+    head_d, hid_d = head.to(DEV), hidden.to(DEV)
+    want = lm.LMHeadArgmax(head_d, B)(hid_d)
+    bounds = [0, 5000, 10_003, 15_000, V]
+    keys = torch.zeros(B, dtype=torch.int64, device=DEV)
+    words = torch.stack([vs.lmhead_keys(hid_d, head_d[a:b].contiguous(), a, keys) for a, b in zip(bounds, bounds[1:])])
+    got = vs.decode_keys(words.max(dim=0).values)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want), (got, want)
+    assert int(got[5]) == 4999
+    assert keys.cpu().tolist() == [0] * B

@@ -3,6 +3,8 @@
 * Vocabulary-sharded sampling: each rank holds a contiguous slice of the head's columns; one NCCL
   all-gather of the packed candidate lists, then every rank draws the same token, which equals the unsharded
   kernel's token on the whole row (and the oracle's).
+* The greedy step from a vocabulary-sharded LM head: each rank's slice on the tensor cores with the argmax in the
+  epilogue, one NCCL max-all-reduce of [B] int64 words; every rank gets the unsharded launch's tokens.
 """
 
 from __future__ import annotations
@@ -57,8 +59,16 @@ def _worker(rank: int, world: int, port: int, out_q):
         # the unsharded kernel on the whole row, on this rank's GPU
         full = torch.from_numpy(x).to(dev).to(torch.bfloat16)
         want = ts.sample(full, h, seeds, steps, cfg)
+        # the greedy step from a vocabulary-sharded LM head (hidden 512): the same head on every rank, one slice each
+        g = torch.Generator().manual_seed(9)
+        hid = torch.randn(B, 512, generator=g).to(torch.bfloat16).to(dev)
+        head = (torch.randn(V, 512, generator=g) * (2.0 / 512 ** 0.5)).to(torch.bfloat16).to(dev)
+        keys = torch.zeros(B, dtype=torch.int64, device=dev)
+        gtok = vs.lmhead_argmax_sharded(hid, head[lo:hi].contiguous(), lo, keys, timeout=60)
+        gwant = ts.LMHeadArgmax(head, B)(hid)
         torch.cuda.synchronize()
-        out_q.put((rank, tok.cpu().numpy().tolist(), want.cpu().numpy().tolist(), int(status.item())))
+        out_q.put((rank, tok.cpu().numpy().tolist(), want.cpu().numpy().tolist(), int(status.item()),
+                   gtok.cpu().tolist(), gwant.cpu().tolist()))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -79,7 +89,8 @@ def test_vocab_sharded_two_gpus_matches_unsharded():
         p_.join(timeout=120)
         assert p_.exitcode == 0
     res.sort()
-    (_, tok0, want0, st0), (_, tok1, want1, st1) = res
+    (_, tok0, want0, st0, g0, gw0), (_, tok1, want1, st1, g1, gw1) = res
     assert st0 == 0 and st1 == 0
     assert tok0 == tok1  # every rank draws the same token
     assert tok0 == want0 == want1  # equal to the unsharded kernel's token
+    assert g0 == g1 == gw0 == gw1  # the sharded LM-head greedy step == the unsharded launch, on every rank
