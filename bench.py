@@ -505,6 +505,16 @@ def run_reference(args, w, rank: int):
         return
     from oracle import ref_build
 
+    if w.get("op") == "lmhead":  # the reference's greedy step from the LM head, CPU torch (no oracle port of a GEMM)
+        cb = lmhead_cpu(w, steps=args.steps, warmup=args.warmup)
+        print(json.dumps({"impl": "reference", "metric": metric_of(w), "value": cb["value"], "unit": "rows/s",
+                          "value_per_gpu": cb["value"], "n_gpus": args.gpus, "steps": args.steps,
+                          "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "bf16", "data": "synthetic", "config": config_of(args, w, args.gpus),
+                          "cpu_baseline": cb,
+                          "e2e": {"value": cb["value"], "unit": "rows/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return
     port = cpu_baseline(w, seconds=min(args.cpu_seconds, 5.0))
     if ref_build.available():
         cb = reference_cpu(w, steps=args.steps, warmup=args.warmup)
@@ -651,6 +661,33 @@ def run_head(args, w, rank: int, world: int, local: int):
     print(json.dumps(line))
 
 
+def lmhead_cpu(w, *, steps: int = 0, warmup: int = 1, seconds: float = 10.0) -> dict:
+    """The reference's greedy step on the host cores: ``F.linear(hidden, lm_head).float().argmax(-1)``
+    (``engine/runtime/thinker_decode.py:107``) on CPU torch bf16 tensors of the workload's shape with every host
+    thread; ``steps`` > 0 times exactly that many steps, else as many as fit in ``seconds``."""
+    import torch
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    B, V, Hd = w["rows"], w["vocab"], w["hidden"]
+    hc = torch.randn(B, Hd, generator=g).to(torch.bfloat16)
+    wc = (torch.randn(V, Hd, generator=g) * (2.0 / Hd ** 0.5)).to(torch.bfloat16)
+    for _ in range(max(1, warmup)):
+        torch.nn.functional.linear(hc, wc).float().argmax(-1)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        torch.nn.functional.linear(hc, wc).float().argmax(-1)
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps > 0 and n >= steps) or (steps <= 0 and el >= seconds):
+            break
+    return {"value": B * n / el, "unit": "rows/s", "cores": threads, "kind": "reference",
+            "sample": f"{n} steps x {B} rows: F.linear(hidden, lm_head).float().argmax(-1) (the reference's greedy "
+                      f"step, engine/runtime/thinker_decode.py:107) on CPU torch {torch.__version__}, {threads} threads, "
+                      f"in {el:.1f} s"}
+
+
 def run_lmhead(args, w, rank: int, world: int, local: int):
     """The Thinker's greedy step from its LM head (``thinker_sampler.LMHeadArgmax``): each step reads the whole
     1.24 GB head (larger than the L2) and a rotating set of hidden rows."""
@@ -711,22 +748,7 @@ def run_lmhead(args, w, rank: int, world: int, local: int):
     e2e_value = B * world * e2e_steps / (float(et.item()) / 1e3)
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        # the reference form on the host cores: F.linear on CPU bf16 tensors, .float().argmax(-1), time-bounded
-        threads = len(os.sched_getaffinity(0))
-        torch.set_num_threads(threads)
-        hc, wc = hiddens[0].cpu(), head.cpu()
-        torch.nn.functional.linear(hc, wc).float().argmax(-1)
-        n, t0 = 0, time.perf_counter()
-        while True:
-            torch.nn.functional.linear(hc, wc).float().argmax(-1)
-            n += 1
-            el = time.perf_counter() - t0
-            if el >= min(args.cpu_seconds, 10.0):
-                break
-        cb = {"value": B * n / el, "unit": "rows/s", "cores": threads, "kind": "reference",
-              "sample": f"{n} steps x {B} rows: F.linear(hidden, lm_head).float().argmax(-1) (the reference's greedy "
-                        f"step, engine/runtime/thinker_decode.py:107) on CPU torch {torch.__version__}, {threads} threads, "
-                        f"in {el:.1f} s"}
+        cb = lmhead_cpu(w, seconds=min(args.cpu_seconds, 10.0))
     for gr, _ in graphs:
         del gr
     graphs.clear()
