@@ -122,8 +122,11 @@ struct Elem;
 template <>
 struct Elem<float> {
     static constexpr int SZ = 4, EPV = 4;
-    // a plain (coherent) load: the logits may have been written earlier in the same launch (b2s_head_sample)
     static __device__ __forceinline__ float gld(const void* base, int64_t i) {
+        return __ldg(reinterpret_cast<const float*>(base) + i);
+    }
+    // a plain (coherent) load, for logits written earlier in the same launch (b2s_head_sample)
+    static __device__ __forceinline__ float gld_coh(const void* base, int64_t i) {
         return reinterpret_cast<const float*>(base)[i];
     }
     static __device__ __forceinline__ float sld(const unsigned char* s) { return *reinterpret_cast<const float*>(s); }
@@ -153,6 +156,9 @@ template <>
 struct Elem<__nv_bfloat16> {
     static constexpr int SZ = 2, EPV = 8;
     static __device__ __forceinline__ float gld(const void* base, int64_t i) {
+        return bf16_bits_to_f(__ldg(reinterpret_cast<const unsigned short*>(base) + i));
+    }
+    static __device__ __forceinline__ float gld_coh(const void* base, int64_t i) {
         return bf16_bits_to_f(reinterpret_cast<const unsigned short*>(base)[i]);
     }
     static __device__ __forceinline__ float sld(const unsigned char* s) {
@@ -289,6 +295,7 @@ struct Row {
     float T;
     bool identity;
     int censor;                 // element whose processed value is -inf regardless (omni censored EOS) or -1
+    bool coh = false;           // the row was written earlier in the same launch: coherent loads, not read-only ones
 
     __device__ __forceinline__ float f(float x) const { return identity ? x : __fdiv_rn(x, T); }
     __device__ __forceinline__ bool hbit(int i) const { return bits && ((bits[i >> 5] >> (i & 31)) & 1u); }
@@ -300,7 +307,7 @@ struct Row {
         if (o + n > 32) b |= bits[w + 1] << (32 - o);
         return b & ((1u << n) - 1u);
     }
-    __device__ __forceinline__ float raw(int i) const { return Elem<E>::gld(rowp, i); }
+    __device__ __forceinline__ float raw(int i) const { return coh ? Elem<E>::gld_coh(rowp, i) : Elem<E>::gld(rowp, i); }
     // rank of a history id i among the row's distinct history ids (ascending id order)
     __device__ __forceinline__ int rank(int i) const {
         const int w = i >> 5, sub = w & 3;
@@ -317,7 +324,7 @@ struct Row {
         if (hbit(i)) return htv[rank(i)];
         return f(x);
     }
-    __device__ __forceinline__ uint4 vec(int v) const { return gvec[v]; }  // coherent, like Elem::gld
+    __device__ __forceinline__ uint4 vec(int v) const { return coh ? gvec[v] : __ldg(gvec + v); }
 };
 
 // Visit every element of the row as (index, raw value): interior vectors round-robin over the threads,
@@ -333,9 +340,9 @@ __device__ __forceinline__ void row_visit(const Row<E>& R, Fn fn) {
         for (int j = 0; j < EPV; ++j) fn(b + j, Elem<E>::at(q, j));
     }
     if (tid == 0)
-        for (int i = 0; i < R.nh; ++i) fn(i, Elem<E>::gld(R.rowp, i));
+        for (int i = 0; i < R.nh; ++i) fn(i, R.raw(i));
     if (tid == 1)
-        for (int i = R.e0 + R.nvec * EPV; i < R.V; ++i) fn(i, Elem<E>::gld(R.rowp, i));
+        for (int i = R.e0 + R.nvec * EPV; i < R.V; ++i) fn(i, R.raw(i));
 }
 
 // Ordered scan of the kept mass: every element i with keep(i, P_i) contributes p_i = fl(expf(P_i - m) / s);

@@ -108,7 +108,7 @@ static __device__ __noinline__ void hist_rebuild(const Params p, const Row<E> R,
     __syncthreads();
     const int hd = hist_rank_count<E>(p, R, h, pen_hist, censor, [](int) { return true; }, ctl);
     __syncthreads();
-    hist_values<E>(p, R, h, hd, hf, pen_hist, censor, T, [&](int id) { return Elem<E>::gld(R.rowp, id); });
+    hist_values<E>(p, R, h, hd, hf, pen_hist, censor, T, [&](int id) { return R.raw(id); });
     __syncthreads();
 }
 

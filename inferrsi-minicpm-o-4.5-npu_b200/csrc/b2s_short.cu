@@ -119,6 +119,7 @@ __device__ __forceinline__ void short_rows(const Params& p, unsigned char* smem)
     Row<E> R;
     R.rowp = reinterpret_cast<const unsigned char*>(p.logits) + ((int64_t)f * p.fstride + (int64_t)r * p.lstride) * ES;
     R.V = V;
+    R.coh = HEAD;  // the codec head's logits are written in this launch: no read-only-path loads of the row
     {
         const uintptr_t a = reinterpret_cast<uintptr_t>(R.rowp), b = a + (uintptr_t)V * ES;
         const uintptr_t ace = (a + 15) & ~(uintptr_t)15, bfl = b & ~(uintptr_t)15;
@@ -166,7 +167,7 @@ __device__ __forceinline__ void short_rows(const Params& p, unsigned char* smem)
     const int nx = tid == 0 ? R.nh : tid == 1 ? V - i_end : 0;  // < EPV
     uint32_t ex[EPV - 1];  // the edge elements' bits, packed into q[SV] once they are needed
 #pragma unroll
-    for (int j = 0; j < EPV - 1; ++j) ex[j] = j < nx ? __float_as_uint(Elem<E>::gld(R.rowp, x0 + j)) : 0u;
+    for (int j = 0; j < EPV - 1; ++j) ex[j] = j < nx ? __float_as_uint(R.raw(x0 + j)) : 0u;
     const int64_t step = p.steps ? p.steps[r] : 0;
     const bool is_live = (p.active ? p.active[r] != 0 : true) && !(p.finished ? p.finished[r] != 0 : false);
     const float T = p.rT ? p.rT[r] : p.T;
@@ -217,7 +218,7 @@ __device__ __forceinline__ void short_rows(const Params& p, unsigned char* smem)
     }
     if (hvalid) {
         atomicAdd(&cnts[hc >> 2], 1u << ((hc & 3) * 8));
-        hx = Elem<E>::gld(R.rowp, hv);
+        hx = R.raw(hv);
     }
     cp_async_wait_all();
     __syncthreads();  // the counts are complete; the window and the penalty table are staged
