@@ -180,7 +180,7 @@ def decode_keys(words: torch.Tensor) -> torch.Tensor:
 
 def lmhead_argmax_sharded(hidden: torch.Tensor, head_shard: torch.Tensor, offset: int, keys: torch.Tensor, *,
                           group=None, timeout: Optional[float] = None) -> torch.Tensor:
-    """SURVEY's vocabulary-sharded Thinker head for the greedy step: this rank's LM-head slice (ids ``offset`` ..)
+    """The vocabulary-sharded Thinker head for the greedy step: this rank's LM-head slice (ids ``offset`` ..)
     on the tensor cores with the argmax in its epilogue, one max-all-reduce of [B] int64 words, the global
     argmax ids on every rank (first id among equal maxima, as torch's argmax over the whole row).  The logits are
     never written.  ``timeout`` as for ``exchange``."""
