@@ -184,9 +184,14 @@ def lmhead_argmax_sharded(hidden: torch.Tensor, head_shard: torch.Tensor, offset
     on the tensor cores with the argmax in its epilogue, one max-all-reduce of [B] int64 words, the global
     argmax ids on every rank (first id among equal maxima, as torch's argmax over the whole row).  The logits are
     never written.  ``timeout`` as for ``exchange``."""
+    return merge_keys(lmhead_keys(hidden, head_shard, offset, keys), group=group, timeout=timeout)
+
+
+def merge_keys(words: torch.Tensor, *, group=None, timeout: Optional[float] = None) -> torch.Tensor:
+    """The shards' [B] int64 words max-all-reduced in place (NCCL on the GPUs, gloo on the CPU), decoded to the
+    global argmax ids.  ``timeout`` as for ``exchange``."""
     import torch.distributed as dist
 
-    words = lmhead_keys(hidden, head_shard, offset, keys)
     try:
         work = dist.all_reduce(words, op=dist.ReduceOp.MAX, group=group, async_op=True)
     except Exception as e:
