@@ -117,6 +117,13 @@ def test_product_path_refuses_cpu_tensors(pkg):
     x = torch.zeros(2, 16)
     with pytest.raises(ValueError):
         pkg.thinker_sampler.argmax(x)
+    head = torch.zeros(1000, 64, dtype=torch.bfloat16)  # the head entry points too: no CPU path
+    with pytest.raises(ValueError):
+        pkg.talker_sampler.CodecHead(head, 2)
+    with pytest.raises(ValueError):
+        pkg.thinker_sampler.LMHeadArgmax(head, 2)
+    with pytest.raises(ValueError):
+        pkg.vocab_shard.lmhead_keys(torch.zeros(2, 64, dtype=torch.bfloat16), head, 0, torch.zeros(2, dtype=torch.int64))
 
 
 def test_shard_pending_record_layout(tmp_path):
