@@ -351,7 +351,8 @@ def dtype_of(w) -> str:
 
 
 def rotating_buffers(w) -> int:
-    """Distinct logits buffers (heads, for the codec head): one sweep exceeds twice the L2 and 640 MiB."""
+    """Distinct logits buffers (heads, for the codec head): one sweep exceeds twice the L2 and 640 MiB, at most
+    8192 buffers (the single-row Talker's 26 KB rows: 215 MB, still larger than the L2)."""
     if w.get("op") == "lmhead":
         return 1  # one head already exceeds the L2
     buf = (w["vocab"] * w["hidden"] * 2 if w.get("op") == "head" else
